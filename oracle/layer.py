@@ -1,0 +1,130 @@
+"""MoE layer forward restatements (test infrastructure; see ``oracle/__init__.py``).
+
+``reference_port``  -- the reference's eager torch backend, ``MoE.forward(kernel_backend_moe=torch)``:
+    router ``F.linear`` (``sonicmoe/moe.py:280``), ``topk`` (``moe.py:362-368``), fp32 softmax over
+    the k values cast back to the input dtype (``moe.py:288-289``), ``sort`` of the flat expert ids
+    (``moe.py:303``), ``bincount`` (``moe.py:305``), gather by ``sorted_scattered_idxs // K``
+    (``moe.py:339-345``), per-expert ``F.linear`` (``moe.py:144-147``), SwiGLU with even rows =
+    gate and odd rows = up (``moe.py:23-26``), gate scaling and ``index_add`` into an fp32
+    ``[T, H]`` buffer (``moe.py:354-356``).  Same torch operations in the same order, so on CPU it
+    reproduces the reference bit for bit (pinned by ``tests/golden/layer_*.npz``).  It is also the
+    timed CPU baseline of ``bench.py``.
+
+``expert_loop``  -- the per-expert reference loop of ``benchmarks/moe-cute.py:204-244``: routing by
+    torch top-k, ``swiglu(h, concat_layout)`` (``moe-cute.py:22-27``), ``ref_o[T_idx] += w2_out *
+    score``; it covers top-k-over-softmax (+renorm) and the concatenated w1 layout, which the MoE
+    module cannot select.  Here it takes the routing as an argument and runs in float64.
+
+``fp8_oracle``  -- ``expert_loop`` on fake-quantised operands: x dequantised from its 1x128 e4m3
+    groups, w1/w2 from their 128x128 blocks, the SwiGLU output re-quantised 1x128 and dequantised
+    before the down projection (the "reference FP8 path" the north star's 1e-2 bound refers to).
+"""
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import quant
+from .routing import topk_route
+
+
+def swiglu_interleaved(h):
+    return h[..., 1::2] * F.silu(h[..., ::2])
+
+
+def reference_port(x, router_w, w1, w2, K: int):
+    """Reference eager MoE forward on CPU.  w1: [E, 2I, H] interleaved, w2: [E, H, I]. Returns (o fp32, logits)."""
+    T, H = x.shape
+    E = w1.shape[0]
+    logits = F.linear(x, router_w)
+    if K == 1:
+        vals, sel = logits.max(dim=-1, keepdim=True)
+    else:
+        vals, sel = logits.topk(K, dim=-1)
+    gates = F.softmax(vals.float(), dim=-1).type_as(x)
+    flat = sel.flatten()
+    _, sorted_pos = flat.sort()
+    freq = flat.bincount(minlength=E).to(torch.int32)
+    fan_in = sorted_pos // K
+    batch_gates = gates.flatten()[sorted_pos]
+    h = x[fan_in].split(freq.tolist(), dim=0)
+    h = [F.linear(h[e], w1[e]) for e in range(E)]
+    h = [swiglu_interleaved(t) for t in h]
+    y = torch.cat([F.linear(h[e], w2[e]) for e in range(E)], dim=0)
+    y = y * batch_gates.unsqueeze(-1)
+    o = torch.zeros((T, H), dtype=torch.float32, device=x.device).index_add(0, fan_in, y)
+    return o, logits, freq
+
+
+def expert_loop(x, w1, w2, scores, idx, concat_layout: bool, dtype=torch.float64):
+    """o[t] = sum_k score[t,k] * w2[e] @ swiglu(w1[e] @ x[t]) with e = idx[t,k] (float64 by default)."""
+    x = torch.as_tensor(x).to(dtype)
+    w1 = torch.as_tensor(w1).to(dtype)
+    w2 = torch.as_tensor(w2).to(dtype)
+    scores = torch.as_tensor(np.asarray(scores)).to(dtype)
+    idx = torch.as_tensor(np.asarray(idx)).long()
+    T, H = x.shape
+    E, N2, _ = w1.shape
+    I = N2 // 2
+    o = torch.zeros((T, H), dtype=dtype)
+    for e in range(E):
+        t_idx, k_idx = torch.nonzero(idx == e, as_tuple=True)
+        if t_idx.numel() == 0:
+            continue
+        h = x[t_idx] @ w1[e].T
+        if concat_layout:
+            a = F.silu(h[:, :I]) * h[:, I:]
+        else:
+            a = swiglu_interleaved(h)
+        y = a @ w2[e].T
+        o.index_add_(0, t_idx, y * scores[t_idx, k_idx, None])
+    return o
+
+
+def fp8_oracle(x, logits, w1, w2, K: int, softmax_over_topk=True, norm_topk_probs=False, concat_layout=False):
+    """Fake-quantised FP8 layer: returns (o float64 [T,H], scores, idx).
+
+    x: [T, H] activations (the bf16 values as float32), w1: [E, 2I, H] in the caller's layout
+    (interleaved or concatenated), w2: [E, H, I], logits: [T, E] (bf16 values as float32).
+    """
+    x = np.asarray(x, dtype=np.float32)
+    w1 = np.asarray(w1, dtype=np.float32)
+    w2 = np.asarray(w2, dtype=np.float32)
+    scores, idx = topk_route(logits, K, softmax_over_topk, norm_topk_probs)
+    xq, xs = quant.quant_1x128(x)
+    xd = quant.dequant_1x128(xq, xs)
+    w1q, w1s = quant.quant_128x128(w1)
+    w1d = quant.dequant_128x128(w1q, w1s)
+    w2q, w2s = quant.quant_128x128(w2)
+    w2d = quant.dequant_128x128(w2q, w2s)
+
+    xt = torch.as_tensor(xd).double()
+    w1t = torch.as_tensor(w1d).double()
+    w2t = torch.as_tensor(w2d).double()
+    T, H = x.shape
+    E, N2, _ = w1.shape
+    I = N2 // 2
+    idx_t = torch.as_tensor(idx).long()
+    sc_t = torch.as_tensor(scores).double()
+    o = torch.zeros((T, H), dtype=torch.float64)
+    for e in range(E):
+        t_idx, k_idx = torch.nonzero(idx_t == e, as_tuple=True)
+        if t_idx.numel() == 0:
+            continue
+        h = xt[t_idx] @ w1t[e].T
+        if concat_layout:
+            a = F.silu(h[:, :I]) * h[:, I:]
+        else:
+            a = swiglu_interleaved(h)
+        aq, as_ = quant.quant_1x128(a.float().numpy())
+        ad = torch.as_tensor(quant.dequant_1x128(aq, as_)).double()
+        y = ad @ w2t[e].T
+        o.index_add_(0, t_idx, y * sc_t[t_idx, k_idx, None])
+    return o, scores, idx
+
+
+def rel_fro(a, b) -> float:
+    """||a - b||_F / ||b||_F in float64."""
+    a = torch.as_tensor(np.asarray(a, dtype=np.float64)) if not torch.is_tensor(a) else a.double()
+    b = torch.as_tensor(np.asarray(b, dtype=np.float64)) if not torch.is_tensor(b) else b.double()
+    den = torch.linalg.norm(b).item()
+    return torch.linalg.norm(a - b).item() / (den if den > 0 else 1.0)
