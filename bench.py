@@ -1,0 +1,408 @@
+"""Benchmark of the FP8 MoE-layer forward (T=32768, H=4096, I=1024, E=128, K=8).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one inference forward of the layer on one batch of synthetic input: router logits
+(cuBLAS bf16 GEMM, kept for bit-exact routing as in the reference), then the engine's six
+kernels (router top-k + tile histogram, metadata scan, metadata scatter, quantise + pack, up-proj
+GEMM + SwiGLU + requant, down-proj GEMM + weighted combine).  Inputs are resident in HBM before
+the timed region and larger than L2 (x 268 MB, e4m3 weights 1.6 GB), so no explicit L2 flush.
+The timed steps replay a CUDA graph of the forward, as the reference benchmark does
+(benchmarks/moe-cute.py:308-331).
+
+Synthetic data: x ~ N(0,1) bf16, router/expert weights ~ N(0, 0.02) bf16,
+expert weights quantised to e4m3 with 128x128 UE8M0 scales before timing (weight preparation is
+not part of the forward).  FLOPs per forward: 6*T*K*H*I (benchmarks/moe-cute.py:281-284).
+
+N > 1 (torchrun): every rank runs the same single-GPU layer on its own GPU (replicas, weak
+scaling, no collective on the data path); the step time is the max over ranks.
+
+--impl reference: the reference's eager CPU path (oracle.layer.reference_port, a line-by-line
+restatement of sonicmoe/moe.py:278-360 that reproduces it bit for bit) on the host cores, on a
+bounded token sample of the same configuration, reported as tokens/s.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "sonic-moe_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "FP8 MoE fwd TFLOPS/GPU & tokens/s (T32k,H4096,I1024,E128,K8) at 1/2/4/8 B200"
+CFG = dict(T=32768, H=4096, I=1024, E=128, K=8)
+CPU_SAMPLE_TOKENS = 2048
+
+
+def flops_fwd(T, H, I, K):
+    return 6.0 * T * K * H * I
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "MEASURED_PEAKS.json"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes of the GEMM kernels from the committed ncu summary (or None)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_workload(dev, T, H, I, E, K, seed=1111):
+    import torch
+
+    from sonicmoe import ops
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w1 = (torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w1p = ops.weight_prep(w1)
+    w2p = ops.weight_prep(w2)
+    return x, rw, w1, w2, w1p, w2p
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.nn.functional as F
+
+    from sonicmoe import ops
+    from sonicmoe.functional import moe_TC_softmax_topk_layer
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
+    x, rw, w1, w2, w1p, w2p = build_workload(dev, T, H, I, E, K, seed=1111 + rank)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    freq = torch.empty(E, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def forward():
+        logits = F.linear(x, rw)
+        ops.moe_forward(x, logits, w1p, w2p, K, out=out, expert_frequency=freq, err=err)
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            forward()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            forward()
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    if err.item() != 0:
+        raise RuntimeError(f"kernel error word {err.item()} during warm-up")
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        time.sleep(0.2)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    ms_total = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = t.item()
+        dist.barrier()
+    assert err.item() == 0, f"kernel error word {err.item()}"
+    ms_step = ms_total / args.steps
+
+    # per-kernel live timing of the two GEMMs (same stream, CUDA events around each launch)
+    stage = time_gemm_stages(x, rw, w1p, w2p, K, reps=max(3, min(args.steps, 10)))
+
+    # end to end through the public API: pinned host input -> device, forward, result -> host
+    e2e = time_e2e(x, rw, w1, w2, K, dev, steps=max(3, min(args.steps, 10)))
+    if dist is not None:
+        t = torch.tensor([e2e["ms_step"]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e["ms_step"] = t.item()
+
+    res = {
+        "ms_step": ms_step,
+        "tokens_per_s": world * T / (ms_step / 1e3),
+        "tflops_per_gpu": flops_fwd(T, H, I, K) / (ms_step / 1e3) / 1e12,
+        "stage": stage,
+        "e2e": e2e,
+        "clocks": clk.summary(),
+        "weights": (rw, w1, w2),
+    }
+    del graph
+    return res
+
+
+def time_gemm_stages(x, rw, w1p, w2p, K, reps):
+    import torch
+    import torch.nn.functional as F
+
+    from sonicmoe import ops
+
+    T, H = x.shape
+    E = rw.shape[0]
+    logits = F.linear(x, rw)
+    scores, idx = ops.router_topk(logits, K)
+    err = torch.zeros(1, dtype=torch.int32, device=x.device)
+    plan = ops.route_plan(idx, E, err)
+    xq, xsf = ops.quant_pack(x, idx, plan)
+    aq, asf = ops.moe_up(xq, xsf, w1p, plan, err)
+    out = torch.zeros(T, H, dtype=torch.bfloat16, device=x.device)
+    ops.moe_down_combine(aq, asf, w2p, plan, scores, T, err, out=out)
+    torch.cuda.synchronize()
+    ups, downs, packs = [], [], []
+    for _ in range(reps):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        e[0].record()
+        ops.quant_pack(x, idx, plan)
+        e[1].record()
+        e[2].record()
+        ops.moe_up(xq, xsf, w1p, plan, err)
+        e[3].record()
+        out.zero_()
+        e[4].record()
+        ops.moe_down_combine(aq, asf, w2p, plan, scores, T, err, out=out)
+        e[5].record()
+        torch.cuda.synchronize()
+        packs.append(e[0].elapsed_time(e[1]))
+        ups.append(e[2].elapsed_time(e[3]))
+        downs.append(e[4].elapsed_time(e[5]))
+    assert err.item() == 0
+    return {"pack_ms": statistics.median(packs), "up_ms": statistics.median(ups), "down_ms": statistics.median(downs),
+            "n_blocks": int(plan.n_blocks.item())}
+
+
+def time_e2e(x, rw, w1, w2, K, dev, steps):
+    import torch
+
+    from sonicmoe.functional import moe_TC_softmax_topk_layer
+
+    T, H = x.shape
+    x_host = x.cpu().pin_memory()
+    o_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    w1v, w2v = w1.permute(1, 2, 0), w2.permute(1, 2, 0)
+    xd = torch.empty_like(x)
+
+    def step():
+        xd.copy_(x_host, non_blocking=True)
+        o, _, _ = moe_TC_softmax_topk_layer(xd, rw, w1v, None, w2v, None, K, None, is_inference_mode_enabled=True)
+        o_host.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    nbytes = x.numel() * x.element_size()
+    return {"ms_step": ms, "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": T * H * 2}
+
+
+def cpu_reference(T_sample, reps, threads=None, weights=None):
+    """Reference eager CPU forward (fp32) on T_sample tokens of config 2; returns (tokens/s, cores, sample, sec).
+
+    weights: optional (router_w, w1, w2) device tensors of the GPU run, widened to fp32 on the host,
+    so both arms see the same layer; otherwise drawn here from the same distributions.
+    """
+    import torch
+
+    from oracle.layer import reference_port
+
+    cores = threads or len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    T, H, I, E, K = T_sample, CFG["H"], CFG["I"], CFG["E"], CFG["K"]
+    g = torch.Generator().manual_seed(1111)
+    if weights is not None:
+        rw, w1, w2 = (w.float().cpu() for w in weights)
+    else:
+        rw = torch.randn(E, H, generator=g).mul_(0.02).bfloat16().float()
+        w1 = torch.randn(E, 2 * I, H, generator=g).mul_(0.02).bfloat16().float()
+        w2 = torch.randn(E, H, I, generator=g).mul_(0.02).bfloat16().float()
+    x = torch.randn(T, H, generator=g).bfloat16().float()
+    with torch.no_grad():
+        reference_port(x, rw, w1, w2, K)  # warm-up
+        times = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            reference_port(x, rw, w1, w2, K)
+            times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    sample = f"T={T} tokens of config 2 (H={H}, I={I}, E={E}, K={K}), fp32 eager reference path, median of {reps}"
+    return T / sec, cores, sample, sec
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
+    config = {"workload": "config 2: FP8 MoE forward T=32768 H=4096 I=1024 E=128 K=8, SwiGLU, interleaved w1",
+              "T_per_gpu": T, "H": H, "I": I, "E": E, "K": K, "routing": "softmax_over_topk",
+              "l2": "inputs larger than L2 (x 268 MB, e4m3 weights 1.6 GB); no flush",
+              "timing": "CUDA graph replay of the forward, CUDA events, max over ranks"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cores = len(os.sched_getaffinity(0))
+        tps, cores, sample, sec = cpu_reference(CPU_SAMPLE_TOKENS, reps=max(1, min(args.steps, 3)), threads=cores)
+        line = {"metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": dict(config, parallelism="cpu", sample_tokens=CPU_SAMPLE_TOKENS),
+                "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+                "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import datetime
+
+    import torch
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    res = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks, peak_src = measured_peaks()
+    fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    st = res["stage"]
+    up_flops = 4.0 * T * K * H * I
+    down_flops = 2.0 * T * K * H * I
+    up_tflops = up_flops / (st["up_ms"] / 1e3) / 1e12
+    down_tflops = down_flops / (st["down_ms"] / 1e3) / 1e12
+    traffic = committed_traffic().get("moe_gemm_up_per_launch_bytes")
+    cpu = None
+    if not args.no_cpu_baseline:
+        tps, cores, sample, _ = cpu_reference(CPU_SAMPLE_TOKENS, reps=2, weights=res["weights"])
+        cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    e2e = res["e2e"]
+    line = {
+        "metric": METRIC,
+        "value": res["tokens_per_s"],
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_step": res["ms_step"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3",
+        "data": "synthetic",
+        "config": dict(config, parallelism="replicas" if world > 1 else "single"),
+        "tflops_per_gpu": res["tflops_per_gpu"],
+        "gpu_launches": 6 * args.steps,
+        "e2e": {"value": world * T / (e2e["ms_step"] / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]},
+        "roofline": {"bound": "tensor", "kernel": "moe_gemm_kernel<up> (up-proj GEMM + SwiGLU + requant)",
+                     "achieved": up_tflops, "peak": fp8_peak, "unit": "TFLOP/s", "frac": up_tflops / fp8_peak,
+                     "traffic": traffic,
+                     "peak_source": f"2 x bf16_tflops of {peak_src} (tcgen05 e4m3 rate = 2 x bf16)",
+                     "down_kernel_tflops": down_tflops, "pack_ms": st["pack_ms"], "up_ms": st["up_ms"],
+                     "down_ms": st["down_ms"]},
+        "clocks": res["clocks"],
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

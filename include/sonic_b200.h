@@ -1,0 +1,178 @@
+/*
+ * sonic_b200.h -- C ABI of libsonic_b200.so, the B200 (sm_100a) FP8 MoE-layer forward engine.
+ *
+ * Conventions (every entry point):
+ *   - Pointers are device pointers owned by the caller; nothing is allocated inside except where
+ *     an entry point documents it.  Scratch space is an explicit `workspace` argument.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*); calls are asynchronous,
+ *     perform no host synchronisation and can be captured in a CUDA graph.
+ *   - Return 0 on success or a negative errno-style code: SM_EINVAL (bad shape, alignment or
+ *     pointer), SM_ENOTSUP (a configuration this engine does not implement), SM_EIO (CUDA
+ *     launch error).  sm_last_error() returns a message for the calling thread's last failure.
+ *   - Kernels with bounded waits report a timeout through the int32 `err` word (0 = ok); the
+ *     host reads it whenever it synchronises.  SM_ERR_TIMEOUT_* values identify the wait.
+ *   - bf16 tensors are passed as `const void*` / `void*` (IEEE bfloat16, row-major).
+ *
+ * FP8 format (this engine's quantiser; the reference has none): e4m3 values, one UE8M0 scale
+ * byte (2^(b-127)) per 1x128 activation group or 128x128 weight block, scale = 2^ceil(log2(amax/448)).
+ * Scale bytes are stored in 512-byte "SF atoms" of 128 rows x 4 K-blocks, byte
+ * 16*(r%32) + 4*((r%128)/32) + (kb%4) for row r and K block kb (activations: atom [r/128][kb/4];
+ * weights: atom [expert][n/128][kb/4], every row of a 128-row block holding the block's scale).
+ */
+#ifndef SONIC_B200_H
+#define SONIC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SM_OK 0
+#define SM_EIO (-5)
+#define SM_EINVAL (-22)
+#define SM_ENOTSUP (-95)
+
+#define SM_DTYPE_BF16 0
+#define SM_DTYPE_F16 1
+#define SM_DTYPE_F32 2
+
+#define SM_ERR_TIMEOUT_PRODUCER 101
+#define SM_ERR_TIMEOUT_MMA 102
+#define SM_ERR_TIMEOUT_EPILOGUE 103
+#define SM_ERR_BAD_EXPERT 201
+
+/* Message describing the calling thread's most recent non-zero return. */
+const char* sm_last_error(void);
+
+/* Library version string. */
+const char* sm_version(void);
+
+/*
+ * Router top-k.  Replaces the custom op `sonicmoe::_softmax_topk_fwd`
+ * (reference sonicmoe/functional/forward.py:107-141) and its CuTe kernel
+ * (sonicmoe/functional/topk.py:241-419).
+ *   logits [T, E] (dtype SM_DTYPE_*), scores [T, K] float32, indices [T, K] int32, both in
+ *   descending score order; equal scores go to the lower expert index.
+ *   softmax_over_topk = 1: softmax over the k selected logits; = 0: top-k of the full-row softmax,
+ *   renormalised to sum to 1 when norm_topk_probs = 1 (only valid with softmax_over_topk = 0).
+ *   1 <= K <= min(E, 32), 1 <= E <= 4096.
+ */
+int sm_router_topk(const void* logits, int dtype, int T, int E, int K, int softmax_over_topk, int norm_topk_probs,
+                   float* scores, int32_t* indices, void* stream);
+
+/* Bytes of workspace sm_route_metadata / sm_general_route_metadata need. */
+size_t sm_route_metadata_workspace(int T, int TK, int E);
+
+/*
+ * Token-choice routing metadata.  Replaces `triton_kernels::TC_topk_router_metadata`
+ * (reference sonicmoe/functional/triton_kernels/__init__.py:68-146, bitmatrix.py:18-147).
+ *   topk_indices [T, K] int32 ->
+ *   expert_frequency [E], expert_frequency_offset [E+1] (exclusive cumsum, [E] = T*K),
+ *   s_scatter_idx [T*K] (expert-sorted position -> flat entry t*K+k; stable in entry order),
+ *   s_reverse_scatter_idx [T*K] (its inverse), x_gather_idx [T*K] (= s_scatter_idx / K).
+ *   err: int32 word set to SM_ERR_BAD_EXPERT if an index is outside [0, E).
+ */
+int sm_route_metadata(const int32_t* topk_indices, int T, int K, int E, int32_t* expert_frequency,
+                      int32_t* expert_frequency_offset, int32_t* x_gather_idx, int32_t* s_scatter_idx,
+                      int32_t* s_reverse_scatter_idx, void* workspace, size_t workspace_bytes, int32_t* err,
+                      void* stream);
+
+/*
+ * General-routing metadata.  Replaces `triton_kernels::general_routing_router_metadata`
+ * (reference sonicmoe/functional/triton_kernels/__init__.py:270-353).
+ *   sorted_token_idx [TK] (ascending), expert_idx [TK] -> the five arrays above (x_gather_idx =
+ *   sorted_token_idx[s_scatter_idx]) and num_activated_expert_per_token_offset [T+1].
+ */
+int sm_general_route_metadata(const int32_t* sorted_token_idx, const int32_t* expert_idx, int T, int TK, int E,
+                              int32_t* expert_frequency, int32_t* expert_frequency_offset, int32_t* x_gather_idx,
+                              int32_t* s_scatter_idx, int32_t* s_reverse_scatter_idx,
+                              int32_t* num_activated_expert_per_token_offset, void* workspace,
+                              size_t workspace_bytes, int32_t* err, void* stream);
+
+/*
+ * 1x128 activation quantiser in token order (no reference counterpart; the reference has no FP8
+ * path -- this is the spec entry point the pack kernel shares).
+ *   x [R, C] bf16 (C % 128 == 0) -> q [R, C] e4m3, sf atoms [ceil(R/128)][ceil(C/512)][512].
+ */
+int sm_quant_1x128(const void* x, int R, int C, uint8_t* q, uint8_t* sf_atoms, void* stream);
+
+/* Bytes of the weight SF atoms for a [E, N, K] weight. */
+size_t sm_weight_sf_bytes(int E, int N, int K);
+
+/*
+ * 128x128 weight quantiser (weight preparation, done once per weight version).  Consumes the
+ * reference's expert weights `c_fc.weight` [E, 2I, H] / `c_proj.weight` [E, H, I]
+ * (reference sonicmoe/moe.py:189-203, layout contract functional/__init__.py:560-566).
+ *   w [E, N, K] bf16 (N, K % 128 == 0) -> wq [E, N, K] e4m3 + sf atoms.
+ *   concat_glu = 1: w is a concatenated SwiGLU weight [gate; up] (N = 2I); the output rows are
+ *   re-blocked to [gate_0..127, up_0..127, gate_128..255, ...] so that one 256-row GEMM tile holds
+ *   matching gate and up blocks.  The 128x128 scale blocks are those of the input layout.
+ */
+int sm_weight_prep(const void* w, int E, int N, int K, int concat_glu, uint8_t* wq, uint8_t* sf_atoms,
+                   void* stream);
+
+/* Bytes of workspace sm_moe_forward needs. */
+size_t sm_moe_workspace_bytes(int T, int H, int I, int E, int K);
+
+/*
+ * Whole FP8 MoE-layer forward (inference).  Replaces the forward of
+ * `moe_TC_softmax_topk_layer` after the router GEMM (reference sonicmoe/functional/__init__.py:482-557:
+ * router top-k, routing metadata, _UpProjection, _DownProjection with the expert aggregation).
+ *   x [T, H] bf16, router_logits [T, E] bf16 (x @ router_w^T, computed by the caller),
+ *   w1q/w1_sf from sm_weight_prep of c_fc.weight (interleaved, or concat_layout = 1),
+ *   w2q/w2_sf from sm_weight_prep of c_proj.weight ->
+ *   out [T, H] bf16, expert_frequency [E] int32; topk_scores [T, K] float32 and
+ *   topk_indices [T, K] int32 are written when non-NULL.
+ *   H % 256 == 0, I % 128 == 0, 1 <= K <= min(E, 32), E <= 4096.
+ *   err: int32 word (may be NULL); set non-zero if a kernel gave up on a bounded wait.
+ */
+int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I, int E, int K,
+                   int softmax_over_topk, int norm_topk_probs, int concat_layout, const uint8_t* w1q,
+                   const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, void* out,
+                   int32_t* expert_frequency, float* topk_scores, int32_t* topk_indices, void* workspace,
+                   size_t workspace_bytes, int32_t* err, void* stream);
+
+/*
+ * Stage-level entry points of the forward (same pipeline as sm_moe_forward, exposed so each
+ * stage can be checked on its own).  The padded expert layout: expert e owns rows
+ * [off_pad[e], off_pad[e] + expert_frequency[e]) of a buffer with max_blocks*128 rows, where
+ * max_blocks = sm_max_padded_blocks(T*K, E); blk_expert[b] is the expert of 128-row block b and
+ * n_blocks[0] the number of blocks in use.
+ */
+int sm_max_padded_blocks(long long TK, int E);
+
+/* sm_route_metadata plus the padded layout: off_pad [E+1], blk_expert [max_blocks], n_blocks [1]. */
+int sm_route_plan(const int32_t* topk_indices, int T, int K, int E, int32_t* expert_frequency,
+                  int32_t* expert_frequency_offset, int32_t* x_gather_idx, int32_t* s_scatter_idx,
+                  int32_t* s_reverse_scatter_idx, int32_t* off_pad, int32_t* blk_expert, int32_t* n_blocks,
+                  void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
+
+/* Quantise x [T, H] and write each token's row to its K padded positions:
+ * xq [max_blocks*128, H] e4m3, xsf atoms [max_blocks][ceil(H/512)][512]. */
+int sm_quant_pack(const void* x, int T, int H, const int32_t* topk_indices, int K,
+                  const int32_t* s_reverse_scatter_idx, const int32_t* expert_frequency_offset,
+                  const int32_t* off_pad, uint8_t* xq, uint8_t* xsf, void* stream);
+
+/* Up projection + SwiGLU + 1x128 requantisation (reference _UpProjection.forward,
+ * sonicmoe/functional/__init__.py:227-301): aq [max_blocks*128, I] e4m3 + asf atoms. */
+int sm_moe_up(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1q, const uint8_t* w1_sf, int H, int I, int E,
+              int concat_layout, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+              const int32_t* off_pad, const int32_t* expert_frequency, uint8_t* aq, uint8_t* asf, int32_t* err,
+              void* stream);
+
+/* Down projection with the top-k weighted combine fused (reference _DownProjection.forward and
+ * _router_forward, sonicmoe/functional/__init__.py:365-420, forward.py:64-85).  Adds
+ * score * y into out [T, H] bf16, which the caller zero-fills first. */
+int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2q, const uint8_t* w2_sf, int H,
+                        int I, int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+                        const int32_t* off_pad, const int32_t* expert_frequency_offset,
+                        const int32_t* expert_frequency, const int32_t* s_scatter_idx, const int32_t* x_gather_idx,
+                        const float* topk_scores, void* out, int32_t* err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SONIC_B200_H */

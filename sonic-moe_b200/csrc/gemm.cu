@@ -1,0 +1,342 @@
+// Block-scaled FP8 grouped GEMMs of the MoE layer on tcgen05 (sm_100a).
+//
+// One persistent kernel, two epilogues:
+//   up   : h = A x W1[e]^T over a 128x256 tile (A = packed e4m3 tokens, 1x128 UE8M0 scales;
+//          W1 = e4m3 weights, 128x128 UE8M0 scales), then a = silu(gate) * up and the 1x128
+//          requantisation of `a` to e4m3 + UE8M0, written in the padded expert-major layout the
+//          down projection reads.  (Reference: functional/__init__.py:260-275, QuACK gemm_act.)
+//   down : y = a x W2[e]^T over a 128x256 tile, then o[token] += score * y as bf16 vector
+//          atomics straight into the token-major output, i.e. the top-k weighted combine of
+//          functional/forward.py:64-85 fused into the GEMM epilogue.
+//
+// Tiles: 128 rows of one expert (the padded layout never mixes experts in a tile) x 256 output
+// columns, K consumed 128 at a time.  Roles per CTA (640 threads, one CTA per SM):
+//   warp 0      TMA producer: A and B tiles (128B swizzle) + scale-factor atoms (bulk copies)
+//   warp 1      MMA issuer: tcgen05.cp of the scale factors to tensor memory, then 4 x
+//               tcgen05.mma.kind::mxf8f6f4.block_scale (M=128, N=256, K=32) per stage
+//   warp 2      tensor-memory allocation (512 columns: accumulator 0-255, SFA 256-259, SFB 260-267)
+//   warps 4-19  epilogue: warp w reads TMEM lanes 32*(w%4)..+31, columns chunk (w-4)/4, releases
+//               the accumulator as soon as it sits in registers, then computes and stores while
+//               the next tile's main loop runs.
+// Tile schedule: static round robin over (m-block, n-tile), n fastest; the number of m-blocks is
+// read from device memory, so empty experts cost nothing and no host synchronisation is needed.
+// Every mbarrier wait is bounded (2 s); on a timeout the kernel records an error code, drains its
+// outstanding copies and MMAs with short bounded waits, frees tensor memory and returns.
+#include "common.cuh"
+#include "sonic_internal.h"
+
+namespace smb {
+
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+constexpr int kEpiWarps = 16;
+constexpr int kGemmThreads = (4 + kEpiWarps) * 32;
+constexpr int kABytes = kBlockM * kBlockK;  // 16 KB
+constexpr int kBBytes = kBN * kBlockK;      // 32 KB
+constexpr int kSfaBytes = kSfAtomBytes;
+constexpr int kSfbBytes = 2 * kSfAtomBytes;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemAcc = 0, kTmemSfa = 256, kTmemSfb = 260;
+
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kABytes;
+constexpr int kOffSfa = kOffB + kStages * kBBytes;
+constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
+constexpr int kOffBar = kOffSfb + kStages * kSfbBytes;
+constexpr int kNumBars = 2 * kStages + 4;
+constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
+constexpr int kOffAmax = (kOffTmemHolder + 4 + 15) / 16 * 16;
+constexpr int kAmaxFloats = 2 * 4 * kBlockM;
+constexpr int kSmemBytes = kOffAmax + kAmaxFloats * 4;
+constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack for 1024-byte alignment of the base
+static_assert(kSmemAlloc <= 232448, "shared memory budget");
+
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+__device__ __forceinline__ void red_add_bf16x8(void* addr, float a0, float a1, float a2, float a3, float a4,
+                                               float a5, float a6, float a7) {
+  __nv_bfloat162 p0 = __floats2bfloat162_rn(a0, a1);
+  __nv_bfloat162 p1 = __floats2bfloat162_rn(a2, a3);
+  __nv_bfloat162 p2 = __floats2bfloat162_rn(a4, a5);
+  __nv_bfloat162 p3 = __floats2bfloat162_rn(a6, a7);
+  asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(addr),
+               "r"(*reinterpret_cast<uint32_t*>(&p0)), "r"(*reinterpret_cast<uint32_t*>(&p1)),
+               "r"(*reinterpret_cast<uint32_t*>(&p2)), "r"(*reinterpret_cast<uint32_t*>(&p3))
+               : "memory");
+}
+
+template <bool kUp>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* sA = smem + kOffA;
+  uint8_t* sB = smem + kOffB;
+  uint8_t* sSfa = smem + kOffSfa;
+  uint8_t* sSfb = smem + kOffSfb;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* tmem_full = bars + 2 * kStages;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* drain = tmem_full + 2;
+  uint64_t* amax_bar = tmem_full + 3;  // all epilogue threads: row amax partials written
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffTmemHolder);
+  float* s_amax = reinterpret_cast<float*>(smem + kOffAmax);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, kEpiWarps);
+    mbar_init(drain, 1);
+    mbar_init(amax_bar, kEpiWarps * 32);
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  const int n_blocks = *g.n_blocks;
+  const int ntn = g.N / kBN;
+  const int total = n_blocks * ntn;
+  const int KB = g.Kd / kBlockK;
+  const int KG = (KB + 3) / 4;
+  const int nbk = g.N / kBlockM;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ TMA producer
+      const uint64_t pol_a = policy_evict_first();
+      const uint64_t pol_b = policy_evict_last();
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const int mb = tile / ntn, nt = tile - (tile / ntn) * ntn;
+        const int e = g.blk_expert[mb];
+        const int a_row = mb * kBlockM;
+        const int b_row = e * g.N + nt * kBN;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, g.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const bool sf = (kb & 3) == 0;
+          mbar_arrive_expect_tx(&full[s], kABytes + kBBytes + (sf ? kSfaBytes + kSfbBytes : 0));
+          tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBlockK, a_row, pol_a);
+          tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBlockK, b_row, pol_b);
+          if (sf) {
+            bulk_load(sSfa + s * kSfaBytes, g.a_sf + (static_cast<size_t>(mb) * KG + kb / 4) * kSfAtomBytes,
+                      kSfAtomBytes, &full[s]);
+            const size_t nb0 = static_cast<size_t>(e) * nbk + static_cast<size_t>(nt) * 2;
+            bulk_load(sSfb + s * kSfbBytes, g.b_sf + (nb0 * KG + kb / 4) * kSfAtomBytes, kSfAtomBytes, &full[s]);
+            bulk_load(sSfb + s * kSfbBytes + kSfAtomBytes, g.b_sf + ((nb0 + 1) * KG + kb / 4) * kSfAtomBytes,
+                      kSfAtomBytes, &full[s]);
+          }
+        }
+      }
+      if (!ok) {
+        // an error elsewhere: let the loads already issued land before shared memory goes away
+        const int first = it - kStages > 0 ? it - kStages : 0;
+        for (int j = first; j < it; ++j) mbar_wait_ns(&full[j % kStages], (j / kStages) & 1, 50000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      const uint32_t idesc0 = idesc_mxf8_e4m3(kBlockM, kBN, 0, 0);
+      int it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tcount) {
+        if (!mbar_wait(tmem_empty, (tcount & 1) ^ 1, g.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&full[s], ph, g.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t id = static_cast<uint32_t>(kb & 3);
+          if (id == 0) {
+            tc_cp_sf(tmem + kTmemSfa, sdesc_sf(smem_u32(sSfa + s * kSfaBytes)));
+            tc_cp_sf(tmem + kTmemSfb, sdesc_sf(smem_u32(sSfb + s * kSfbBytes)));
+            tc_cp_sf(tmem + kTmemSfb + 4, sdesc_sf(smem_u32(sSfb + s * kSfbBytes + kSfAtomBytes)));
+          }
+          const uint64_t ad = sdesc_sw128(smem_u32(sA + s * kABytes));
+          const uint64_t bd = sdesc_sw128(smem_u32(sB + s * kBBytes));
+          const uint32_t idesc = idesc0 | (id << 4) | (id << 29);
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 32; ++kk) {
+            // +32 bytes along K inside the 128-byte swizzle row = +2 in the 16-byte address field
+            tc_mma_mxf8(tmem + kTmemAcc, ad + 2 * kk, bd + 2 * kk, idesc, (tmem + kTmemSfa) | (id << 30),
+                        (tmem + kTmemSfb) | (id << 30), (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(tmem_full);
+      }
+      // every MMA issued by this thread has finished once `drain` completes
+      tc_commit(drain);
+      mbar_wait_ns(drain, 0, 100000000ull);
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------------- epilogue
+    const int ew = warp - 4;
+    const int q = warp & 3;
+    const int cc = ew >> 2;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tcount) {
+      const int mb = tile / ntn, nt = tile - (tile / ntn) * ntn;
+      const int e = g.blk_expert[mb];
+      if (!mbar_wait(tmem_full, tcount & 1, g.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      uint32_t v[64];
+      if (kUp && g.concat) {
+        tmem_ld32(lane_base + kTmemAcc + 32 * cc, v);
+        tmem_ld32(lane_base + kTmemAcc + 128 + 32 * cc, v + 32);
+      } else {
+        tmem_ld32(lane_base + kTmemAcc + 64 * cc, v);
+        tmem_ld32(lane_base + kTmemAcc + 64 * cc + 32, v + 32);
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tmem_empty);
+
+      const int p = mb * kBlockM + r;
+      const int rel = p - g.off_pad[e];
+      const bool valid = rel < g.freq[e];
+      if constexpr (kUp) {
+        float o[32];
+        float am = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float gt = __uint_as_float(g.concat ? v[j] : v[2 * j]);
+          const float up = __uint_as_float(g.concat ? v[32 + j] : v[2 * j + 1]);
+          o[j] = valid ? silu_f(gt) * up : 0.0f;
+          am = fmaxf(am, fabsf(o[j]));
+        }
+        float* amax_buf = s_amax + (tcount & 1) * (4 * kBlockM);
+        amax_buf[cc * kBlockM + r] = am;
+        mbar_arrive(amax_bar);
+        if (!mbar_wait(amax_bar, tcount & 1, g.err, kErrTimeoutEpilogue)) break;
+        am = fmaxf(fmaxf(amax_buf[r], amax_buf[kBlockM + r]), fmaxf(amax_buf[2 * kBlockM + r], amax_buf[3 * kBlockM + r]));
+        const int e8 = scale_exp_of_amax(am);
+        const float inv = exp2_neg(e8);
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          w[i] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(o[4 * i], inv), __fmul_rn(o[4 * i + 1], inv))) |
+                 (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(o[4 * i + 2], inv), __fmul_rn(o[4 * i + 3], inv)))
+                  << 16);
+        }
+        const int I2 = g.N / 2;
+        uint8_t* dst = g.out_q + static_cast<size_t>(p) * I2 + nt * kBlockM + cc * 32;
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        if (cc == 0) {
+          const int KG2 = (I2 / kBlockK + 3) / 4;
+          g.out_sf[(static_cast<size_t>(mb) * KG2 + nt / 4) * kSfAtomBytes + 16 * (r % 32) + 4 * (r / 32) + (nt % 4)] =
+              static_cast<uint8_t>(e8 + 127);
+        }
+      } else {
+        if (valid) {
+          const int rs = rel + g.off[e];
+          const int f = g.s_scatter[rs];
+          const int tok = g.x_gather[rs];
+          const float sc = g.scores[f];
+          __nv_bfloat16* dst =
+              static_cast<__nv_bfloat16*>(g.out_bf16) + static_cast<size_t>(tok) * g.N + nt * kBN + cc * 64;
+#pragma unroll
+          for (int j = 0; j < 64; j += 8) {
+            red_add_bf16x8(dst + j, sc * __uint_as_float(v[j]), sc * __uint_as_float(v[j + 1]),
+                           sc * __uint_as_float(v[j + 2]), sc * __uint_as_float(v[j + 3]),
+                           sc * __uint_as_float(v[j + 4]), sc * __uint_as_float(v[j + 5]),
+                           sc * __uint_as_float(v[j + 6]), sc * __uint_as_float(v[j + 7]));
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side: tensor maps and launch
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D e4m3 (byte) tensor [rows, cols] row-major; box = box_rows x 128 bytes with the 128B swizzle.
+static bool make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool kUp>
+static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
+  const long long max_blocks = g.a_rows / kBlockM;
+  const long long max_tiles = max_blocks * (g.N / kBN);
+  if (max_tiles == 0) return cudaSuccess;
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, g.a, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.Kd), kBlockM)) return cudaErrorInvalidValue;
+  if (!make_tmap(&tb, g.b, static_cast<uint64_t>(g.E) * g.N, static_cast<uint64_t>(g.Kd), kBN)) return cudaErrorInvalidValue;
+  auto kern = moe_gemm_kernel<kUp>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+  if (e != cudaSuccess) return e;
+  const int grid = static_cast<int>(max_tiles < g.num_sms ? max_tiles : g.num_sms);
+  kern<<<grid, kGemmThreads, kSmemAlloc, st>>>(ta, tb, g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st) { return launch_gemm<true>(g, st); }
+cudaError_t launch_moe_down(const GemmArgs& g, cudaStream_t st) { return launch_gemm<false>(g, st); }
+
+}  // namespace smb

@@ -1,0 +1,168 @@
+// Activation quantiser + scatter-pack, and weight quantiser (e4m3, UE8M0 power-of-two scales).
+//
+// Spec (identical to oracle/quant.py): per group amax = max|x|; e = ceil(log2(amax / 448)) taken
+// exactly from the float32 bits and clamped to [-127, 127]; q = e4m3_rn_satfinite(x * 2^-e);
+// scale byte = e + 127.  Groups are 1x128 along K for activations and 128x128 for weights.
+//
+// Scale-factor atoms: 512 bytes per (128 rows, 4 consecutive 128-wide K blocks); byte
+// 16*(r % 32) + 4*((r % 128) / 32) + (kb % 4) belongs to row r, K block kb -- the order in which
+// tcgen05.cp 32x128b.warpx4 lays scale factors out in tensor memory for the block-scaled MMA.
+#include "common.cuh"
+#include "sonic_internal.h"
+
+namespace smb {
+
+constexpr int kQuantWarps = 8;
+constexpr int kQuantBatch = 4;  // 256-element chunks loaded before any is processed
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& raw, float* v) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// One warp per token.  Lane l covers elements [h0 + 8l, h0 + 8l + 8) of each 256-wide chunk, so
+// lanes 0-15 and 16-31 each hold one 128-wide group.  The token's quantised row and scale bytes
+// are written to each of its K destination rows of the padded expert-major layout
+// (row = s_rev[f] - off[e] + off_pad[e] for entry f = t*K + k, e = experts[f]).  With
+// experts == nullptr the destination is row t itself (plain token-order quantisation, K = 1).
+__global__ void __launch_bounds__(kQuantWarps * 32)
+    quant_pack_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, const int32_t* __restrict__ experts, int K,
+                      const int32_t* __restrict__ s_rev, const int32_t* __restrict__ off,
+                      const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq, uint8_t* __restrict__ xsf) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kQuantWarps + warp;
+  if (t >= T) return;
+  const int ncopy = experts ? K : 1;
+  int my_dst = 0;
+  if (!experts) {
+    my_dst = t;
+  } else if (lane < K) {
+    const int f = t * K + lane;
+    const int e = experts[f];
+    my_dst = s_rev[f] - off[e] + off_pad[e];
+  }
+  const int KG = (H / kBlockK + 3) / 4;
+  const __nv_bfloat16* src = x + static_cast<size_t>(t) * H;
+  uint32_t sfword = 0;
+  for (int hb = 0; hb < H; hb += 256 * kQuantBatch) {
+    uint4 raw[kQuantBatch];
+#pragma unroll
+    for (int c = 0; c < kQuantBatch; ++c) {
+      const int h = hb + 256 * c + 8 * lane;
+      raw[c] = (h < H) ? *reinterpret_cast<const uint4*>(src + h) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int c = 0; c < kQuantBatch; ++c) {
+      const int h0 = hb + 256 * c;
+      if (h0 >= H) break;
+      const int h = h0 + 8 * lane;
+      float v[8];
+      bf16x8_to_f32(raw[c], v);
+      float am = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      const int e8 = scale_exp_of_amax(am);
+      const float inv = exp2_neg(e8);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int i = 0; i < 4; i += 2) {
+        lo |= static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[i], inv), __fmul_rn(v[i + 1], inv))) << (8 * i);
+        hi |= static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[4 + i], inv), __fmul_rn(v[5 + i], inv))) << (8 * i);
+      }
+      const uint2 packed = make_uint2(lo, hi);
+      for (int k = 0; k < ncopy; ++k) {
+        const int p = __shfl_sync(0xffffffffu, my_dst, k);
+        if (h < H) *reinterpret_cast<uint2*>(xq + static_cast<size_t>(p) * H + h) = packed;
+      }
+      const int gA = h0 / kBlockK;
+      const int eA = __shfl_sync(0xffffffffu, e8, 0);
+      const int eB = __shfl_sync(0xffffffffu, e8, 16);
+      sfword |= static_cast<uint32_t>(eA + 127) << (8 * (gA % 4));
+      if (h0 + 128 < H) sfword |= static_cast<uint32_t>(eB + 127) << (8 * ((gA + 1) % 4));
+      if ((gA % 4) == 2 || h0 + 256 >= H) {
+        const int kg = gA / 4;
+        if (lane < ncopy) {
+          const int p = my_dst;
+          const size_t o = (static_cast<size_t>(p / kBlockM) * KG + kg) * kSfAtomBytes + 16 * (p % 32) +
+                           4 * ((p % kBlockM) / 32);
+          *reinterpret_cast<uint32_t*>(xsf + o) = sfword;
+        }
+        sfword = 0;
+      }
+    }
+  }
+}
+
+// One CTA per 128x128 block: blockIdx = (k block, destination n block, expert).  With concat_glu
+// the destination row blocks interleave the gate and up halves at 128-row granularity:
+// destination block 2j <- gate block j, 2j+1 <- up block j (rows I + 128j ...).
+__global__ void __launch_bounds__(256)
+    weight_prep_kernel(const __nv_bfloat16* __restrict__ w, int E, int N, int Kd, int concat_glu,
+                       uint8_t* __restrict__ wq, uint8_t* __restrict__ wsf) {
+  __shared__ float s_red[8];
+  const int kb = blockIdx.x, nb = blockIdx.y, e = blockIdx.z;
+  const int nbs = concat_glu ? ((nb % 2 == 0) ? nb / 2 : (N / 2) / kBlockM + nb / 2) : nb;
+  const int tid = threadIdx.x;
+  const int row = tid >> 1, half = tid & 1;
+  const __nv_bfloat16* src =
+      w + (static_cast<size_t>(e) * N + static_cast<size_t>(nbs) * kBlockM + row) * Kd + kb * kBlockK + half * 64;
+  float v[64];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) bf16x8_to_f32(reinterpret_cast<const uint4*>(src)[i], v + 8 * i);
+  float am = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+  if ((tid & 31) == 0) s_red[tid >> 5] = am;
+  __syncthreads();
+  am = s_red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) am = fmaxf(am, s_red[i]);
+  const int e8 = scale_exp_of_amax(am);
+  const float inv = exp2_neg(e8);
+  uint8_t* dst =
+      wq + (static_cast<size_t>(e) * N + static_cast<size_t>(nb) * kBlockM + row) * Kd + kb * kBlockK + half * 64;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t wd[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float* q = v + 16 * i + 4 * j;
+      wd[j] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[0], inv), __fmul_rn(q[1], inv))) |
+              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[2], inv), __fmul_rn(q[3], inv))) << 16);
+    }
+    reinterpret_cast<uint4*>(dst)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+  if (tid < 128) {
+    const int KG = (Kd / kBlockK + 3) / 4;
+    const size_t atom = ((static_cast<size_t>(e) * (N / kBlockM) + nb) * KG + kb / 4) * kSfAtomBytes;
+    wsf[atom + 16 * (tid >> 2) + 4 * (tid & 3) + (kb % 4)] = static_cast<uint8_t>(e8 + 127);
+  }
+}
+
+cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* s_rev,
+                              const int32_t* off, const int32_t* off_pad, uint8_t* xq, uint8_t* xsf,
+                              cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  const int grid = (T + kQuantWarps - 1) / kQuantWarps;
+  quant_pack_kernel<<<grid, kQuantWarps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, experts, K, s_rev,
+                                                       off, off_pad, xq, xsf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_glu, uint8_t* wq, uint8_t* wsf,
+                               cudaStream_t st) {
+  if (E == 0) return cudaSuccess;
+  dim3 grid(Kd / kBlockK, N / kBlockM, E);
+  weight_prep_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), E, N, Kd, concat_glu, wq, wsf);
+  return cudaGetLastError();
+}
+
+}  // namespace smb

@@ -1,0 +1,75 @@
+// Internal constants and kernel launchers shared by the .cu files of libsonic_b200.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace smb {
+
+constexpr int kTileTokens = 128;  // tokens per routing tile (router histogram / scatter)
+constexpr int kBlockM = 128;      // GEMM tile height; experts are padded to multiples of it
+constexpr int kBlockK = 128;      // K extent of one pipeline stage (= one scale-factor group)
+constexpr int kSfAtomBytes = 512; // 128 rows x 4 K-blocks of UE8M0 scale factors
+
+enum Dtype : int { kDtypeBF16 = 0, kDtypeF16 = 1, kDtypeF32 = 2 };
+
+inline int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+
+// Upper bound on the number of 128-row blocks of the padded expert layout.
+inline int max_padded_blocks(long long TK, int E) {
+  const long long nonempty = TK < E ? TK : E;
+  return static_cast<int>((TK + kBlockM - 1) / kBlockM + nonempty);
+}
+
+cudaError_t launch_router_topk(const void* logits, int dtype, int T, int E, int K, int sot, int renorm,
+                               float* scores, int32_t* idx, int32_t* tile_counts, cudaStream_t st);
+cudaError_t launch_route_hist(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,
+                              int32_t* tile_counts, int* err, cudaStream_t st);
+cudaError_t launch_route_scan(int32_t* tile_counts, int n_tiles, int E, int TK, int32_t* freq, int32_t* off,
+                              int32_t* off_pad, int32_t* blk_expert, int32_t* n_blocks, cudaStream_t st);
+cudaError_t launch_route_scatter(const int32_t* experts, const int32_t* token_of_entry, int TK, int K,
+                                 int entries_per_tile, int E, int n_tiles, const int32_t* tile_base,
+                                 const int32_t* off, int32_t* s_scatter, int32_t* s_rev, int32_t* x_gather,
+                                 cudaStream_t st);
+cudaError_t launch_token_offset(const int32_t* sorted_tokens, int T, int TK, int32_t* offset, cudaStream_t st);
+
+cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* s_rev,
+                              const int32_t* off, const int32_t* off_pad, uint8_t* xq, uint8_t* xsf,
+                              cudaStream_t st);
+cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_glu, uint8_t* wq, uint8_t* wsf,
+                               cudaStream_t st);
+
+struct GemmArgs {
+  // A: padded expert-major activations [rows, Kd] e4m3 + SF atoms [rows/128][ceil(Kd/512)][512]
+  const uint8_t* a;
+  const uint8_t* a_sf;
+  long long a_rows;
+  // B: expert weights [E, N, Kd] e4m3 + SF atoms [E][N/128][ceil(Kd/512)][512]
+  const uint8_t* b;
+  const uint8_t* b_sf;
+  int E, N, Kd;
+  // padded layout
+  const int32_t* blk_expert;
+  const int32_t* n_blocks;
+  const int32_t* off_pad;
+  const int32_t* off;
+  const int32_t* freq;
+  // up-projection outputs: intermediate [rows, N/2] e4m3 + SF atoms
+  uint8_t* out_q;
+  uint8_t* out_sf;
+  int concat;  // 1: B rows are 128-row blocks [gate_j; up_j] (concatenated w1 after weight prep)
+  // down-projection epilogue: o[token] += score * y (bf16 atomics)
+  const int32_t* s_scatter;
+  const int32_t* x_gather;
+  const float* scores;
+  void* out_bf16;
+  int* err;
+  int num_sms;
+};
+
+cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st);
+cudaError_t launch_moe_down(const GemmArgs& g, cudaStream_t st);
+
+}  // namespace smb

@@ -1,0 +1,168 @@
+"""Functional API of the reference (``sonicmoe/functional/__init__.py``), on the FP8 B200 engine.
+
+Same names, arguments and return values as the reference:
+
+* ``moe_TC_softmax_topk_layer`` (reference ``functional/__init__.py:482-557``)
+* ``moe_general_routing_inputs`` (reference ``functional/__init__.py:571-652``)
+* ``TC_topk_router_metadata_triton`` / ``general_routing_router_metadata_triton`` and
+  ``_topk_softmax_fwd`` (reference ``triton_kernels/__init__.py:78-146, 281-353``,
+  ``forward.py:107-141``), here backed by the CUDA metadata and router kernels.
+
+Weight-format contract (reference ``functional/__init__.py:560-566``): ``w1`` is the
+``(2I, H, E)`` view of ``c_fc.weight`` ``[E, 2I, H]`` (stride order (2, 0, 1)), interleaved
+``[g0, u0, g1, u1, ...]`` or, with ``concat_layout=True``, ``[g0..g_{I-1}, u0..u_{I-1}]``;
+``w2`` is the ``(H, I, E)`` view of ``c_proj.weight`` ``[E, H, I]``.  The bf16 weights are
+quantised to e4m3 with 128x128 UE8M0 block scales on first use and cached per weight version;
+already prepared :class:`~sonicmoe.ops.Fp8ExpertWeights` may be passed instead.
+
+Differences from the reference, all explicit errors: biases and activations other than SwiGLU
+raise ``NotImplementedError`` (the FP8 engine implements the bias-free SwiGLU layer); the forward
+is inference-only (no autograd graph is recorded).
+"""
+from collections import OrderedDict
+
+import torch
+import torch.nn.functional as F
+
+from .. import ops
+from ..enums import ActivationType
+from ..ops import Fp8ExpertWeights
+
+__all__ = [
+    "moe_TC_softmax_topk_layer",
+    "moe_general_routing_inputs",
+    "TC_topk_router_metadata_triton",
+    "general_routing_router_metadata_triton",
+    "prepare_fp8_weights",
+    "Fp8ExpertWeights",
+]
+
+_WEIGHT_CACHE: "OrderedDict[tuple, Fp8ExpertWeights]" = OrderedDict()
+_WEIGHT_CACHE_SIZE = 8
+
+
+def _as_expert_major(w: torch.Tensor) -> torch.Tensor:
+    """(N, K, E) reference view -> [E, N, K] tensor (a view when w came from permute(1, 2, 0))."""
+    return w.permute(2, 0, 1)
+
+
+def prepare_fp8_weights(w, concat_glu: bool = False) -> Fp8ExpertWeights:
+    """e4m3 + 128x128 UE8M0 version of an expert weight given in the reference's (N, K, E) view.
+
+    Cached on (storage pointer, version counter, shape, strides, layout), so repeated forwards with
+    unchanged weights quantise once.
+    """
+    if isinstance(w, Fp8ExpertWeights):
+        return w
+    key = (w.data_ptr(), w._version, tuple(w.shape), tuple(w.stride()), bool(concat_glu), w.dtype)
+    hit = _WEIGHT_CACHE.get(key)
+    if hit is not None:
+        _WEIGHT_CACHE.move_to_end(key)
+        return hit
+    with torch.no_grad():
+        prepared = ops.weight_prep(_as_expert_major(w.detach()), concat_glu=concat_glu)
+    _WEIGHT_CACHE[key] = prepared
+    while len(_WEIGHT_CACHE) > _WEIGHT_CACHE_SIZE:
+        _WEIGHT_CACHE.popitem(last=False)
+    return prepared
+
+
+def _check_common(b1, b2, activation_type):
+    assert ((b1 is None) and (b2 is None)) or (
+        (b1 is not None) and (b2 is not None)
+    ), "b1 and b2 has to be None or not None at the same time!"
+    if b1 is not None:
+        raise NotImplementedError("the FP8 engine implements the bias-free layer (b1 = b2 = None)")
+    if isinstance(activation_type, str):
+        activation_type = ActivationType(activation_type)
+    if activation_type != ActivationType.SWIGLU:
+        raise NotImplementedError(f"the FP8 engine implements SwiGLU only, got {activation_type}")
+    return activation_type
+
+
+def moe_TC_softmax_topk_layer(
+    x: torch.Tensor,
+    router_w: torch.Tensor,
+    w1,
+    b1,
+    w2,
+    b2,
+    K: int,
+    stream_id: int,
+    activation_type=ActivationType.SWIGLU,
+    is_inference_mode_enabled: bool = False,
+    is_softmax_over_topk: bool = True,
+    norm_topk_probs: bool = False,
+    concat_layout: bool = False,
+):
+    """Token-choice top-k MoE layer forward.  Returns (o [T, H], router_logits [T, E], expert_frequency [E]).
+
+    ``stream_id`` is ignored, as in the reference (the current torch stream is used).
+    """
+    _check_common(b1, b2, activation_type)
+    if norm_topk_probs and is_softmax_over_topk:
+        raise ValueError("`norm_topk_prob` only works with softmax-then-topk")
+    E = router_w.size(0)
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    x = x.contiguous()
+    router_logits = F.linear(x, router_w.to(x.dtype))
+    w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+    w2q = prepare_fp8_weights(w2, concat_glu=False)
+    if w1q.concat_glu != bool(concat_layout):
+        raise ValueError("prepared w1 layout does not match concat_layout")
+    o, expert_frequency = ops.moe_forward(
+        x, router_logits.contiguous(), w1q, w2q, K, is_softmax_over_topk, norm_topk_probs
+    )
+    return o, router_logits, expert_frequency
+
+
+def moe_general_routing_inputs(
+    x: torch.Tensor,
+    router_scores: torch.Tensor,
+    token_indices: torch.Tensor,
+    expert_indices: torch.Tensor,
+    w1,
+    b1,
+    w2,
+    b2,
+    E: int,
+    stream_id: int,
+    activation_type=ActivationType.SWIGLU,
+    is_inference_mode_enabled: bool = False,
+    concat_layout: bool = False,
+):
+    """MoE forward from explicit (token, expert, score) lists; token_indices must be sorted ascending.
+
+    Returns (o [T, H], expert_frequency [E]).
+    """
+    _check_common(b1, b2, activation_type)
+    raise NotImplementedError("moe_general_routing_inputs is not implemented by the FP8 engine yet")
+
+
+def TC_topk_router_metadata_triton(
+    topk_router_indices, E, expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx,
+    s_reverse_scatter_idx,
+) -> None:
+    """Reference signature (triton_kernels/__init__.py:78-86): fills the five output tensors in place."""
+    res = ops.route_metadata(topk_router_indices.to(torch.int32).contiguous(), E)
+    for dst, src in zip(
+        (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx), res
+    ):
+        dst.copy_(src)
+
+
+def general_routing_router_metadata_triton(
+    sorted_selected_T, selected_E, T, E, expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx,
+    s_reverse_scatter_idx, num_activated_expert_per_token_offset,
+) -> None:
+    """Reference signature (triton_kernels/__init__.py:281-292): fills the six output tensors in place."""
+    res = ops.general_route_metadata(
+        sorted_selected_T.to(torch.int32).contiguous(), selected_E.to(torch.int32).contiguous(), T, E
+    )
+    for dst, src in zip(
+        (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx,
+         num_activated_expert_per_token_offset),
+        res,
+    ):
+        dst.copy_(src)

@@ -1,0 +1,284 @@
+"""Torch-facing wrappers of the libsonic_b200 entry points.
+
+Every function takes/returns CUDA tensors, validates dtypes and contiguity, and enqueues the
+kernels on the current torch CUDA stream (the reference's ops run on the current stream too,
+``sonicmoe/functional/forward.py:43``).  Nothing here computes on the host.
+"""
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as nat
+
+_BLOCK_M = 128
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need(t: torch.Tensor, name: str, dtype=None):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+_LOGIT_DTYPES = {torch.bfloat16: nat.DTYPE_BF16, torch.float16: nat.DTYPE_F16, torch.float32: nat.DTYPE_F32}
+
+
+def router_topk(router_logits: torch.Tensor, K: int, softmax_over_topk: bool = True, norm_topk_probs: bool = False):
+    """(scores fp32 [T,K], indices int32 [T,K]) -- reference ``_topk_softmax_fwd`` (forward.py:107-141)."""
+    _need(router_logits, "router_logits")
+    if router_logits.dtype not in _LOGIT_DTYPES:
+        raise ValueError(f"unsupported logits dtype {router_logits.dtype}")
+    T, E = router_logits.shape
+    scores = torch.empty(T, K, dtype=torch.float32, device=router_logits.device)
+    idx = torch.empty(T, K, dtype=torch.int32, device=router_logits.device)
+    nat.call(
+        "sm_router_topk",
+        _ptr(router_logits),
+        _LOGIT_DTYPES[router_logits.dtype],
+        T,
+        E,
+        K,
+        int(softmax_over_topk),
+        int(norm_topk_probs),
+        _ptr(scores),
+        _ptr(idx),
+        _stream(),
+    )
+    return scores, idx
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+def route_metadata(topk_indices: torch.Tensor, E: int, err: torch.Tensor = None):
+    """Reference ``TC_topk_router_metadata_triton`` (triton_kernels/__init__.py:78-146).
+
+    Returns (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx).
+    """
+    _need(topk_indices, "topk_indices", torch.int32)
+    T, K = topk_indices.shape
+    TK = T * K
+    dev = topk_indices.device
+    freq = torch.empty(E, dtype=torch.int32, device=dev)
+    off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    xg = torch.empty(TK, dtype=torch.int32, device=dev)
+    ss = torch.empty(TK, dtype=torch.int32, device=dev)
+    sr = torch.empty(TK, dtype=torch.int32, device=dev)
+    if err is None:
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _workspace(nat.load().sm_route_metadata_workspace(T, TK, E), dev)
+    nat.call(
+        "sm_route_metadata", _ptr(topk_indices), T, K, E, _ptr(freq), _ptr(off), _ptr(xg), _ptr(ss), _ptr(sr),
+        _ptr(ws), ws.numel(), _ptr(err), _stream(),
+    )
+    return freq, off, xg, ss, sr
+
+
+def general_route_metadata(sorted_token_idx: torch.Tensor, expert_idx: torch.Tensor, T: int, E: int, err=None):
+    """Reference ``general_routing_router_metadata_triton`` (triton_kernels/__init__.py:281-353).
+
+    Returns (freq, offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx, token_offset[T+1]).
+    """
+    _need(sorted_token_idx, "sorted_token_idx", torch.int32)
+    _need(expert_idx, "expert_idx", torch.int32)
+    TK = expert_idx.numel()
+    dev = expert_idx.device
+    freq = torch.empty(E, dtype=torch.int32, device=dev)
+    off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    xg = torch.empty(TK, dtype=torch.int32, device=dev)
+    ss = torch.empty(TK, dtype=torch.int32, device=dev)
+    sr = torch.empty(TK, dtype=torch.int32, device=dev)
+    tok_off = torch.empty(T + 1, dtype=torch.int32, device=dev)
+    if err is None:
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _workspace(nat.load().sm_route_metadata_workspace(T, TK, E), dev)
+    nat.call(
+        "sm_general_route_metadata", _ptr(sorted_token_idx), _ptr(expert_idx), T, TK, E, _ptr(freq), _ptr(off),
+        _ptr(xg), _ptr(ss), _ptr(sr), _ptr(tok_off), _ptr(ws), ws.numel(), _ptr(err), _stream(),
+    )
+    return freq, off, xg, ss, sr, tok_off
+
+
+def quant_1x128(x: torch.Tensor):
+    """1x128 e4m3 quantisation in token order: (q uint8 [R,C], sf atoms uint8 [ceil(R/128), ceil(C/512), 512])."""
+    _need(x, "x", torch.bfloat16)
+    R, C = x.shape
+    q = torch.empty(R, C, dtype=torch.uint8, device=x.device)
+    sf = torch.zeros(-(-R // _BLOCK_M), -(-C // 512), 512, dtype=torch.uint8, device=x.device)
+    nat.call("sm_quant_1x128", _ptr(x), R, C, _ptr(q), _ptr(sf), _stream())
+    return q, sf
+
+
+@dataclass
+class Fp8ExpertWeights:
+    """e4m3 expert weights + 128x128 UE8M0 scale atoms, as produced by ``weight_prep``.
+
+    ``q``: [E, N, K] uint8 (e4m3 bits); ``sf``: [E, N/128, ceil(K/512), 512] uint8;
+    ``concat_glu``: the rows were re-blocked from a concatenated [gate; up] layout.
+    """
+
+    q: torch.Tensor
+    sf: torch.Tensor
+    concat_glu: bool
+
+    @property
+    def shape(self):
+        return tuple(self.q.shape)
+
+
+def weight_prep(w: torch.Tensor, concat_glu: bool = False) -> Fp8ExpertWeights:
+    """Quantise expert weights [E, N, K] (bf16) to e4m3 with 128x128 UE8M0 scales."""
+    if w.dtype != torch.bfloat16:
+        w = w.to(torch.bfloat16)
+    w = w.contiguous()
+    _need(w, "w", torch.bfloat16)
+    E, N, K = w.shape
+    q = torch.empty(E, N, K, dtype=torch.uint8, device=w.device)
+    sf = torch.zeros(E, N // _BLOCK_M, -(-(K // 128) // 4), 512, dtype=torch.uint8, device=w.device)
+    nat.call("sm_weight_prep", _ptr(w), E, N, K, int(concat_glu), _ptr(q), _ptr(sf), _stream())
+    return Fp8ExpertWeights(q, sf, bool(concat_glu))
+
+
+def max_padded_blocks(TK: int, E: int) -> int:
+    return nat.load().sm_max_padded_blocks(TK, E)
+
+
+@dataclass
+class RoutePlan:
+    """Routing metadata plus the 128-row padded expert layout the GEMMs run on."""
+
+    freq: torch.Tensor
+    off: torch.Tensor
+    x_gather: torch.Tensor
+    s_scatter: torch.Tensor
+    s_rev: torch.Tensor
+    off_pad: torch.Tensor
+    blk_expert: torch.Tensor
+    n_blocks: torch.Tensor
+    max_blocks: int
+
+
+def route_plan(topk_indices: torch.Tensor, E: int, err: torch.Tensor) -> RoutePlan:
+    _need(topk_indices, "topk_indices", torch.int32)
+    T, K = topk_indices.shape
+    TK = T * K
+    dev = topk_indices.device
+    mb = max_padded_blocks(TK, E)
+    p = RoutePlan(
+        freq=torch.empty(E, dtype=torch.int32, device=dev),
+        off=torch.empty(E + 1, dtype=torch.int32, device=dev),
+        x_gather=torch.empty(TK, dtype=torch.int32, device=dev),
+        s_scatter=torch.empty(TK, dtype=torch.int32, device=dev),
+        s_rev=torch.empty(TK, dtype=torch.int32, device=dev),
+        off_pad=torch.empty(E + 1, dtype=torch.int32, device=dev),
+        blk_expert=torch.empty(mb + 1, dtype=torch.int32, device=dev),
+        n_blocks=torch.empty(1, dtype=torch.int32, device=dev),
+        max_blocks=mb,
+    )
+    ws = _workspace(nat.load().sm_route_metadata_workspace(T, TK, E), dev)
+    nat.call(
+        "sm_route_plan", _ptr(topk_indices), T, K, E, _ptr(p.freq), _ptr(p.off), _ptr(p.x_gather),
+        _ptr(p.s_scatter), _ptr(p.s_rev), _ptr(p.off_pad), _ptr(p.blk_expert), _ptr(p.n_blocks), _ptr(ws),
+        ws.numel(), _ptr(err), _stream(),
+    )
+    return p
+
+
+def quant_pack(x: torch.Tensor, topk_indices: torch.Tensor, plan: RoutePlan):
+    """Quantise x and place each token at its K padded rows: (xq [mb*128, H], xsf atoms)."""
+    _need(x, "x", torch.bfloat16)
+    T, H = x.shape
+    K = topk_indices.shape[1]
+    xq = torch.empty(plan.max_blocks * _BLOCK_M, H, dtype=torch.uint8, device=x.device)
+    xsf = torch.zeros(plan.max_blocks, -(-H // 512), 512, dtype=torch.uint8, device=x.device)
+    nat.call(
+        "sm_quant_pack", _ptr(x), T, H, _ptr(topk_indices), K, _ptr(plan.s_rev), _ptr(plan.off), _ptr(plan.off_pad),
+        _ptr(xq), _ptr(xsf), _stream(),
+    )
+    return xq, xsf
+
+
+def moe_up(xq, xsf, w1: Fp8ExpertWeights, plan: RoutePlan, err):
+    E, N2, H = w1.shape
+    I = N2 // 2
+    aq = torch.empty(plan.max_blocks * _BLOCK_M, I, dtype=torch.uint8, device=xq.device)
+    asf = torch.zeros(plan.max_blocks, -(-I // 512), 512, dtype=torch.uint8, device=xq.device)
+    nat.call(
+        "sm_moe_up", _ptr(xq), _ptr(xsf), _ptr(w1.q), _ptr(w1.sf), H, I, E, int(w1.concat_glu), plan.max_blocks,
+        _ptr(plan.blk_expert), _ptr(plan.n_blocks), _ptr(plan.off_pad), _ptr(plan.freq), _ptr(aq), _ptr(asf),
+        _ptr(err), _stream(),
+    )
+    return aq, asf
+
+
+def moe_down_combine(aq, asf, w2: Fp8ExpertWeights, plan: RoutePlan, scores: torch.Tensor, T: int, err, out=None):
+    E, H, I = w2.shape
+    if out is None:
+        out = torch.zeros(T, H, dtype=torch.bfloat16, device=aq.device)
+    nat.call(
+        "sm_moe_down_combine", _ptr(aq), _ptr(asf), _ptr(w2.q), _ptr(w2.sf), H, I, E, plan.max_blocks,
+        _ptr(plan.blk_expert), _ptr(plan.n_blocks), _ptr(plan.off_pad), _ptr(plan.off), _ptr(plan.freq),
+        _ptr(plan.s_scatter), _ptr(plan.x_gather), _ptr(scores), _ptr(out), _ptr(err), _stream(),
+    )
+    return out
+
+
+_WS_CACHE = {}
+
+
+def moe_forward(
+    x: torch.Tensor,
+    router_logits: torch.Tensor,
+    w1: Fp8ExpertWeights,
+    w2: Fp8ExpertWeights,
+    K: int,
+    softmax_over_topk: bool = True,
+    norm_topk_probs: bool = False,
+    out: torch.Tensor = None,
+    expert_frequency: torch.Tensor = None,
+    topk_scores: torch.Tensor = None,
+    topk_indices: torch.Tensor = None,
+    err: torch.Tensor = None,
+):
+    """The whole FP8 layer forward after the router GEMM (one C-ABI call, 7 kernels).
+
+    The scratch workspace is cached per (device, size) and shared by every call of that shape, so
+    concurrent calls of the same shape on different streams must not overlap.
+    """
+    _need(x, "x", torch.bfloat16)
+    _need(router_logits, "router_logits", torch.bfloat16)
+    T, H = x.shape
+    E, N2, H1 = w1.shape
+    E2, H2, I = w2.shape
+    if H1 != H or H2 != H or N2 != 2 * I or E2 != E or router_logits.shape != (T, E):
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)}, logits {tuple(router_logits.shape)}, "
+                         f"w1 {w1.shape}, w2 {w2.shape}")
+    dev = x.device
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    if expert_frequency is None:
+        expert_frequency = torch.empty(E, dtype=torch.int32, device=dev)
+    nbytes = nat.load().sm_moe_workspace_bytes(T, H, I, E, K)
+    key = (dev.index, nbytes)
+    ws = _WS_CACHE.get(key)
+    if ws is None:
+        # kept for the life of the process: a captured CUDA graph may still point at it
+        ws = _workspace(nbytes, dev)
+        _WS_CACHE[key] = ws
+    nat.call(
+        "sm_moe_forward", _ptr(x), _ptr(router_logits), T, H, I, E, K, int(softmax_over_topk), int(norm_topk_probs),
+        int(w1.concat_glu), _ptr(w1.q), _ptr(w1.sf), _ptr(w2.q), _ptr(w2.sf), _ptr(out), _ptr(expert_frequency),
+        _ptr(topk_scores), _ptr(topk_indices), _ptr(ws), ws.numel(), _ptr(err), _stream(),
+    )
+    return out, expert_frequency

@@ -1,0 +1,170 @@
+"""GPU parity of the FP8 GEMM stages and the whole layer against the fake-quantised oracle.
+
+Tolerance (north star): relative Frobenius error <= 1e-2 against the reference math run on the
+same e4m3 operands (oracle.layer.fp8_oracle).  The gap to the dense bf16 oracle is reported, not
+asserted: e4m3 with 1x128 / 128x128 scales sits near 6e-2 there for these distributions.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import layer as olayer
+from oracle import metadata as ometa
+from oracle import quant as oq
+from oracle import routing as oroute
+from _util import make_layer_inputs, rel_fro, sf_bytes_of_rows
+
+pytestmark = pytest.mark.gpu
+
+TOL_FP8 = 1e-2
+
+
+@pytest.fixture(scope="module")
+def sm():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import sonicmoe
+    from sonicmoe import ops
+
+    return sonicmoe, ops
+
+
+def _prep(ops, w1, w2, concat):
+    return ops.weight_prep(w1.cuda(), concat_glu=concat), ops.weight_prep(w2.cuda(), concat_glu=False)
+
+
+def _oracle_a_rows(x, w1, idx, concat):
+    """Oracle SwiGLU output (float64) for every flat entry, from fake-quantised x and w1."""
+    xq, xs = oq.quant_1x128(x.float().numpy())
+    xd = oq.dequant_1x128(xq, xs).astype(np.float64)
+    w1q, w1s = oq.quant_128x128(w1.float().numpy())
+    w1d = oq.dequant_128x128(w1q, w1s).astype(np.float64)
+    T, K = idx.shape
+    I = w1.shape[1] // 2
+    a = np.zeros((T * K, I))
+    for f in range(T * K):
+        t, e = f // K, idx.reshape(-1)[f]
+        h = w1d[e] @ xd[t]
+        g, u = (h[:I], h[I:]) if concat else (h[0::2], h[1::2])
+        a[f] = g / (1.0 + np.exp(-g)) * u
+    return a
+
+
+@pytest.mark.parametrize("concat", [False, True])
+@pytest.mark.parametrize("T,H,I,E,K", [(256, 512, 256, 8, 2), (200, 256, 384, 4, 2)])
+def test_moe_up_stage(sm, T, H, I, E, K, concat):
+    _, ops = sm
+    x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=T + I)
+    logits = (x.float() @ rw.float().T).to(torch.bfloat16)
+    _, idx = oroute.topk_route(logits.float().numpy(), K)
+    w1p, _ = _prep(ops, w1, w2, concat)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    idx_t = torch.from_numpy(idx).cuda()
+    plan = ops.route_plan(idx_t, E, err)
+    xq, xsf = ops.quant_pack(x.cuda(), idx_t, plan)
+    aq, asf = ops.moe_up(xq, xsf, w1p, plan, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0, f"kernel error word {err.item()}"
+    freq, off, _, _, s_rev = ometa.tc_metadata(idx, E)
+    off_pad, _, _ = ometa.padded_layout(freq)
+    rows = ometa.padded_rows(idx, s_rev, off, off_pad)
+    a_ref = _oracle_a_rows(x, w1, idx, concat)
+    q_gpu = aq.cpu().numpy()[rows]
+    sf_gpu = sf_bytes_of_rows(asf.cpu().numpy(), rows, I // 128)
+    a_gpu = oq.dequant_1x128(q_gpu, sf_gpu)
+    assert rel_fro(a_gpu, a_ref) < 3e-2  # e4m3 requantisation of `a` dominates
+    q_ref, sf_ref = oq.quant_1x128(a_ref.astype(np.float32))
+    assert (q_gpu == q_ref).mean() > 0.97  # codes agree except at rounding boundaries
+    assert (sf_gpu == sf_ref).mean() > 0.99
+
+
+@pytest.mark.parametrize("T,H,I,E,K", [(256, 512, 256, 8, 2), (300, 768, 128, 16, 4)])
+def test_moe_down_stage(sm, T, H, I, E, K):
+    _, ops = sm
+    x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=T + H)
+    logits = (x.float() @ rw.float().T).to(torch.bfloat16)
+    scores, idx = oroute.topk_route(logits.float().numpy(), K)
+    w1p, w2p = _prep(ops, w1, w2, False)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    idx_t = torch.from_numpy(idx).cuda()
+    plan = ops.route_plan(idx_t, E, err)
+    xq, xsf = ops.quant_pack(x.cuda(), idx_t, plan)
+    aq, asf = ops.moe_up(xq, xsf, w1p, plan, err)
+    out = ops.moe_down_combine(aq, asf, w2p, plan, torch.from_numpy(scores).cuda(), T, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    # oracle down projection on the GPU's own intermediate
+    freq, off, _, _, s_rev = ometa.tc_metadata(idx, E)
+    off_pad, _, _ = ometa.padded_layout(freq)
+    rows = ometa.padded_rows(idx, s_rev, off, off_pad)
+    a_gpu = oq.dequant_1x128(aq.cpu().numpy()[rows], sf_bytes_of_rows(asf.cpu().numpy(), rows, I // 128))
+    w2q, w2s = oq.quant_128x128(w2.float().numpy())
+    w2d = oq.dequant_128x128(w2q, w2s).astype(np.float64)
+    o_ref = np.zeros((T, H))
+    flat_e = idx.reshape(-1)
+    for f in range(T * K):
+        o_ref[f // K] += scores.reshape(-1)[f] * (w2d[flat_e[f]] @ a_gpu[f].astype(np.float64))
+    assert rel_fro(out.float().cpu().numpy(), o_ref) < 5e-3  # bf16 output + bf16 atomics only
+
+
+LAYER_CASES = [
+    # T, H, I, E, K, softmax_over_topk, norm, concat
+    (256, 512, 256, 8, 2, True, False, False),  # config 1 shape
+    (512, 512, 256, 16, 4, False, True, True),  # Qwen3-style routing + concat layout (small)
+    (384, 1024, 384, 32, 8, True, False, False),
+    (1, 256, 128, 8, 2, True, False, False),
+    (64, 512, 256, 64, 8, False, False, False),  # many empty experts
+]
+
+
+@pytest.mark.parametrize("T,H,I,E,K,sot,norm,concat", LAYER_CASES)
+def test_layer_forward_vs_fp8_oracle(sm, T, H, I, E, K, sot, norm, concat):
+    sonicmoe, ops = sm
+    from sonicmoe.functional import moe_TC_softmax_topk_layer
+
+    x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=7 * T + E)
+    xc, rwc, w1c, w2c = x.cuda(), rw.cuda(), w1.cuda(), w2.cuda()
+    o, logits, freq = moe_TC_softmax_topk_layer(
+        xc, rwc, w1c.permute(1, 2, 0), None, w2c.permute(1, 2, 0), None, K, None,
+        is_inference_mode_enabled=True, is_softmax_over_topk=sot, norm_topk_probs=norm, concat_layout=concat,
+    )
+    torch.cuda.synchronize()
+    lg = logits.float().cpu().numpy()
+    o_ref, scores, idx = olayer.fp8_oracle(x.float().numpy(), lg, w1.float().numpy(), w2.float().numpy(), K, sot,
+                                           norm, concat)
+    np.testing.assert_array_equal(freq.cpu().numpy(), np.bincount(idx.reshape(-1), minlength=E))
+    err8 = rel_fro(o.float().cpu().numpy(), o_ref.numpy())
+    assert err8 <= TOL_FP8, f"rel Frobenius vs fp8 oracle {err8:.4g}"
+    o_dense = olayer.expert_loop(x.float(), w1.float(), w2.float(), scores, idx, concat)
+    err_dense = rel_fro(o.float().cpu().numpy(), o_dense.numpy())
+    assert err_dense < 0.15  # e4m3 floor ~0.06 for these distributions; reported by bench
+
+
+def test_layer_empty_batch(sm):
+    _, ops = sm
+    from sonicmoe.functional import moe_TC_softmax_topk_layer
+
+    _, rw, w1, w2 = make_layer_inputs(1, 256, 128, 4)
+    x = torch.zeros(0, 256, dtype=torch.bfloat16, device="cuda")
+    o, logits, freq = moe_TC_softmax_topk_layer(
+        x, rw.cuda(), w1.cuda().permute(1, 2, 0), None, w2.cuda().permute(1, 2, 0), None, 2, None
+    )
+    assert o.shape == (0, 256) and int(freq.sum().item()) == 0
+
+
+def test_moe_module_forward(sm):
+    sonicmoe, _ = sm
+    torch.manual_seed(0)
+    T, H, I, E, K = 128, 512, 256, 8, 2
+    m = sonicmoe.MoE(E, K, H, I, sonicmoe.ActivationType.SWIGLU, False, 0.02).to(torch.bfloat16).cuda()
+    x = torch.randn(2, T // 2, H, dtype=torch.bfloat16, device="cuda")
+    o, aux = m(x, is_inference_mode=True)
+    assert o.shape == x.shape and aux is None
+    o2, aux2 = m(x)
+    assert aux2 is not None and torch.isfinite(aux2)
+    x2 = x.view(-1, H)
+    lg = torch.nn.functional.linear(x2, m.router.weight).float().cpu().numpy()  # same cuBLAS call as inside
+    o_ref, _, _ = olayer.fp8_oracle(x2.float().cpu().numpy(), lg, m.c_fc.weight.float().cpu().numpy(),
+                                    m.c_proj.weight.float().cpu().numpy(), K)
+    assert rel_fro(o.view(-1, H).float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
+    with pytest.raises(NotImplementedError):
+        m(x, kernel_backend_moe=sonicmoe.KernelBackendMoE.torch)
