@@ -206,6 +206,28 @@ def run_ours(args, rank, world, local_rank):
     return res
 
 
+def run_profile(args, local_rank):
+    """Eager forwards only, with the bf16 expert weights freed after preparation (smaller footprint)."""
+    import torch
+    import torch.nn.functional as F
+
+    from sonicmoe import ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
+    x, rw, w1, w2, w1p, w2p = build_workload(dev, T, H, I, E, K)
+    del w1, w2
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    freq = torch.empty(E, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    for _ in range(args.warmup + args.steps):
+        logits = F.linear(x, rw)
+        ops.moe_forward(x, logits, w1p, w2p, K, out=out, expert_frequency=freq, err=err)
+    torch.cuda.synchronize()
+    assert err.item() == 0, f"kernel error word {err.item()}"
+
+
 def time_gemm_stages(x, rw, w1p, w2p, K, reps):
     import torch
     import torch.nn.functional as F
@@ -315,7 +337,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=CFG["T"], help="tokens per GPU (profiling of smaller cases)")
+    ap.add_argument("--profile", action="store_true",
+                    help="only run warmup + steps eager forwards (no graph, baselines or extra timing), "
+                         "for ncu captures; prints nothing")
     args = ap.parse_args()
+    CFG["T"] = args.tokens
     if args.warmup < 3:
         args.warmup = 3
 
@@ -345,6 +372,10 @@ def main():
     import datetime
 
     import torch
+
+    if args.profile:
+        run_profile(args, local_rank)
+        return
 
     if world > 1:
         import torch.distributed as dist

@@ -162,9 +162,11 @@ def test_moe_module_forward(sm):
     o2, aux2 = m(x)
     assert aux2 is not None and torch.isfinite(aux2)
     x2 = x.view(-1, H)
-    lg = torch.nn.functional.linear(x2, m.router.weight).float().cpu().numpy()  # same cuBLAS call as inside
-    o_ref, _, _ = olayer.fp8_oracle(x2.float().cpu().numpy(), lg, m.c_fc.weight.float().cpu().numpy(),
-                                    m.c_proj.weight.float().cpu().numpy(), K)
+    with torch.no_grad():
+        lg = torch.nn.functional.linear(x2, m.router.weight).float().cpu().numpy()  # same cuBLAS call as inside
+        w1 = m.c_fc.weight.float().cpu().numpy()
+        w2 = m.c_proj.weight.float().cpu().numpy()
+    o_ref, _, _ = olayer.fp8_oracle(x2.float().cpu().numpy(), lg, w1, w2, K)
     assert rel_fro(o.view(-1, H).float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
     with pytest.raises(NotImplementedError):
         m(x, kernel_backend_moe=sonicmoe.KernelBackendMoE.torch)
