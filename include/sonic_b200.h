@@ -92,6 +92,22 @@ int sm_general_route_metadata(const int32_t* sorted_token_idx, const int32_t* ex
                               size_t workspace_bytes, int32_t* err, void* stream);
 
 /*
+ * sm_route_metadata without a workspace argument.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory when they route -- a host that records the step
+ * into a CUDA graph (cudaMalloc is not allowed during stream capture) or a runtime that reserved
+ * all device memory up front and has no allocator to hand out scratch.  The scratch (per-tile
+ * counts and the padded layout) lives in a 1 MiB static device array that each GPU loading the
+ * library keeps until the process exits; shapes needing more (E * ceil(T/128) + T*K/128 + 2E
+ * int32 entries, roughly) return SM_EINVAL.  Same outputs as sm_route_metadata.  The first call
+ * on a device looks up the array's address and should come before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race, so the caller serialises them.
+ * Allocates nothing (no cudaMalloc / cudaFree).
+ */
+int sm_route_metadata_noalloc(const int32_t* topk_indices, int T, int K, int E, int32_t* expert_frequency,
+                              int32_t* expert_frequency_offset, int32_t* x_gather_idx, int32_t* s_scatter_idx,
+                              int32_t* s_reverse_scatter_idx, int32_t* err, void* stream);
+
+/*
  * 1x128 activation quantiser in token order (no reference counterpart; the reference has no FP8
  * path -- this is the spec entry point the pack kernel shares).
  *   x [R, C] bf16 (C % 128 == 0) -> q [R, C] e4m3, sf atoms [ceil(R/128)][ceil(C/512)][512].

@@ -10,10 +10,10 @@
 using namespace smb;
 
 namespace {
-
 thread_local std::string g_last_error;
+}  // namespace
 
-int fail(int code, const char* fmt, ...) {
+int smb::set_last_error(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;
   va_start(ap, fmt);
@@ -21,6 +21,13 @@ int fail(int code, const char* fmt, ...) {
   va_end(ap);
   g_last_error = buf;
   return code;
+}
+
+namespace {
+
+template <typename... A>
+int fail(int code, const char* fmt, A... args) {
+  return set_last_error(code, fmt, args...);
 }
 
 int cuda_status(cudaError_t e, const char* what) {

@@ -15,6 +15,9 @@ constexpr int kSfAtomBytes = 512; // 128 rows x 4 K-blocks of UE8M0 scale factor
 
 enum Dtype : int { kDtypeBF16 = 0, kDtypeF16 = 1, kDtypeF32 = 2 };
 
+// Records the calling thread's message for sm_last_error() and returns `code`.
+int set_last_error(int code, const char* fmt, ...);
+
 inline int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
 // Upper bound on the number of 128-row blocks of the padded expert layout.

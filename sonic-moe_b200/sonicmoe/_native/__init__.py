@@ -37,6 +37,7 @@ SIGNATURES = {
     "sm_route_metadata_workspace": (_SZ, [_I, _I, _I]),
     "sm_route_metadata": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "sm_general_route_metadata": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
+    "sm_route_metadata_noalloc": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "sm_quant_1x128": (_I, [_P, _I, _I, _P, _P, _P]),
     "sm_weight_sf_bytes": (_SZ, [_I, _I, _I]),
     "sm_weight_prep": (_I, [_P, _I, _I, _I, _I, _P, _P, _P]),
