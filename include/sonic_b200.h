@@ -150,6 +150,25 @@ int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I
                    int32_t* expert_frequency, float* topk_scores, int32_t* topk_indices, void* workspace,
                    size_t workspace_bytes, int32_t* err, void* stream);
 
+/* Bytes of workspace sm_moe_general_forward needs for T tokens and TK routed (token, expert) entries. */
+size_t sm_moe_general_workspace_bytes(int T, int TK, int H, int I, int E);
+
+/*
+ * FP8 MoE-layer forward from explicit routing lists.  Replaces the forward of
+ * `moe_general_routing_inputs` (reference sonicmoe/functional/__init__.py:571-652: general routing
+ * metadata, _UpProjection / _DownProjection with variable experts per token, varlen-K
+ * aggregation of reduction_over_k_gather.py:77-83).
+ *   x [T, H] bf16; router_scores [TK] float32, token_indices [TK] int32 sorted ascending,
+ *   expert_indices [TK] int32 (entry f routes token token_indices[f] to expert expert_indices[f]
+ *   with weight router_scores[f]); w1/w2 as for sm_moe_forward ->
+ *   out [T, H] bf16 (tokens without entries get zeros), expert_frequency [E] int32.
+ */
+int sm_moe_general_forward(const void* x, int T, int H, int I, int E, int TK, const float* router_scores,
+                           const int32_t* token_indices, const int32_t* expert_indices, int concat_layout,
+                           const uint8_t* w1q, const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf,
+                           void* out, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
+                           int32_t* err, void* stream);
+
 /*
  * Stage-level entry points of the forward (same pipeline as sm_moe_forward, exposed so each
  * stage can be checked on its own).  The padded expert layout: expert e owns rows
@@ -180,9 +199,10 @@ int sm_moe_up(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1q, const u
 
 /* Down projection with the top-k weighted combine fused (reference _DownProjection.forward and
  * _router_forward, sonicmoe/functional/__init__.py:365-420, forward.py:64-85).  Adds
- * score * y into out [T, H] bf16, which the caller zero-fills first. */
+ * score * y into out [T, H] bf16, which the caller zero-fills first.  Tiles are visited one
+ * output-column slice at a time so that the slice being reduced into stays resident in L2. */
 int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2q, const uint8_t* w2_sf, int H,
-                        int I, int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+                        int I, int E, int T, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
                         const int32_t* off_pad, const int32_t* expert_frequency_offset,
                         const int32_t* expert_frequency, const int32_t* s_scatter_idx, const int32_t* x_gather_idx,
                         const float* topk_scores, void* out, int32_t* err, void* stream);

@@ -122,6 +122,38 @@ def fp8_oracle(x, logits, w1, w2, K: int, softmax_over_topk=True, norm_topk_prob
     return o, scores, idx
 
 
+def fp8_general_oracle(x, router_scores, token_idx, expert_idx, w1, w2, concat_layout=False):
+    """Fake-quantised FP8 layer for explicit routing lists (``moe_general_routing_inputs``,
+    reference functional/__init__.py:571-652): o[t] = sum over entries f with token t of
+    score[f] * W2q[e] requant(swiglu(W1q[e] xq[t])), e = expert_idx[f]."""
+    x = np.asarray(x, dtype=np.float32)
+    w1 = np.asarray(w1, dtype=np.float32)
+    w2 = np.asarray(w2, dtype=np.float32)
+    xq, xs = quant.quant_1x128(x)
+    xt = torch.as_tensor(quant.dequant_1x128(xq, xs)).double()
+    w1q, w1s = quant.quant_128x128(w1)
+    w1t = torch.as_tensor(quant.dequant_128x128(w1q, w1s)).double()
+    w2q, w2s = quant.quant_128x128(w2)
+    w2t = torch.as_tensor(quant.dequant_128x128(w2q, w2s)).double()
+    T, H = x.shape
+    E, N2, _ = w1.shape
+    I = N2 // 2
+    tok = torch.as_tensor(np.asarray(token_idx)).long()
+    exp_ = torch.as_tensor(np.asarray(expert_idx)).long()
+    sc = torch.as_tensor(np.asarray(router_scores, dtype=np.float32)).double()
+    o = torch.zeros((T, H), dtype=torch.float64)
+    for e in range(E):
+        sel = torch.nonzero(exp_ == e, as_tuple=True)[0]
+        if sel.numel() == 0:
+            continue
+        h = xt[tok[sel]] @ w1t[e].T
+        a = F.silu(h[:, :I]) * h[:, I:] if concat_layout else swiglu_interleaved(h)
+        aq, as_ = quant.quant_1x128(a.float().numpy())
+        ad = torch.as_tensor(quant.dequant_1x128(aq, as_)).double()
+        o.index_add_(0, tok[sel], (ad @ w2t[e].T) * sc[sel, None])
+    return o
+
+
 def rel_fro(a, b) -> float:
     """||a - b||_F / ||b||_F in float64."""
     a = torch.as_tensor(np.asarray(a, dtype=np.float64)) if not torch.is_tensor(a) else a.double()

@@ -115,6 +115,37 @@ FwdWs carve_fwd(Carve& c, int T, int H, int I, int E, int K) {
   return w;
 }
 
+struct GenWs {
+  RouteWs route;
+  int32_t* off;
+  int32_t* s_scatter;
+  int32_t* s_rev;
+  int32_t* x_gather;
+  int32_t* tok_off;
+  uint8_t* xq;
+  uint8_t* xsf;
+  uint8_t* aq;
+  uint8_t* asf;
+  int32_t* err;
+};
+
+GenWs carve_general(Carve& c, int T, long long TK, int H, int I, int E) {
+  GenWs w;
+  const int mb = max_padded_blocks(TK, E);
+  w.route = carve_route(c, 0, TK, E);
+  w.off = c.take<int32_t>(E + 1);
+  w.s_scatter = c.take<int32_t>(TK);
+  w.s_rev = c.take<int32_t>(TK);
+  w.x_gather = c.take<int32_t>(TK);
+  w.tok_off = c.take<int32_t>(static_cast<size_t>(T) + 1);
+  w.xq = c.take<uint8_t>(static_cast<size_t>(mb) * kBlockM * H);
+  w.xsf = c.take<uint8_t>(static_cast<size_t>(mb) * ceil_div(H, 512) * kSfAtomBytes);
+  w.aq = c.take<uint8_t>(static_cast<size_t>(mb) * kBlockM * I);
+  w.asf = c.take<uint8_t>(static_cast<size_t>(mb) * ceil_div(I, 512) * kSfAtomBytes);
+  w.err = c.take<int32_t>(1);
+  return w;
+}
+
 int check_router_args(int T, int E, int K, int sot, int norm) {
   if (T < 0) return fail(SM_EINVAL, "T must be >= 0 (got %d)", T);
   if (E < 1 || E > 4096) return fail(SM_EINVAL, "E must be in [1, 4096] (got %d)", E);
@@ -204,7 +235,7 @@ int sm_quant_1x128(const void* x, int R, int C, uint8_t* q, uint8_t* sf_atoms, v
   if (R < 0 || C <= 0 || C % 128) return fail(SM_EINVAL, "need R >= 0 and C %% 128 == 0 (R=%d C=%d)", R, C);
   if (R > 0 && (!x || !q || !sf_atoms)) return fail(SM_EINVAL, "null pointer");
   if (!aligned16(x) || !aligned16(q) || !aligned16(sf_atoms)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
-  return cuda_status(launch_quant_pack(x, R, C, nullptr, 1, nullptr, nullptr, nullptr, q, sf_atoms,
+  return cuda_status(launch_quant_pack(x, R, C, nullptr, 1, nullptr, nullptr, nullptr, nullptr, q, sf_atoms,
                                        static_cast<cudaStream_t>(stream)),
                      "quant_1x128");
 }
@@ -266,7 +297,7 @@ static GemmArgs up_args(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1
 }
 
 static GemmArgs down_args(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2q, const uint8_t* w2_sf, int H,
-                          int I, int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+                          int I, int E, int T, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
                           const int32_t* off_pad, const int32_t* off, const int32_t* freq, const int32_t* s_scatter,
                           const int32_t* x_gather, const float* scores, void* out, int32_t* err) {
   GemmArgs g{};
@@ -289,6 +320,7 @@ static GemmArgs down_args(const uint8_t* aq, const uint8_t* asf, const uint8_t* 
   g.out_bf16 = out;
   g.err = err;
   g.num_sms = num_sms();
+  g.tokens = T;
   return g;
 }
 
@@ -311,7 +343,7 @@ int sm_quant_pack(const void* x, int T, int H, const int32_t* topk_indices, int 
                   void* stream) {
   if (T < 0 || H <= 0 || H % 128 || K < 1 || K > 32) return fail(SM_EINVAL, "bad shape T=%d H=%d K=%d", T, H, K);
   if (!aligned16(x) || !aligned16(xq) || !aligned16(xsf)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
-  return cuda_status(launch_quant_pack(x, T, H, topk_indices, K, s_reverse_scatter_idx, expert_frequency_offset,
+  return cuda_status(launch_quant_pack(x, T, H, topk_indices, K, nullptr, s_reverse_scatter_idx, expert_frequency_offset,
                                        off_pad, xq, xsf, static_cast<cudaStream_t>(stream)),
                      "quant_pack");
 }
@@ -329,14 +361,14 @@ int sm_moe_up(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1q, const u
 }
 
 int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2q, const uint8_t* w2_sf, int H, int I,
-                        int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+                        int E, int T, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
                         const int32_t* off_pad, const int32_t* expert_frequency_offset,
                         const int32_t* expert_frequency, const int32_t* s_scatter_idx, const int32_t* x_gather_idx,
                         const float* topk_scores, void* out, int32_t* err, void* stream) {
-  if (H <= 0 || H % 256 || I <= 0 || I % 128 || E < 1 || max_blocks < 0)
-    return fail(SM_ENOTSUP, "bad shape H=%d I=%d E=%d (H %% 256 == 0, I %% 128 == 0)", H, I, E);
+  if (H <= 0 || H % 256 || I <= 0 || I % 128 || E < 1 || T < 0 || max_blocks < 0)
+    return fail(SM_ENOTSUP, "bad shape H=%d I=%d E=%d T=%d (H %% 256 == 0, I %% 128 == 0)", H, I, E, T);
   if (!err) return fail(SM_EINVAL, "err word required");
-  GemmArgs g = down_args(aq, asf, w2q, w2_sf, H, I, E, max_blocks, blk_expert, n_blocks, off_pad,
+  GemmArgs g = down_args(aq, asf, w2q, w2_sf, H, I, E, T, max_blocks, blk_expert, n_blocks, off_pad,
                          expert_frequency_offset, expert_frequency, s_scatter_idx, x_gather_idx, topk_scores, out, err);
   return cuda_status(launch_moe_down(g, static_cast<cudaStream_t>(stream)), "moe_down_combine");
 }
@@ -381,7 +413,8 @@ int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I
   if (e == cudaSuccess)
     e = launch_route_scatter(idx, nullptr, static_cast<int>(TK), K, kTileTokens * K, E, n_tiles, w.route.tile_counts,
                              w.off, w.s_scatter, w.s_rev, w.x_gather, st);
-  if (e == cudaSuccess) e = launch_quant_pack(x, T, H, idx, K, w.s_rev, w.off, w.route.off_pad, w.xq, w.xsf, st);
+  if (e == cudaSuccess)
+    e = launch_quant_pack(x, T, H, idx, K, nullptr, w.s_rev, w.off, w.route.off_pad, w.xq, w.xsf, st);
   if (e == cudaSuccess) e = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * H * 2, st);
   if (e == cudaSuccess) {
     GemmArgs g = up_args(w.xq, w.xsf, w1q, w1_sf, H, I, E, concat_layout, mb, w.route.blk_expert, w.route.n_blocks,
@@ -389,11 +422,70 @@ int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I
     e = launch_moe_up(g, st);
   }
   if (e == cudaSuccess) {
-    GemmArgs g = down_args(w.aq, w.asf, w2q, w2_sf, H, I, E, mb, w.route.blk_expert, w.route.n_blocks,
+    GemmArgs g = down_args(w.aq, w.asf, w2q, w2_sf, H, I, E, T, mb, w.route.blk_expert, w.route.n_blocks,
                            w.route.off_pad, w.off, expert_frequency, w.s_scatter, w.x_gather, scores, out, errw);
     e = launch_moe_down(g, st);
   }
   return cuda_status(e, "moe_forward");
+}
+
+size_t sm_moe_general_workspace_bytes(int T, int TK, int H, int I, int E) {
+  Carve c{nullptr, 0};
+  carve_general(c, T, TK, H, I, E);
+  return c.used + 256;
+}
+
+int sm_moe_general_forward(const void* x, int T, int H, int I, int E, int TK, const float* router_scores,
+                           const int32_t* token_indices, const int32_t* expert_indices, int concat_layout,
+                           const uint8_t* w1q, const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf,
+                           void* out, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
+                           int32_t* err, void* stream) {
+  int rc = check_layer_args(T, H, I, E, 1);
+  if (rc) return rc;
+  if (TK < 0) return fail(SM_EINVAL, "TK must be >= 0");
+  if (!expert_frequency) return fail(SM_EINVAL, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0 || TK == 0) {
+    cudaError_t e0 = cudaMemsetAsync(expert_frequency, 0, sizeof(int32_t) * E, st);
+    if (e0 == cudaSuccess && T > 0) e0 = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * H * 2, st);
+    return cuda_status(e0, "moe_general_forward");
+  }
+  if (!x || !router_scores || !token_indices || !expert_indices || !w1q || !w1_sf || !w2q || !w2_sf || !out)
+    return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(x) || !aligned16(out) || !aligned16(w1q) || !aligned16(w2q) || !aligned16(w1_sf) ||
+      !aligned16(w2_sf) || !aligned16(workspace))
+    return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  GenWs w = carve_general(c, T, TK, H, I, E);
+  if (!c.ok) return fail(SM_EINVAL, "workspace too small (%zu < %zu)", workspace_bytes, c.used);
+  int32_t* errw = err ? err : w.err;
+  const int n_tiles = route_tiles_general(TK);
+  const int mb = max_padded_blocks(TK, E);
+  cudaError_t e = cudaSuccess;
+  if (!err) e = cudaMemsetAsync(w.err, 0, sizeof(int32_t), st);
+  if (e == cudaSuccess) e = launch_route_hist(expert_indices, TK, 1024, E, n_tiles, w.route.tile_counts, errw, st);
+  if (e == cudaSuccess)
+    e = launch_route_scan(w.route.tile_counts, n_tiles, E, TK, expert_frequency, w.off, w.route.off_pad,
+                          w.route.blk_expert, w.route.n_blocks, st);
+  if (e == cudaSuccess)
+    e = launch_route_scatter(expert_indices, token_indices, TK, 1, 1024, E, n_tiles, w.route.tile_counts, w.off,
+                             w.s_scatter, w.s_rev, w.x_gather, st);
+  if (e == cudaSuccess) e = launch_token_offset(token_indices, T, TK, w.tok_off, st);
+  if (e == cudaSuccess)
+    e = launch_quant_pack(x, T, H, expert_indices, 0, w.tok_off, w.s_rev, w.off, w.route.off_pad, w.xq, w.xsf, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * H * 2, st);
+  if (e == cudaSuccess) {
+    GemmArgs g = up_args(w.xq, w.xsf, w1q, w1_sf, H, I, E, concat_layout, mb, w.route.blk_expert, w.route.n_blocks,
+                         w.route.off_pad, expert_frequency, w.aq, w.asf, errw);
+    e = launch_moe_up(g, st);
+  }
+  if (e == cudaSuccess) {
+    GemmArgs g = down_args(w.aq, w.asf, w2q, w2_sf, H, I, E, T, mb, w.route.blk_expert, w.route.n_blocks,
+                           w.route.off_pad, w.off, expert_frequency, w.s_scatter, w.x_gather, router_scores, out,
+                           errw);
+    e = launch_moe_down(g, st);
+  }
+  return cuda_status(e, "moe_general_forward");
 }
 
 }  // extern "C"

@@ -127,6 +127,25 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// Bulk (TMA) reduction of `bytes` contiguous bf16 values from shared memory into global memory,
+// tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void bulk_reduce_add_bf16(void* gdst, const void* ssrc, uint32_t bytes, uint64_t policy) {
+  asm volatile(
+      "cp.reduce.async.bulk.global.shared::cta.bulk_group.L2::cache_hint.add.noftz.bf16 [%0], [%1], %2, %3;" ::"l"(
+          gdst),
+      "r"(smem_u32(ssrc)), "r"(bytes), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every bulk operation committed by this thread has finished reading its shared-memory source
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every bulk operation committed by this thread has completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// make this thread's generic-proxy shared-memory writes visible to the async (TMA) proxy
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // --------------------------------------------------------------------------------------------
 // tcgen05: tensor memory, block-scaled MMA, copies
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {

@@ -22,13 +22,14 @@
 // read from device memory, so empty experts cost nothing and no host synchronisation is needed.
 // Every mbarrier wait is bounded (2 s); on a timeout the kernel records an error code, drains its
 // outstanding copies and MMAs with short bounded waits, frees tensor memory and returns.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "sonic_internal.h"
 
 namespace smb {
 
 constexpr int kBN = 256;
-constexpr int kStages = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kGemmThreads = (4 + kEpiWarps) * 32;
 constexpr int kABytes = kBlockM * kBlockK;  // 16 KB
@@ -37,54 +38,73 @@ constexpr int kSfaBytes = kSfAtomBytes;
 constexpr int kSfbBytes = 2 * kSfAtomBytes;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemAcc = 0, kTmemSfa = 256, kTmemSfb = 260;
+constexpr int kNumBars = 2 * 4 + 4;  // full/empty per stage (at most 4 stages) + 4
+constexpr int kRowChunkBytes = 128;  // down epilogue: one thread's 64 bf16 of one output row
 
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kStages * kABytes;
-constexpr int kOffSfa = kOffB + kStages * kBBytes;
-constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
-constexpr int kOffBar = kOffSfb + kStages * kSfbBytes;
-constexpr int kNumBars = 2 * kStages + 4;
-constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
-constexpr int kOffAmax = (kOffTmemHolder + 4 + 15) / 16 * 16;
-constexpr int kAmaxFloats = 2 * 4 * kBlockM;
-constexpr int kSmemBytes = kOffAmax + kAmaxFloats * 4;
-constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack for 1024-byte alignment of the base
-static_assert(kSmemAlloc <= 232448, "shared memory budget");
+// Shared-memory layout per epilogue kind.  The up projection keeps a 4-stage ring; the down
+// projection gives one stage up for 64 KB of per-thread staging from which its output rows are
+// reduced into global memory by TMA bulk reductions.
+template <bool kUp>
+struct GemmSmem {
+  static constexpr int kStages = kUp ? 4 : 3;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + kStages * kABytes;
+  static constexpr int kOffSfa = kOffB + kStages * kBBytes;
+  static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
+  static constexpr int kOffStage = kOffSfb + kStages * kSfbBytes;
+  static constexpr int kStageBytes = kUp ? 0 : kEpiWarps * 32 * kRowChunkBytes;
+  static constexpr int kOffBar = kOffStage + kStageBytes;
+  static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
+  static constexpr int kOffAmax = (kOffTmemHolder + 4 + 15) / 16 * 16;
+  static constexpr int kAmaxFloats = kUp ? 2 * 4 * kBlockM : 0;
+  static constexpr int kBytes = kOffAmax + kAmaxFloats * 4;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
+  static_assert(kAlloc <= 232448, "shared memory budget");
+  static_assert(kOffStage % 128 == 0, "staging alignment");
+};
 
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-__device__ __forceinline__ void red_add_bf16x8(void* addr, float a0, float a1, float a2, float a3, float a4,
-                                               float a5, float a6, float a7) {
-  __nv_bfloat162 p0 = __floats2bfloat162_rn(a0, a1);
-  __nv_bfloat162 p1 = __floats2bfloat162_rn(a2, a3);
-  __nv_bfloat162 p2 = __floats2bfloat162_rn(a4, a5);
-  __nv_bfloat162 p3 = __floats2bfloat162_rn(a6, a7);
-  asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(addr),
-               "r"(*reinterpret_cast<uint32_t*>(&p0)), "r"(*reinterpret_cast<uint32_t*>(&p1)),
-               "r"(*reinterpret_cast<uint32_t*>(&p2)), "r"(*reinterpret_cast<uint32_t*>(&p3))
-               : "memory");
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+// Tile -> (m-block, n-tile).  The n-tiles are split into `n_slices` column slices; all tiles of
+// one slice come before the next slice, n fastest inside a slice.  With one slice this is plain
+// m-major order.  The down projection uses several slices so that the slice of the bf16 output
+// its reductions land in stays resident in L2 while the slice is being computed.
+__device__ __forceinline__ void tile_coords(int tile, int n_blocks, int ntn, int n_slices, int& mb, int& nt) {
+  const int nts = ntn / n_slices;
+  const int per_slice = n_blocks * nts;
+  const int slice = tile / per_slice;
+  const int r = tile - slice * per_slice;
+  mb = r / nts;
+  nt = slice * nts + (r - mb * nts);
 }
 
 template <bool kUp>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const GemmArgs g) {
+  using L = GemmSmem<kUp>;
+  constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint8_t* sA = smem + kOffA;
-  uint8_t* sB = smem + kOffB;
-  uint8_t* sSfa = smem + kOffSfa;
-  uint8_t* sSfb = smem + kOffSfb;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint8_t* sA = smem + L::kOffA;
+  uint8_t* sB = smem + L::kOffB;
+  uint8_t* sSfa = smem + L::kOffSfa;
+  uint8_t* sSfb = smem + L::kOffSfb;
+  uint8_t* sStage = smem + L::kOffStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + kStages;
   uint64_t* tmem_full = bars + 2 * kStages;
   uint64_t* tmem_empty = tmem_full + 1;
   uint64_t* drain = tmem_full + 2;
   uint64_t* amax_bar = tmem_full + 3;  // all epilogue threads: row amax partials written
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffTmemHolder);
-  float* s_amax = reinterpret_cast<float*>(smem + kOffAmax);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kOffTmemHolder);
+  float* s_amax = reinterpret_cast<float*>(smem + L::kOffAmax);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -126,7 +146,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const int mb = tile / ntn, nt = tile - (tile / ntn) * ntn;
+        int mb, nt;
+        tile_coords(tile, n_blocks, ntn, g.n_slices, mb, nt);
         const int e = g.blk_expert[mb];
         const int a_row = mb * kBlockM;
         const int b_row = e * g.N + nt * kBN;
@@ -209,8 +230,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     int tcount = 0;
+    const uint64_t pol_out = policy_evict_last();
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tcount) {
-      const int mb = tile / ntn, nt = tile - (tile / ntn) * ntn;
+      int mb, nt;
+      tile_coords(tile, n_blocks, ntn, g.n_slices, mb, nt);
       const int e = g.blk_expert[mb];
       if (!mbar_wait(tmem_full, tcount & 1, g.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
@@ -264,23 +287,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               static_cast<uint8_t>(e8 + 127);
         }
       } else {
+        // Scale the row chunk, stage it in this thread's own 128 bytes of shared memory and let
+        // the TMA unit add it into the token's output row (one line-sized bulk reduction instead
+        // of eight 16-byte vector atomics).  The slot is reused only after the previous bulk
+        // reduction has finished reading it.
+        uint8_t* slot = sStage + (ew * 32 + lane) * kRowChunkBytes;
+        bulk_wait_read0();
         if (valid) {
           const int rs = rel + g.off[e];
           const int f = g.s_scatter[rs];
           const int tok = g.x_gather[rs];
           const float sc = g.scores[f];
-          __nv_bfloat16* dst =
-              static_cast<__nv_bfloat16*>(g.out_bf16) + static_cast<size_t>(tok) * g.N + nt * kBN + cc * 64;
 #pragma unroll
           for (int j = 0; j < 64; j += 8) {
-            red_add_bf16x8(dst + j, sc * __uint_as_float(v[j]), sc * __uint_as_float(v[j + 1]),
-                           sc * __uint_as_float(v[j + 2]), sc * __uint_as_float(v[j + 3]),
-                           sc * __uint_as_float(v[j + 4]), sc * __uint_as_float(v[j + 5]),
-                           sc * __uint_as_float(v[j + 6]), sc * __uint_as_float(v[j + 7]));
+            uint4 w;
+            w.x = pack_bf16x2(sc * __uint_as_float(v[j]), sc * __uint_as_float(v[j + 1]));
+            w.y = pack_bf16x2(sc * __uint_as_float(v[j + 2]), sc * __uint_as_float(v[j + 3]));
+            w.z = pack_bf16x2(sc * __uint_as_float(v[j + 4]), sc * __uint_as_float(v[j + 5]));
+            w.w = pack_bf16x2(sc * __uint_as_float(v[j + 6]), sc * __uint_as_float(v[j + 7]));
+            *reinterpret_cast<uint4*>(slot + 2 * j) = w;
           }
+          fence_proxy_async_smem();
+          __nv_bfloat16* dst =
+              static_cast<__nv_bfloat16*>(g.out_bf16) + static_cast<size_t>(tok) * g.N + nt * kBN + cc * 64;
+          bulk_reduce_add_bf16(dst, slot, kRowChunkBytes, pol_out);
+          bulk_commit();
         }
       }
     }
+    if constexpr (!kUp) bulk_wait_all();
   }
   __syncthreads();
   if (warp == 2) {
@@ -329,10 +364,24 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
   if (!make_tmap(&ta, g.a, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.Kd), kBlockM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tb, g.b, static_cast<uint64_t>(g.E) * g.N, static_cast<uint64_t>(g.Kd), kBN)) return cudaErrorInvalidValue;
   auto kern = moe_gemm_kernel<kUp>;
+  constexpr int kSmemAlloc = GemmSmem<kUp>::kAlloc;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
   if (e != cudaSuccess) return e;
   const int grid = static_cast<int>(max_tiles < g.num_sms ? max_tiles : g.num_sms);
-  kern<<<grid, kGemmThreads, kSmemAlloc, st>>>(ta, tb, g);
+  GemmArgs ga = g;
+  ga.n_slices = 1;
+  if (!kUp) {
+    // Largest column slice whose bf16 output slab (tokens x slice) fits the L2 budget.
+    const int ntn = g.N / kBN;
+    long long budget = 160ll << 20;
+    if (const char* env = getenv("SONIC_B200_DOWN_SLAB_MB")) budget = atoll(env) << 20;
+    int slices = 1;
+    while (slices < ntn && static_cast<long long>(g.tokens) * (g.N / slices) * 2 > budget &&
+           ntn % (slices * 2) == 0)
+      slices *= 2;
+    ga.n_slices = slices;
+  }
+  kern<<<grid, kGemmThreads, kSmemAlloc, st>>>(ta, tb, ga);
   return cudaGetLastError();
 }
 

@@ -26,74 +26,84 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& raw, float* v) {
 
 // One warp per token.  Lane l covers elements [h0 + 8l, h0 + 8l + 8) of each 256-wide chunk, so
 // lanes 0-15 and 16-31 each hold one 128-wide group.  The token's quantised row and scale bytes
-// are written to each of its K destination rows of the padded expert-major layout
-// (row = s_rev[f] - off[e] + off_pad[e] for entry f = t*K + k, e = experts[f]).  With
-// experts == nullptr the destination is row t itself (plain token-order quantisation, K = 1).
+// are written to each destination row of the padded expert-major layout that one of its routed
+// entries owns (row = s_rev[f] - off[e] + off_pad[e] for entry f, e = experts[f]).  The token's
+// entries are f in [t*K, t*K + K) for token-choice routing, or [tok_off[t], tok_off[t+1]) for
+// general routing (tok_off != nullptr); with experts == nullptr the destination is row t itself
+// (plain token-order quantisation).  Destinations are handled 32 at a time (one per lane).
 __global__ void __launch_bounds__(kQuantWarps * 32)
     quant_pack_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, const int32_t* __restrict__ experts, int K,
-                      const int32_t* __restrict__ s_rev, const int32_t* __restrict__ off,
-                      const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq, uint8_t* __restrict__ xsf) {
+                      const int32_t* __restrict__ tok_off, const int32_t* __restrict__ s_rev,
+                      const int32_t* __restrict__ off, const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq,
+                      uint8_t* __restrict__ xsf) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * kQuantWarps + warp;
   if (t >= T) return;
-  const int ncopy = experts ? K : 1;
-  int my_dst = 0;
-  if (!experts) {
-    my_dst = t;
-  } else if (lane < K) {
-    const int f = t * K + lane;
-    const int e = experts[f];
-    my_dst = s_rev[f] - off[e] + off_pad[e];
+  int f0 = t, ncopy = 1;
+  if (experts) {
+    f0 = tok_off ? tok_off[t] : t * K;
+    ncopy = tok_off ? tok_off[t + 1] - f0 : K;
   }
   const int KG = (H / kBlockK + 3) / 4;
   const __nv_bfloat16* src = x + static_cast<size_t>(t) * H;
-  uint32_t sfword = 0;
-  for (int hb = 0; hb < H; hb += 256 * kQuantBatch) {
-    uint4 raw[kQuantBatch];
-#pragma unroll
-    for (int c = 0; c < kQuantBatch; ++c) {
-      const int h = hb + 256 * c + 8 * lane;
-      raw[c] = (h < H) ? *reinterpret_cast<const uint4*>(src + h) : make_uint4(0, 0, 0, 0);
+  for (int c0 = 0; c0 < ncopy; c0 += 32) {
+    const int nc = min(32, ncopy - c0);
+    int my_dst = 0;
+    if (!experts) {
+      my_dst = t;
+    } else if (lane < nc) {
+      const int f = f0 + c0 + lane;
+      const int e = experts[f];
+      my_dst = s_rev[f] - off[e] + off_pad[e];
     }
+    uint32_t sfword = 0;
+    for (int hb = 0; hb < H; hb += 256 * kQuantBatch) {
+      uint4 raw[kQuantBatch];
 #pragma unroll
-    for (int c = 0; c < kQuantBatch; ++c) {
-      const int h0 = hb + 256 * c;
-      if (h0 >= H) break;
-      const int h = h0 + 8 * lane;
-      float v[8];
-      bf16x8_to_f32(raw[c], v);
-      float am = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-      const int e8 = scale_exp_of_amax(am);
-      const float inv = exp2_neg(e8);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int i = 0; i < 4; i += 2) {
-        lo |= static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[i], inv), __fmul_rn(v[i + 1], inv))) << (8 * i);
-        hi |= static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[4 + i], inv), __fmul_rn(v[5 + i], inv))) << (8 * i);
+      for (int c = 0; c < kQuantBatch; ++c) {
+        const int h = hb + 256 * c + 8 * lane;
+        raw[c] = (h < H) ? *reinterpret_cast<const uint4*>(src + h) : make_uint4(0, 0, 0, 0);
       }
-      const uint2 packed = make_uint2(lo, hi);
-      for (int k = 0; k < ncopy; ++k) {
-        const int p = __shfl_sync(0xffffffffu, my_dst, k);
-        if (h < H) *reinterpret_cast<uint2*>(xq + static_cast<size_t>(p) * H + h) = packed;
-      }
-      const int gA = h0 / kBlockK;
-      const int eA = __shfl_sync(0xffffffffu, e8, 0);
-      const int eB = __shfl_sync(0xffffffffu, e8, 16);
-      sfword |= static_cast<uint32_t>(eA + 127) << (8 * (gA % 4));
-      if (h0 + 128 < H) sfword |= static_cast<uint32_t>(eB + 127) << (8 * ((gA + 1) % 4));
-      if ((gA % 4) == 2 || h0 + 256 >= H) {
-        const int kg = gA / 4;
-        if (lane < ncopy) {
-          const int p = my_dst;
-          const size_t o = (static_cast<size_t>(p / kBlockM) * KG + kg) * kSfAtomBytes + 16 * (p % 32) +
-                           4 * ((p % kBlockM) / 32);
-          *reinterpret_cast<uint32_t*>(xsf + o) = sfword;
+#pragma unroll
+      for (int c = 0; c < kQuantBatch; ++c) {
+        const int h0 = hb + 256 * c;
+        if (h0 >= H) break;
+        const int h = h0 + 8 * lane;
+        float v[8];
+        bf16x8_to_f32(raw[c], v);
+        float am = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        const int e8 = scale_exp_of_amax(am);
+        const float inv = exp2_neg(e8);
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i += 2) {
+          lo |= static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[i], inv), __fmul_rn(v[i + 1], inv))) << (8 * i);
+          hi |= static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[4 + i], inv), __fmul_rn(v[5 + i], inv))) << (8 * i);
         }
-        sfword = 0;
+        const uint2 packed = make_uint2(lo, hi);
+        for (int k = 0; k < nc; ++k) {
+          const int p = __shfl_sync(0xffffffffu, my_dst, k);
+          if (h < H) *reinterpret_cast<uint2*>(xq + static_cast<size_t>(p) * H + h) = packed;
+        }
+        const int gA = h0 / kBlockK;
+        const int eA = __shfl_sync(0xffffffffu, e8, 0);
+        const int eB = __shfl_sync(0xffffffffu, e8, 16);
+        sfword |= static_cast<uint32_t>(eA + 127) << (8 * (gA % 4));
+        if (h0 + 128 < H) sfword |= static_cast<uint32_t>(eB + 127) << (8 * ((gA + 1) % 4));
+        if ((gA % 4) == 2 || h0 + 256 >= H) {
+          const int kg = gA / 4;
+          if (lane < nc) {
+            const int p = my_dst;
+            const size_t o = (static_cast<size_t>(p / kBlockM) * KG + kg) * kSfAtomBytes + 16 * (p % 32) +
+                             4 * ((p % kBlockM) / 32);
+            *reinterpret_cast<uint32_t*>(xsf + o) = sfword;
+          }
+          sfword = 0;
+        }
       }
     }
   }
@@ -147,13 +157,13 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* s_rev,
-                              const int32_t* off, const int32_t* off_pad, uint8_t* xq, uint8_t* xsf,
-                              cudaStream_t st) {
+cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* tok_off,
+                              const int32_t* s_rev, const int32_t* off, const int32_t* off_pad, uint8_t* xq,
+                              uint8_t* xsf, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   const int grid = (T + kQuantWarps - 1) / kQuantWarps;
-  quant_pack_kernel<<<grid, kQuantWarps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, experts, K, s_rev,
-                                                       off, off_pad, xq, xsf);
+  quant_pack_kernel<<<grid, kQuantWarps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, experts, K,
+                                                       tok_off, s_rev, off, off_pad, xq, xsf);
   return cudaGetLastError();
 }
 

@@ -38,9 +38,9 @@ cudaError_t launch_route_scatter(const int32_t* experts, const int32_t* token_of
                                  cudaStream_t st);
 cudaError_t launch_token_offset(const int32_t* sorted_tokens, int T, int TK, int32_t* offset, cudaStream_t st);
 
-cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* s_rev,
-                              const int32_t* off, const int32_t* off_pad, uint8_t* xq, uint8_t* xsf,
-                              cudaStream_t st);
+cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* tok_off,
+                              const int32_t* s_rev, const int32_t* off, const int32_t* off_pad, uint8_t* xq,
+                              uint8_t* xsf, cudaStream_t st);
 cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_glu, uint8_t* wq, uint8_t* wsf,
                                cudaStream_t st);
 
@@ -70,6 +70,8 @@ struct GemmArgs {
   void* out_bf16;
   int* err;
   int num_sms;
+  int tokens;    // T (rows of the token-major output), for the down projection's slice choice
+  int n_slices;  // set by the launcher
 };
 
 cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st);

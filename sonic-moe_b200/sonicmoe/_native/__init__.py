@@ -46,13 +46,18 @@ SIGNATURES = {
         _I,
         [_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P],
     ),
+    "sm_moe_general_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "sm_moe_general_forward": (
+        _I,
+        [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P],
+    ),
     "sm_max_padded_blocks": (_I, [_LL, _I]),
     "sm_route_plan": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "sm_quant_pack": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_moe_down_combine": (
         _I,
-        [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+        [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     ),
 }
 

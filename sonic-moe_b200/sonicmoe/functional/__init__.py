@@ -134,10 +134,26 @@ def moe_general_routing_inputs(
 ):
     """MoE forward from explicit (token, expert, score) lists; token_indices must be sorted ascending.
 
-    Returns (o [T, H], expert_frequency [E]).
+    Returns (o [T, H], expert_frequency [E]).  ``E`` is taken from ``w2`` as in the reference
+    (``functional/__init__.py:592``).
     """
     _check_common(b1, b2, activation_type)
-    raise NotImplementedError("moe_general_routing_inputs is not implemented by the FP8 engine yet")
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    x = x.contiguous()
+    w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+    w2q = prepare_fp8_weights(w2, concat_glu=False)
+    if router_scores.dtype != torch.float32:
+        router_scores = router_scores.float()
+    o, expert_frequency = ops.moe_general_forward(
+        x,
+        router_scores.contiguous(),
+        token_indices.to(torch.int32).contiguous(),
+        expert_indices.to(torch.int32).contiguous(),
+        w1q,
+        w2q,
+    )
+    return o, expert_frequency
 
 
 def TC_topk_router_metadata_triton(

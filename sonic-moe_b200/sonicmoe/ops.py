@@ -227,7 +227,7 @@ def moe_down_combine(aq, asf, w2: Fp8ExpertWeights, plan: RoutePlan, scores: tor
     if out is None:
         out = torch.zeros(T, H, dtype=torch.bfloat16, device=aq.device)
     nat.call(
-        "sm_moe_down_combine", _ptr(aq), _ptr(asf), _ptr(w2.q), _ptr(w2.sf), H, I, E, plan.max_blocks,
+        "sm_moe_down_combine", _ptr(aq), _ptr(asf), _ptr(w2.q), _ptr(w2.sf), H, I, E, T, plan.max_blocks,
         _ptr(plan.blk_expert), _ptr(plan.n_blocks), _ptr(plan.off_pad), _ptr(plan.off), _ptr(plan.freq),
         _ptr(plan.s_scatter), _ptr(plan.x_gather), _ptr(scores), _ptr(out), _ptr(err), _stream(),
     )
@@ -280,5 +280,42 @@ def moe_forward(
         "sm_moe_forward", _ptr(x), _ptr(router_logits), T, H, I, E, K, int(softmax_over_topk), int(norm_topk_probs),
         int(w1.concat_glu), _ptr(w1.q), _ptr(w1.sf), _ptr(w2.q), _ptr(w2.sf), _ptr(out), _ptr(expert_frequency),
         _ptr(topk_scores), _ptr(topk_indices), _ptr(ws), ws.numel(), _ptr(err), _stream(),
+    )
+    return out, expert_frequency
+
+
+def moe_general_forward(
+    x: torch.Tensor,
+    router_scores: torch.Tensor,
+    token_indices: torch.Tensor,
+    expert_indices: torch.Tensor,
+    w1: Fp8ExpertWeights,
+    w2: Fp8ExpertWeights,
+    out: torch.Tensor = None,
+    expert_frequency: torch.Tensor = None,
+    err: torch.Tensor = None,
+):
+    """FP8 layer forward from explicit (token, expert, score) entries, token_indices sorted ascending."""
+    _need(x, "x", torch.bfloat16)
+    _need(router_scores, "router_scores", torch.float32)
+    _need(token_indices, "token_indices", torch.int32)
+    _need(expert_indices, "expert_indices", torch.int32)
+    T, H = x.shape
+    E, N2, H1 = w1.shape
+    E2, H2, I = w2.shape
+    TK = router_scores.numel()
+    if H1 != H or H2 != H or N2 != 2 * I or E2 != E or token_indices.numel() != TK or expert_indices.numel() != TK:
+        raise ValueError("shape mismatch between x, routing lists and weights")
+    dev = x.device
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    if expert_frequency is None:
+        expert_frequency = torch.empty(E, dtype=torch.int32, device=dev)
+    nbytes = nat.load().sm_moe_general_workspace_bytes(T, TK, H, I, E)
+    ws = _workspace(nbytes, dev)
+    nat.call(
+        "sm_moe_general_forward", _ptr(x), T, H, I, E, TK, _ptr(router_scores), _ptr(token_indices),
+        _ptr(expert_indices), int(w1.concat_glu), _ptr(w1.q), _ptr(w1.sf), _ptr(w2.q), _ptr(w2.sf), _ptr(out),
+        _ptr(expert_frequency), _ptr(ws), ws.numel(), _ptr(err), _stream(),
     )
     return out, expert_frequency

@@ -170,3 +170,39 @@ def test_moe_module_forward(sm):
     assert rel_fro(o.view(-1, H).float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
     with pytest.raises(NotImplementedError):
         m(x, kernel_backend_moe=sonicmoe.KernelBackendMoE.torch)
+
+
+def _general_inputs(T, E, avg_k, seed):
+    """Variable experts per token, token-sorted lists (as tests/metadata_test.py:82-100 builds them)."""
+    rs = np.random.RandomState(seed)
+    toks, exps, scs = [], [], []
+    for t in range(T):
+        k = rs.randint(0, min(2 * avg_k, E) + 1)  # 0 experts allowed: such tokens produce zeros
+        e = rs.permutation(E)[:k]
+        w = rs.rand(k).astype(np.float32)
+        toks += [t] * k
+        exps += list(e)
+        scs += list(w / max(w.sum(), 1e-6))
+    return (np.array(toks, dtype=np.int32), np.array(exps, dtype=np.int32), np.array(scs, dtype=np.float32))
+
+
+@pytest.mark.parametrize("T,H,I,E,avg_k,concat", [(256, 512, 256, 8, 2, False), (300, 512, 384, 16, 4, True),
+                                                  (64, 256, 128, 64, 20, False)])
+def test_general_routing_layer_vs_fp8_oracle(sm, T, H, I, E, avg_k, concat):
+    _, _ = sm
+    from sonicmoe.functional import moe_general_routing_inputs
+
+    x, _, w1, w2 = make_layer_inputs(T, H, I, E, seed=T + 3 * E)
+    tok, ex, sc = _general_inputs(T, E, avg_k, seed=T)
+    o, freq = moe_general_routing_inputs(
+        x.cuda(), torch.from_numpy(sc).cuda(), torch.from_numpy(tok).cuda(), torch.from_numpy(ex).cuda(),
+        w1.cuda().permute(1, 2, 0), None, w2.cuda().permute(1, 2, 0), None, E, None,
+        is_inference_mode_enabled=True, concat_layout=concat,
+    )
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(freq.cpu().numpy(), np.bincount(ex, minlength=E))
+    o_ref = olayer.fp8_general_oracle(x.float().numpy(), sc, tok, ex, w1.float().numpy(), w2.float().numpy(), concat)
+    err8 = rel_fro(o.float().cpu().numpy(), o_ref.numpy())
+    assert err8 <= TOL_FP8, f"rel Frobenius vs fp8 oracle {err8:.4g}"
+    counts = np.bincount(tok, minlength=T)
+    assert torch.all(o[torch.from_numpy(counts == 0).cuda()] == 0)
