@@ -14,8 +14,11 @@ Synthetic data: x ~ N(0,1) bf16, router/expert weights ~ N(0
 expert weights quantised to e4m3 with 128x128 UE8M0 scales before timing (weight preparation is
 not part of the forward).  FLOPs per forward: 6*T*K*H*I (benchmarks/moe-cute.py:281-284).
 
-N > 1 (torchrun): every rank runs the same single-GPU layer on its own GPU (replicas, weak
-scaling, no collective on the data path); the step time is the max over ranks.
+N > 1 (torchrun): expert parallel.  Each rank keeps T=32768 tokens (weak scaling) and E/N of the
+128 experts; one step = router GEMM, dispatch (top-k + e4m3 records per destination rank), NCCL
+all-to-all of counts and records, the local expert GEMMs, NCCL all-to-all of the bf16 partial rows
+back, and the fp32 combine (sonicmoe.ep).  The step time is the max over ranks.  The expert-parallel
+step reads the record counts on the host, so it is timed as eager launches, not a CUDA graph.
 
 --impl reference: the reference's eager CPU path (oracle.layer.reference_port, a line-by-line
 restatement of sonicmoe/moe.py:278-360 that reproduces it bit for bit) on the host cores, on a
@@ -117,6 +120,79 @@ class ClockSampler:
         reasons = sorted(n for n, bit in self.REASONS.items() if any(s[1] & bit for s in self.samples))
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
                 "samples": len(sm), "power_w_max": max((s[2] for s in self.samples), default=None)}
+
+
+def build_ep_workload(dev, rank, world, T, H, I, E, K):
+    """This rank's tokens and expert shard.  Router weights and each expert's weights are drawn from
+    per-tensor seeds, so every world size builds the same global model."""
+    import torch
+
+    from sonicmoe import ops
+
+    g = torch.Generator(device=dev).manual_seed(1111 + rank)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    g.manual_seed(7)
+    rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    El = E // world
+    w1 = torch.empty(El, 2 * I, H, dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty(El, H, I, dtype=torch.bfloat16, device=dev)
+    for j in range(El):
+        g.manual_seed(100003 * (rank * El + j) + 11)
+        w1[j] = (torch.randn(2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w2[j] = (torch.randn(H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    return x, rw, ops.weight_prep(w1), ops.weight_prep(w2)
+
+
+def run_ep(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from sonicmoe.ep import ExpertParallelMoE
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
+    x, rw, w1p, w2p = build_ep_workload(dev, rank, world, T, H, I, E, K)
+    moe = ExpertParallelMoE(rw, w1p, w2p, E, K)
+    for _ in range(args.warmup):
+        moe.forward(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            moe.forward(x)
+        ev1.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = t.item() / args.steps
+    # end to end through the public API with pinned host buffers
+    x_host = x.cpu().pin_memory()
+    o_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+    steps_e2e = max(3, min(args.steps, 10))
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps_e2e):
+        xd.copy_(x_host, non_blocking=True)
+        o, _, _ = moe.forward(xd)
+        o_host.copy_(o, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps_e2e], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {
+        "ms_step": ms_step,
+        "tokens_per_s": world * T / (ms_step / 1e3),
+        "tflops_per_gpu": flops_fwd(T, H, I, K) / (ms_step / 1e3) / 1e12,
+        "e2e": {"ms_step": t.item(), "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2},
+        "clocks": clk.summary(),
+    }
 
 
 def build_workload(dev, T, H, I, E, K, seed=1111):
@@ -392,14 +468,29 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    res = run_ours(args, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist
 
+        res = run_ep(args, rank, world, local_rank)
         dist.barrier()
         dist.destroy_process_group()
-    if rank != 0:
+        if rank != 0:
+            return
+        e2e = res["e2e"]
+        line = {
+            "metric": METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_step": res["ms_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
+            "config": dict(config, parallelism=f"ep{world}", experts_per_rank=E // world,
+                           timing="eager steps (host reads record counts), CUDA events, max over ranks"),
+            "tflops_per_gpu": res["tflops_per_gpu"], "gpu_launches": 14 * args.steps,
+            "e2e": {"value": world * T / (e2e["ms_step"] / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]},
+            "clocks": res["clocks"],
+        }
+        print(json.dumps(line))
         return
+    res = run_ours(args, rank, world, local_rank)
 
     peaks, peak_src = measured_peaks()
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))

@@ -207,6 +207,36 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
                         const int32_t* expert_frequency, const int32_t* s_scatter_idx, const int32_t* x_gather_idx,
                         const float* topk_scores, void* out, int32_t* err, void* stream);
 
+/*
+ * Expert parallelism (no counterpart in the reference, which is single-GPU: its blog lists EP as
+ * future work).  E experts are sharded over W ranks, El = E / W contiguous experts per rank.  The
+ * host exchanges the buffers these stages produce with NCCL all-to-alls:
+ *   1. sm_ep_dispatch_prepare: route this rank's T tokens (router top-k as sm_router_topk) and
+ *      write one dispatch record per (token, destination rank), rank-major in token order, plus
+ *      send_counts [W] (records per destination) and ret_row [T*K] (the record index of entry k
+ *      of token t if it is the first entry of its rank for the token, else -1).
+ *   2. all-to-all of send_counts, then of the records (record size sm_ep_record_bytes(H, K):
+ *      e4m3 row, H/128 scale bytes, then at the next 16-byte boundary K int32 local expert ids
+ *      (-1 = not on this rank) and K float32 scores).
+ *   3. sm_ep_expert_forward on the R received records: local routing metadata, packing, the two
+ *      FP8 GEMMs; out_rows [R, H] bf16 row j = sum over the record's local experts of
+ *      score * expert output (the per-(token, rank) partial sum).
+ *   4. all-to-all of out_rows back (reversed splits) into ret [sum(send_counts), H].
+ *   5. sm_ep_combine: out [T, H] = sum of each token's returned rows (fp32 accumulation).
+ */
+int sm_ep_record_bytes(int H, int K);
+size_t sm_ep_dispatch_workspace_bytes(int T, int E, int K, int W);
+int sm_ep_dispatch_prepare(const void* x, const void* router_logits, int T, int H, int E, int K, int W, int rank,
+                           int softmax_over_topk, int norm_topk_probs, uint8_t* records, int32_t* ret_row,
+                           int32_t* send_counts, float* topk_scores, int32_t* topk_indices, void* workspace,
+                           size_t workspace_bytes, int32_t* err, void* stream);
+size_t sm_ep_expert_workspace_bytes(int R, int H, int I, int El, int K);
+int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, int K, const uint8_t* w1q,
+                         const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout,
+                         void* out_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
+                         int32_t* err, void* stream);
+int sm_ep_combine(const void* ret_rows, const int32_t* ret_row, int T, int K, int H, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,382 @@
+// Expert-parallel stages of the layer forward (experts sharded over W ranks, El = E / W per rank;
+// rank d owns global experts [d*El, (d+1)*El)).  The exchanges themselves are NCCL all-to-alls
+// issued by the host; these kernels build and consume the exchanged buffers.
+//
+// A dispatch record carries one token to one destination rank (a token routed to several experts
+// of the same rank travels once):
+//   [ H bytes e4m3 row | H/128 UE8M0 scale bytes | pad to 16 | K int32 local expert ids |
+//     K float32 scores | pad to 16 ]
+// Expert slots not on the destination rank hold -1 / 0.  The metadata starts on a 16-byte boundary
+// (meta_offset) so its 4-byte fields are aligned whatever H is.
+//
+// ep_dest_kernel       -- per (token, k): destination rank if k is the first entry of that rank for
+//                         the token, else -1 (duplicates ride along in the same record)
+// ep_send_pack_kernel  -- quantise each token once (1x128, same spec as the local path) and write
+//                         its records at their dispatch positions (rank-major, token order)
+// ep_recv_unpack_kernel-- local expert ids / scores of the received records as [R, K] arrays
+// ep_pack_fp8_kernel   -- copy received e4m3 rows + scales into the padded expert-major layout
+// ep_combine_kernel    -- owner side: o[t] = sum of the returned partial rows of token t (fp32)
+#include "../../include/sonic_b200.h"
+#include "common.cuh"
+#include "sonic_internal.h"
+
+namespace smb {
+
+__host__ __device__ constexpr int ep_meta_offset(int H) { return (H + H / kBlockK + 15) / 16 * 16; }
+
+__device__ __forceinline__ void bf16x8_to_f32_ep(const uint4& raw, float* v) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__global__ void ep_dest_kernel(const int32_t* __restrict__ idx, int T, int K, int El, int32_t* __restrict__ dest) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  for (int k = 0; k < K; ++k) {
+    const int d = idx[t * K + k] / El;
+    bool first = true;
+    for (int j = 0; j < k; ++j) first = first && (idx[t * K + j] / El != d);
+    dest[t * K + k] = first ? d : -1;
+  }
+}
+
+// One warp per token (same lane layout as quant_pack_kernel).
+__global__ void __launch_bounds__(256)
+    ep_send_pack_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, const int32_t* __restrict__ idx,
+                        const float* __restrict__ scores, int K, int El, const int32_t* __restrict__ dest,
+                        const int32_t* __restrict__ pos, int record_bytes, uint8_t* __restrict__ records,
+                        int32_t* __restrict__ ret_row) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  // destination record of each of the token's (up to 32) entries; lane k holds entry k
+  int my_pos = -1, my_rank = -1;
+  if (lane < K) {
+    const int f = t * K + lane;
+    my_rank = dest[f];
+    my_pos = my_rank >= 0 ? pos[f] : -1;
+    ret_row[f] = my_pos;
+  }
+  const __nv_bfloat16* src = x + static_cast<size_t>(t) * H;
+  for (int h0 = 0; h0 < H; h0 += 256) {
+    const int h = h0 + 8 * lane;
+    float v[8];
+    uint4 raw = (h < H) ? *reinterpret_cast<const uint4*>(src + h) : make_uint4(0, 0, 0, 0);
+    bf16x8_to_f32_ep(raw, v);
+    float am = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const int e8 = scale_exp_of_amax(am);
+    const float inv = exp2_neg(e8);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i += 2) {
+      lo |= static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[i], inv), __fmul_rn(v[i + 1], inv))) << (8 * i);
+      hi |= static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[4 + i], inv), __fmul_rn(v[5 + i], inv))) << (8 * i);
+    }
+    for (int k = 0; k < K; ++k) {
+      const int p = __shfl_sync(0xffffffffu, my_pos, k);
+      if (p < 0) continue;
+      uint8_t* rec = records + static_cast<size_t>(p) * record_bytes;
+      if (h < H) *reinterpret_cast<uint2*>(rec + h) = make_uint2(lo, hi);
+      if ((lane & 15) == 0 && h < H) rec[H + h / kBlockK] = static_cast<uint8_t>(e8 + 127);
+    }
+  }
+  // metadata: the token's experts on each destination rank
+  for (int k = 0; k < K; ++k) {
+    const int p = __shfl_sync(0xffffffffu, my_pos, k);
+    const int d = __shfl_sync(0xffffffffu, my_rank, k);
+    if (p < 0) continue;
+    uint8_t* rec = records + static_cast<size_t>(p) * record_bytes + ep_meta_offset(H);
+    if (lane < K) {
+      const int e = idx[t * K + lane];
+      const bool mine = (e / El) == d;
+      reinterpret_cast<int32_t*>(rec)[lane] = mine ? e - d * El : -1;
+      reinterpret_cast<float*>(rec + 4 * K)[lane] = mine ? scores[t * K + lane] : 0.0f;
+    }
+  }
+}
+
+__global__ void ep_recv_unpack_kernel(const uint8_t* __restrict__ records, int R, int H, int K, int record_bytes,
+                                      int32_t* __restrict__ idx_local, float* __restrict__ scores) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= R * K) return;
+  const int j = i / K, k = i - (i / K) * K;
+  const uint8_t* meta = records + static_cast<size_t>(j) * record_bytes + ep_meta_offset(H);
+  idx_local[i] = reinterpret_cast<const int32_t*>(meta)[k];
+  scores[i] = reinterpret_cast<const float*>(meta + 4 * K)[k];
+}
+
+// One warp per received record: its e4m3 row and scale bytes go to the padded row of each of its
+// local entries (entries with expert -1 are skipped).
+__global__ void __launch_bounds__(256)
+    ep_pack_fp8_kernel(const uint8_t* __restrict__ records, int R, int H, int K, int El, int record_bytes,
+                       const int32_t* __restrict__ idx_local, const int32_t* __restrict__ s_rev,
+                       const int32_t* __restrict__ off, const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq,
+                       uint8_t* __restrict__ xsf) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x * 8 + warp;
+  if (j >= R) return;
+  int my_dst = -1;
+  if (lane < K) {
+    const int f = j * K + lane;
+    const int e = idx_local[f];
+    if (e >= 0 && e < El) my_dst = s_rev[f] - off[e] + off_pad[e];
+  }
+  const uint8_t* rec = records + static_cast<size_t>(j) * record_bytes;
+  const int G = H / kBlockK;
+  const int KG = (G + 3) / 4;
+  for (int k = 0; k < K; ++k) {
+    const int p = __shfl_sync(0xffffffffu, my_dst, k);
+    if (p < 0) continue;
+    uint8_t* dst = xq + static_cast<size_t>(p) * H;
+    for (int h = 16 * lane; h < H; h += 512)
+      *reinterpret_cast<uint4*>(dst + h) = *reinterpret_cast<const uint4*>(rec + h);
+    for (int g = lane; g < G; g += 32) {
+      const size_t o = (static_cast<size_t>(p / kBlockM) * KG + g / 4) * kSfAtomBytes + 16 * (p % 32) +
+                       4 * ((p % kBlockM) / 32) + (g % 4);
+      xsf[o] = rec[H + g];
+    }
+  }
+}
+
+// One CTA per token: o[t] = sum over the token's returned rows (fp32), rounded once to bf16.
+__global__ void __launch_bounds__(256)
+    ep_combine_kernel(const __nv_bfloat16* __restrict__ ret, const int32_t* __restrict__ ret_row, int T, int K, int H,
+                      __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  __shared__ int rows[32];
+  __shared__ int nrows;
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int k = 0; k < K; ++k) {
+      const int r = ret_row[t * K + k];
+      if (r >= 0) rows[n++] = r;
+    }
+    nrows = n;
+  }
+  __syncthreads();
+  for (int h = 8 * threadIdx.x; h < H; h += 8 * blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i < nrows; ++i) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(ret + static_cast<size_t>(rows[i]) * H + h);
+      float v[8];
+      bf16x8_to_f32_ep(raw, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += v[q];
+    }
+    uint4 w;
+    w.x = (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(acc[1]))) << 16) |
+          __bfloat16_as_ushort(__float2bfloat16_rn(acc[0]));
+    w.y = (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(acc[3]))) << 16) |
+          __bfloat16_as_ushort(__float2bfloat16_rn(acc[2]));
+    w.z = (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(acc[5]))) << 16) |
+          __bfloat16_as_ushort(__float2bfloat16_rn(acc[4]));
+    w.w = (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(acc[7]))) << 16) |
+          __bfloat16_as_ushort(__float2bfloat16_rn(acc[6]));
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + h) = w;
+  }
+}
+
+}  // namespace smb
+
+using namespace smb;
+
+namespace {
+
+size_t a256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+int ep_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return SM_OK;
+  return set_last_error(SM_EIO, "%s: %s", what, cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" {
+
+int sm_ep_record_bytes(int H, int K) { return (ep_meta_offset(H) + 8 * K + 15) / 16 * 16; }
+
+size_t sm_ep_dispatch_workspace_bytes(int T, int E, int K, int W) {
+  const long long TK = static_cast<long long>(T) * K;
+  return a256(TK * 4) * 5 + a256(static_cast<size_t>(W) * (ceil_div(T, kTileTokens) + 1) * 4) +
+         a256(static_cast<size_t>(W + 1) * 4) * 2 + a256((static_cast<size_t>(max_padded_blocks(TK, W)) + 2) * 4) +
+         a256(4) + 4096;
+}
+
+int sm_ep_dispatch_prepare(const void* x, const void* router_logits, int T, int H, int E, int K, int W, int rank,
+                           int softmax_over_topk, int norm_topk_probs, uint8_t* records, int32_t* ret_row,
+                           int32_t* send_counts, float* topk_scores, int32_t* topk_indices, void* workspace,
+                           size_t workspace_bytes, int32_t* err, void* stream) {
+  (void)rank;
+  if (T < 0 || H <= 0 || H % 256 || E < 1 || W < 1 || E % W || K < 1 || K > 32 || K > E)
+    return set_last_error(SM_EINVAL, "ep dispatch: bad shape T=%d H=%d E=%d K=%d W=%d", T, H, E, K, W);
+  if (!send_counts || !err || (T > 0 && (!x || !router_logits || !records || !ret_row || !topk_scores ||
+                                         !topk_indices)))
+    return set_last_error(SM_EINVAL, "ep dispatch: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int El = E / W;
+  const long long TK = static_cast<long long>(T) * K;
+  const int n_tiles = ceil_div(T, kTileTokens);
+  uint8_t* p = static_cast<uint8_t*>(workspace);
+  size_t used = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* q = p + used;
+    used += a256(bytes);
+    return q;
+  };
+  int32_t* dest = reinterpret_cast<int32_t*>(take(TK * 4));
+  int32_t* pos = reinterpret_cast<int32_t*>(take(TK * 4));
+  int32_t* s_scatter = reinterpret_cast<int32_t*>(take(TK * 4));
+  int32_t* x_gather = reinterpret_cast<int32_t*>(take(TK * 4));
+  take(TK * 4);
+  int32_t* tile_counts = reinterpret_cast<int32_t*>(take(static_cast<size_t>(W) * (n_tiles + 1) * 4));
+  int32_t* off = reinterpret_cast<int32_t*>(take(static_cast<size_t>(W + 1) * 4));
+  int32_t* off_pad = reinterpret_cast<int32_t*>(take(static_cast<size_t>(W + 1) * 4));
+  int32_t* blk = reinterpret_cast<int32_t*>(take((static_cast<size_t>(max_padded_blocks(TK, W)) + 2) * 4));
+  int32_t* nblk = reinterpret_cast<int32_t*>(take(4));
+  if (used > workspace_bytes) return set_last_error(SM_EINVAL, "ep dispatch: workspace too small");
+  if (T == 0) return ep_status(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * W, st), "ep dispatch");
+  cudaError_t e = launch_router_topk(router_logits, kDtypeBF16, T, E, K, softmax_over_topk, norm_topk_probs,
+                                     topk_scores, topk_indices, nullptr, st);
+  if (e == cudaSuccess) {
+    ep_dest_kernel<<<(T + 255) / 256, 256, 0, st>>>(topk_indices, T, K, El, dest);
+    e = cudaGetLastError();
+  }
+  // rank-major dispatch order: the token-choice metadata over "experts" = destination ranks, with
+  // duplicate (token, rank) entries as holes
+  if (e == cudaSuccess)
+    e = launch_route_hist_holes(dest, static_cast<int>(TK), kTileTokens * K, W, n_tiles, tile_counts, err, st);
+  if (e == cudaSuccess)
+    e = launch_route_scan(tile_counts, n_tiles, W, static_cast<int>(TK), send_counts, off, off_pad, blk, nblk, st);
+  if (e == cudaSuccess)
+    e = launch_route_scatter(dest, nullptr, static_cast<int>(TK), K, kTileTokens * K, W, n_tiles, tile_counts, off,
+                             s_scatter, pos, x_gather, st);
+  if (e == cudaSuccess) {
+    ep_send_pack_kernel<<<(T + 7) / 8, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, topk_indices,
+                                                     topk_scores, K, El, dest, pos, sm_ep_record_bytes(H, K), records,
+                                                     ret_row);
+    e = cudaGetLastError();
+  }
+  return ep_status(e, "ep dispatch");
+}
+
+size_t sm_ep_expert_workspace_bytes(int R, int H, int I, int El, int K) {
+  const long long TK = static_cast<long long>(R) * K;
+  const size_t mb = max_padded_blocks(TK, El);
+  return a256(TK * 4) * 5 + a256(static_cast<size_t>(El) * (ceil_div(R, kTileTokens) + 1) * 4) +
+         a256(static_cast<size_t>(El + 1) * 4) * 2 + a256((mb + 2) * 4) + a256(4) +
+         a256(mb * kBlockM * static_cast<size_t>(H)) + a256(mb * ceil_div(H, 512) * kSfAtomBytes) +
+         a256(mb * kBlockM * static_cast<size_t>(I)) + a256(mb * ceil_div(I, 512) * kSfAtomBytes) + 4096;
+}
+
+int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, int K, const uint8_t* w1q,
+                         const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout,
+                         void* out_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
+                         int32_t* err, void* stream) {
+  if (R < 0 || H <= 0 || H % 256 || I <= 0 || I % 128 || El < 1 || K < 1 || K > 32)
+    return set_last_error(SM_EINVAL, "ep expert: bad shape R=%d H=%d I=%d El=%d K=%d", R, H, I, El, K);
+  if (!expert_frequency || !err) return set_last_error(SM_EINVAL, "ep expert: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (R == 0) return ep_status(cudaMemsetAsync(expert_frequency, 0, sizeof(int32_t) * El, st), "ep expert");
+  const long long TK = static_cast<long long>(R) * K;
+  const int n_tiles = ceil_div(R, kTileTokens);
+  const int mb = max_padded_blocks(TK, El);
+  uint8_t* p = static_cast<uint8_t*>(workspace);
+  size_t used = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* q = p + used;
+    used += a256(bytes);
+    return q;
+  };
+  int32_t* idx = reinterpret_cast<int32_t*>(take(TK * 4));
+  float* scores = reinterpret_cast<float*>(take(TK * 4));
+  int32_t* s_scatter = reinterpret_cast<int32_t*>(take(TK * 4));
+  int32_t* s_rev = reinterpret_cast<int32_t*>(take(TK * 4));
+  int32_t* x_gather = reinterpret_cast<int32_t*>(take(TK * 4));
+  int32_t* tile_counts = reinterpret_cast<int32_t*>(take(static_cast<size_t>(El) * (n_tiles + 1) * 4));
+  int32_t* off = reinterpret_cast<int32_t*>(take(static_cast<size_t>(El + 1) * 4));
+  int32_t* off_pad = reinterpret_cast<int32_t*>(take(static_cast<size_t>(El + 1) * 4));
+  int32_t* blk = reinterpret_cast<int32_t*>(take((static_cast<size_t>(mb) + 2) * 4));
+  int32_t* nblk = reinterpret_cast<int32_t*>(take(4));
+  uint8_t* xq = take(static_cast<size_t>(mb) * kBlockM * H);
+  uint8_t* xsf = take(static_cast<size_t>(mb) * ceil_div(H, 512) * kSfAtomBytes);
+  uint8_t* aq = take(static_cast<size_t>(mb) * kBlockM * I);
+  uint8_t* asf = take(static_cast<size_t>(mb) * ceil_div(I, 512) * kSfAtomBytes);
+  if (used > workspace_bytes) return set_last_error(SM_EINVAL, "ep expert: workspace too small");
+  const int rb = sm_ep_record_bytes(H, K);
+  ep_recv_unpack_kernel<<<static_cast<int>((TK + 255) / 256), 256, 0, st>>>(records, R, H, K, rb, idx, scores);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess)
+    e = launch_route_hist_holes(idx, static_cast<int>(TK), kTileTokens * K, El, n_tiles, tile_counts, err, st);
+  if (e == cudaSuccess)
+    e = launch_route_scan(tile_counts, n_tiles, El, static_cast<int>(TK), expert_frequency, off, off_pad, blk, nblk,
+                          st);
+  if (e == cudaSuccess)
+    e = launch_route_scatter(idx, nullptr, static_cast<int>(TK), K, kTileTokens * K, El, n_tiles, tile_counts, off,
+                             s_scatter, s_rev, x_gather, st);
+  if (e == cudaSuccess) {
+    ep_pack_fp8_kernel<<<(R + 7) / 8, 256, 0, st>>>(records, R, H, K, El, rb, idx, s_rev, off, off_pad, xq, xsf);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemsetAsync(out_rows, 0, static_cast<size_t>(R) * H * 2, st);
+  if (e == cudaSuccess) {
+    GemmArgs g{};
+    g.a = xq;
+    g.a_sf = xsf;
+    g.a_rows = static_cast<long long>(mb) * kBlockM;
+    g.b = w1q;
+    g.b_sf = w1_sf;
+    g.E = El;
+    g.N = 2 * I;
+    g.Kd = H;
+    g.blk_expert = blk;
+    g.n_blocks = nblk;
+    g.off_pad = off_pad;
+    g.freq = expert_frequency;
+    g.out_q = aq;
+    g.out_sf = asf;
+    g.concat = concat_layout;
+    g.err = err;
+    int dev = 0, nsm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    g.num_sms = nsm > 0 ? nsm : 148;
+    g.tokens = R;
+    e = launch_moe_up(g, st);
+    if (e == cudaSuccess) {
+      GemmArgs d = g;
+      d.a = aq;
+      d.a_sf = asf;
+      d.b = w2q;
+      d.b_sf = w2_sf;
+      d.N = H;
+      d.Kd = I;
+      d.off = off;
+      d.s_scatter = s_scatter;
+      d.x_gather = x_gather;
+      d.scores = scores;
+      d.out_bf16 = out_rows;
+      d.out_q = nullptr;
+      d.out_sf = nullptr;
+      e = launch_moe_down(d, st);
+    }
+  }
+  return ep_status(e, "ep expert forward");
+}
+
+int sm_ep_combine(const void* ret_rows, const int32_t* ret_row, int T, int K, int H, void* out, void* stream) {
+  if (T < 0 || K < 1 || K > 32 || H <= 0 || H % 8) return set_last_error(SM_EINVAL, "ep combine: bad shape");
+  if (T == 0) return SM_OK;
+  ep_combine_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(ret_rows), ret_row, T, K, H, static_cast<__nv_bfloat16*>(out));
+  return ep_status(cudaGetLastError(), "ep combine");
+}
+
+}  // extern "C"

@@ -234,8 +234,11 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
 // ---------------------------------------------------------------------------------------------
 // Tile histogram of externally supplied expert ids.  Tile t covers flat entries
 // [t * entries_per_tile, (t + 1) * entries_per_tile).
+// With allow_holes, negative ids mark "no entry" (used by the expert-parallel path) and are skipped
+// silently; otherwise they are reported like any id outside [0, E).
 __global__ void route_hist_kernel(const int32_t* __restrict__ experts, int TK, int entries_per_tile, int E,
-                                  int n_tiles, int32_t* __restrict__ tile_counts, int* __restrict__ err) {
+                                  int n_tiles, int allow_holes, int32_t* __restrict__ tile_counts,
+                                  int* __restrict__ err) {
   extern __shared__ int32_t s_hist[];
   const int tile = blockIdx.x;
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
@@ -246,7 +249,7 @@ __global__ void route_hist_kernel(const int32_t* __restrict__ experts, int TK, i
     const int e = experts[f];
     if (e >= 0 && e < E) {
       atomicAdd(&s_hist[e], 1);
-    } else {
+    } else if (!(allow_holes && e < 0)) {
       atomicCAS(err, 0, kErrBadExpert);
     }
   }
@@ -446,14 +449,25 @@ cudaError_t launch_router_topk(const void* logits, int dtype, int T, int E, int 
   }
 }
 
-cudaError_t launch_route_hist(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,
-                              int32_t* tile_counts, int* err, cudaStream_t st) {
+static cudaError_t route_hist_impl(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,
+                                   int allow_holes, int32_t* tile_counts, int* err, cudaStream_t st) {
   if (n_tiles == 0) return cudaSuccess;
   const size_t smem = static_cast<size_t>(E) * sizeof(int32_t);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(route_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  route_hist_kernel<<<n_tiles, 256, smem, st>>>(experts, TK, entries_per_tile, E, n_tiles, tile_counts, err);
+  route_hist_kernel<<<n_tiles, 256, smem, st>>>(experts, TK, entries_per_tile, E, n_tiles, allow_holes, tile_counts,
+                                                err);
   return cudaGetLastError();
+}
+
+cudaError_t launch_route_hist(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,
+                              int32_t* tile_counts, int* err, cudaStream_t st) {
+  return route_hist_impl(experts, TK, entries_per_tile, E, n_tiles, 0, tile_counts, err, st);
+}
+
+cudaError_t launch_route_hist_holes(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,
+                                    int32_t* tile_counts, int* err, cudaStream_t st) {
+  return route_hist_impl(experts, TK, entries_per_tile, E, n_tiles, 1, tile_counts, err, st);
 }
 
 cudaError_t launch_route_scan(int32_t* tile_counts, int n_tiles, int E, int TK, int32_t* freq, int32_t* off,

@@ -30,6 +30,9 @@ cudaError_t launch_router_topk(const void* logits, int dtype, int T, int E, int 
                                float* scores, int32_t* idx, int32_t* tile_counts, cudaStream_t st);
 cudaError_t launch_route_hist(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,
                               int32_t* tile_counts, int* err, cudaStream_t st);
+// Same, but negative expert ids are holes (no entry) instead of errors.
+cudaError_t launch_route_hist_holes(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,
+                                    int32_t* tile_counts, int* err, cudaStream_t st);
 cudaError_t launch_route_scan(int32_t* tile_counts, int n_tiles, int E, int TK, int32_t* freq, int32_t* off,
                               int32_t* off_pad, int32_t* blk_expert, int32_t* n_blocks, cudaStream_t st);
 cudaError_t launch_route_scatter(const int32_t* experts, const int32_t* token_of_entry, int TK, int K,

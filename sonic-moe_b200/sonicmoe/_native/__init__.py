@@ -52,6 +52,18 @@ SIGNATURES = {
         [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P],
     ),
     "sm_max_padded_blocks": (_I, [_LL, _I]),
+    "sm_ep_record_bytes": (_I, [_I, _I]),
+    "sm_ep_dispatch_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "sm_ep_dispatch_prepare": (
+        _I,
+        [_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _SZ, _P, _P],
+    ),
+    "sm_ep_expert_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "sm_ep_expert_forward": (
+        _I,
+        [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P, _P],
+    ),
+    "sm_ep_combine": (_I, [_P, _P, _I, _I, _I, _P, _P]),
     "sm_route_plan": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "sm_quant_pack": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),

@@ -1,0 +1,108 @@
+"""Expert-parallel host logic on CPU: 2 gloo ranks, device stages replaced by oracle stand-ins.
+
+Checks the orchestration of sonicmoe.ep (count exchange, split sizes, the two all-to-alls and the
+combine) against the single-process fake-quantised oracle over all tokens, and that a bad count
+injected on one rank makes every rank raise (the validation is agreed collectively, so nobody
+waits in a collective the others skipped).
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+T_PER_RANK, H, I, E, K, W = 48, 256, 128, 8, 3, 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(W * T_PER_RANK, H, generator=g).to(torch.bfloat16)
+    rw = (torch.randn(E, H, generator=g) * 0.05).to(torch.bfloat16)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    return x, rw, w1, w2
+
+
+def _worker(rank, port, bad_rank, q):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "sonic-moe_b200"), os.path.join(root, "tests")):
+        sys.path.insert(0, p)
+    import datetime
+
+    import torch.distributed as dist
+
+    from _ep_fakes import FakeStages
+    from sonicmoe.ep import ExpertParallelMoE
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=W, timeout=datetime.timedelta(seconds=60))
+    try:
+        x, rw, w1, w2 = _inputs()
+        El = E // W
+        moe = ExpertParallelMoE(rw, w1[rank * El:(rank + 1) * El], w2[rank * El:(rank + 1) * El], E, K,
+                                stages=FakeStages(bad_count_rank=bad_rank))
+        xs = x[rank * T_PER_RANK:(rank + 1) * T_PER_RANK].float()
+        try:
+            out, logits, freq = moe.forward(xs.to(torch.bfloat16))
+            q.put((rank, "ok", out.float().numpy(), logits.float().numpy()))
+        except RuntimeError as e:
+            q.put((rank, "error", str(e), None))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(bad_rank):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, port, bad_rank, q)) for r in range(W)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(W):
+        r, status, a, b = q.get(timeout=240)
+        res[r] = (status, a, b)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return res
+
+
+def test_ep_two_ranks_matches_single_process_oracle():
+    from oracle.layer import fp8_oracle, rel_fro
+
+    res = _run(bad_rank=None)
+    assert all(res[r][0] == "ok" for r in range(W)), res
+    x, rw, w1, w2 = _inputs()
+    out = np.concatenate([res[r][1] for r in range(W)])
+    logits = np.concatenate([res[r][2] for r in range(W)])
+    o_ref, _, _ = fp8_oracle(x.float().numpy(), logits, w1.float().numpy(), w2.float().numpy(), K)
+    assert rel_fro(out, o_ref.numpy()) < 5e-3  # bf16 rounding of the per-rank partial rows only
+
+
+def test_ep_bad_count_aborts_every_rank():
+    res = _run(bad_rank=1)
+    assert all(res[r][0] == "error" for r in range(W)), res
+    assert "negative record count" in res[1][1]
+    assert "peer rank" in res[0][1]
+
+
+def test_check_counts():
+    from sonicmoe.ep import check_counts
+
+    assert check_counts([1, 2], [3, 4], 10) == ""
+    assert "negative" in check_counts([1, -1], [0, 0], 10)
+    assert "exceed" in check_counts([6, 6], [0, 0], 10)
