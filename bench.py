@@ -153,7 +153,7 @@ def run_ep(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
     x, rw, w1p, w2p = build_ep_workload(dev, rank, world, T, H, I, E, K)
-    moe = ExpertParallelMoE(rw, w1p, w2p, E, K)
+    moe = ExpertParallelMoE(rw, w1p, w2p, E, K, max_tokens=T, hidden_size=H)
     for _ in range(args.warmup):
         moe.forward(x)
     torch.cuda.synchronize()
@@ -186,6 +186,7 @@ def run_ep(args, rank, world, local_rank):
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) / steps_e2e], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    moe.close()
     return {
         "ms_step": ms_step,
         "tokens_per_s": world * T / (ms_step / 1e3),

@@ -237,6 +237,43 @@ int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, in
                          int32_t* err, void* stream);
 int sm_ep_combine(const void* ret_rows, const int32_t* ret_row, int T, int K, int H, void* out, void* stream);
 
+/*
+ * Peer-memory variants (GPUs of one node, buffers mapped with sm_ipc_open): the exchanges become
+ * loads over NVLink inside the stage kernels instead of separate all-to-alls.
+ *   sm_ep_expert_forward_p2p reads the records of source rank s directly from s's send buffer
+ *   peer_send_bases[s], starting at record seg_off[s] (the offset of this rank's segment there),
+ *   recv_counts[s] records; the received records are numbered in source order.
+ *   sm_ep_combine_p2p reads each token's partial rows from the output rows of the destination
+ *   ranks: this rank's send record p of destination d (send_counts gives the segments) is row
+ *   recv_start[d] + (p - segment start) of peer_out_bases[d].
+ * All arrays here are host arrays of W <= 16 entries (passed to the kernels by value).  The caller
+ * orders the stages with barriers (a rank's send buffer is complete before peers read it, its
+ * output rows before peers combine, and nobody rewrites a buffer a peer may still read).
+ */
+int sm_ep_expert_forward_p2p(const void* const* peer_send_bases, const int32_t* seg_off, const int32_t* recv_counts,
+                             int W, int H, int I, int El, int K, const uint8_t* w1q, const uint8_t* w1_sf,
+                             const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout, void* out_rows,
+                             int32_t* expert_frequency, void* workspace, size_t workspace_bytes, int32_t* err,
+                             void* stream);
+int sm_ep_combine_p2p(const void* const* peer_out_bases, const int32_t* send_counts, const int32_t* recv_start,
+                      int W, const int32_t* ret_row, int T, int K, int H, void* out, void* stream);
+
+/*
+ * Device buffers shared between the processes of one node through CUDA IPC (no counterpart in the
+ * reference).  sm_ipc_alloc allocates (cudaMalloc -- an explicit allocation, unlike every compute
+ * entry point) and returns the 64-byte IPC handle; a peer process maps it with sm_ipc_open and
+ * unmaps with sm_ipc_close; the owner frees with sm_ipc_free.
+ */
+int sm_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int sm_ipc_open(const void* handle, void** ptr);
+int sm_ipc_close(void* ptr);
+int sm_ipc_free(void* ptr);
+
+/* Leave n SMs of each device out of the persistent GEMM grids (process-wide setting, default 0), so
+ * that communication kernels launched alongside (the expert-parallel all-to-alls) find free SMs.
+ * No counterpart in the reference. */
+int sm_set_gemm_sm_reserve(int n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,12 +37,7 @@ int cuda_status(cudaError_t e, const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int num_sms() {
-  int dev = 0, n = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
-}
+int num_sms() { return gemm_grid_sms(); }
 
 // Bump allocator over a caller-provided workspace (256-byte aligned pieces).
 struct Carve {

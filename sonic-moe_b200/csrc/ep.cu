@@ -16,6 +16,8 @@
 // ep_recv_unpack_kernel-- local expert ids / scores of the received records as [R, K] arrays
 // ep_pack_fp8_kernel   -- copy received e4m3 rows + scales into the padded expert-major layout
 // ep_combine_kernel    -- owner side: o[t] = sum of the returned partial rows of token t (fp32)
+#include <cstring>
+
 #include "../../include/sonic_b200.h"
 #include "common.cuh"
 #include "sonic_internal.h"
@@ -23,6 +25,44 @@
 namespace smb {
 
 __host__ __device__ constexpr int ep_meta_offset(int H) { return (H + H / kBlockK + 15) / 16 * 16; }
+
+constexpr int kMaxRanks = 16;
+
+// Where received record j lives: in the send buffer of source rank s (possibly another GPU's memory,
+// reached by peer loads) at record index seg_off[s] + (j - start[s]), for start[s] <= j < start[s+1].
+// A contiguous local buffer is the case W = 1, seg_off = 0.
+struct RecordSource {
+  const uint8_t* base[kMaxRanks];
+  int seg_off[kMaxRanks];
+  int start[kMaxRanks + 1];
+  int W;
+  int rb;
+};
+
+__device__ __forceinline__ const uint8_t* record_ptr(const RecordSource& rs, int j) {
+  int s = 0;
+  while (s + 1 < rs.W && j >= rs.start[s + 1]) ++s;
+  return rs.base[s] + static_cast<size_t>(rs.seg_off[s] + (j - rs.start[s])) * rs.rb;
+}
+
+// Where the partial row for this rank's send record p lives: p falls in the segment of destination
+// rank d (send_off[d] <= p < send_off[d+1]); rank d computed it as row recv_start[d] + (p - send_off[d])
+// of its output rows at base[d].
+struct RowSource {
+  const __nv_bfloat16* base[kMaxRanks];
+  int send_off[kMaxRanks + 1];
+  int recv_start[kMaxRanks];
+  int W;
+};
+
+__device__ __forceinline__ const __nv_bfloat16* partial_row_ptr(const RowSource& rs, int p, int H) {
+  int d = 0;
+  while (d + 1 < rs.W && p >= rs.send_off[d + 1]) ++d;
+  return rs.base[d] + static_cast<size_t>(rs.recv_start[d] + (p - rs.send_off[d])) * H;
+}
+
+// 16-byte load cached in L2 only (peer memory written by another GPU's kernel).
+__device__ __forceinline__ uint4 ld_cg16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
 
 __device__ __forceinline__ void bf16x8_to_f32_ep(const uint4& raw, float* v) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -103,23 +143,25 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-__global__ void ep_recv_unpack_kernel(const uint8_t* __restrict__ records, int R, int H, int K, int record_bytes,
-                                      int32_t* __restrict__ idx_local, float* __restrict__ scores) {
+__global__ void ep_recv_unpack_kernel(const RecordSource rs, int R, int H, int K, int32_t* __restrict__ idx_local,
+                                      float* __restrict__ scores) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= R * K) return;
   const int j = i / K, k = i - (i / K) * K;
-  const uint8_t* meta = records + static_cast<size_t>(j) * record_bytes + ep_meta_offset(H);
-  idx_local[i] = reinterpret_cast<const int32_t*>(meta)[k];
-  scores[i] = reinterpret_cast<const float*>(meta + 4 * K)[k];
+  const uint8_t* meta = record_ptr(rs, j) + ep_meta_offset(H);
+  idx_local[i] = __ldcg(reinterpret_cast<const int32_t*>(meta) + k);
+  scores[i] = __ldcg(reinterpret_cast<const float*>(meta + 4 * K) + k);
 }
 
 // One warp per received record: its e4m3 row and scale bytes go to the padded row of each of its
-// local entries (entries with expert -1 are skipped).
+// local entries (entries with expert -1 are skipped).  The record may sit in another GPU's send
+// buffer; the row is read once (up to 8 x 16 B per lane in flight) and written to every entry.
+constexpr int kPackChunks = 8;  // 16-byte loads per lane per pass (H <= 4096 in one pass)
+
 __global__ void __launch_bounds__(256)
-    ep_pack_fp8_kernel(const uint8_t* __restrict__ records, int R, int H, int K, int El, int record_bytes,
-                       const int32_t* __restrict__ idx_local, const int32_t* __restrict__ s_rev,
-                       const int32_t* __restrict__ off, const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq,
-                       uint8_t* __restrict__ xsf) {
+    ep_pack_fp8_kernel(const RecordSource rs, int R, int H, int K, int El, const int32_t* __restrict__ idx_local,
+                       const int32_t* __restrict__ s_rev, const int32_t* __restrict__ off,
+                       const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq, uint8_t* __restrict__ xsf) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = blockIdx.x * 8 + warp;
   if (j >= R) return;
@@ -129,47 +171,72 @@ __global__ void __launch_bounds__(256)
     const int e = idx_local[f];
     if (e >= 0 && e < El) my_dst = s_rev[f] - off[e] + off_pad[e];
   }
-  const uint8_t* rec = records + static_cast<size_t>(j) * record_bytes;
+  const uint8_t* rec = record_ptr(rs, j);
   const int G = H / kBlockK;
   const int KG = (G + 3) / 4;
+  const uint8_t sfb = (lane < G) ? __ldcg(rec + H + lane) : 0;
+  for (int h0 = 0; h0 < H; h0 += 512 * kPackChunks) {
+    uint4 v[kPackChunks];
+#pragma unroll
+    for (int c = 0; c < kPackChunks; ++c) {
+      const int h = h0 + 512 * c + 16 * lane;
+      v[c] = (h < H) ? ld_cg16(rec + h) : make_uint4(0, 0, 0, 0);
+    }
+    for (int k = 0; k < K; ++k) {
+      const int p = __shfl_sync(0xffffffffu, my_dst, k);
+      if (p < 0) continue;
+      uint8_t* dst = xq + static_cast<size_t>(p) * H;
+#pragma unroll
+      for (int c = 0; c < kPackChunks; ++c) {
+        const int h = h0 + 512 * c + 16 * lane;
+        if (h < H) *reinterpret_cast<uint4*>(dst + h) = v[c];
+      }
+    }
+  }
   for (int k = 0; k < K; ++k) {
     const int p = __shfl_sync(0xffffffffu, my_dst, k);
     if (p < 0) continue;
-    uint8_t* dst = xq + static_cast<size_t>(p) * H;
-    for (int h = 16 * lane; h < H; h += 512)
-      *reinterpret_cast<uint4*>(dst + h) = *reinterpret_cast<const uint4*>(rec + h);
     for (int g = lane; g < G; g += 32) {
+      const uint8_t b = (g < 32) ? sfb : __ldcg(rec + H + g);  // g == lane below 32
       const size_t o = (static_cast<size_t>(p / kBlockM) * KG + g / 4) * kSfAtomBytes + 16 * (p % 32) +
                        4 * ((p % kBlockM) / 32) + (g % 4);
-      xsf[o] = rec[H + g];
+      xsf[o] = b;
     }
   }
 }
 
-// One CTA per token: o[t] = sum over the token's returned rows (fp32), rounded once to bf16.
+// One CTA per token: o[t] = sum over the token's partial rows (fp32), rounded once to bf16.  The
+// rows may sit in other GPUs' output buffers (peer loads); all of a token's rows for one 8-column
+// slice are loaded before they are summed.
 __global__ void __launch_bounds__(256)
-    ep_combine_kernel(const __nv_bfloat16* __restrict__ ret, const int32_t* __restrict__ ret_row, int T, int K, int H,
+    ep_combine_kernel(const RowSource rs, const int32_t* __restrict__ ret_row, int T, int K, int H,
                       __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
-  __shared__ int rows[32];
+  __shared__ const __nv_bfloat16* rows[32];
   __shared__ int nrows;
   if (threadIdx.x == 0) {
     int n = 0;
     for (int k = 0; k < K; ++k) {
-      const int r = ret_row[t * K + k];
-      if (r >= 0) rows[n++] = r;
+      const int p = ret_row[t * K + k];
+      if (p >= 0) rows[n++] = partial_row_ptr(rs, p, H);
     }
     nrows = n;
   }
   __syncthreads();
+  const int n = nrows;
   for (int h = 8 * threadIdx.x; h < H; h += 8 * blockDim.x) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int i = 0; i < nrows; ++i) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(ret + static_cast<size_t>(rows[i]) * H + h);
-      float v[8];
-      bf16x8_to_f32_ep(raw, v);
+    for (int i0 = 0; i0 < n; i0 += 8) {
+      uint4 raw[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += v[q];
+      for (int i = 0; i < 8; ++i) raw[i] = (i0 + i < n) ? ld_cg16(rows[i0 + i] + h) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float v[8];
+        bf16x8_to_f32_ep(raw[i], v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += v[q];
+      }
     }
     uint4 w;
     w.x = (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(acc[1]))) << 16) |
@@ -276,10 +343,10 @@ size_t sm_ep_expert_workspace_bytes(int R, int H, int I, int El, int K) {
          a256(mb * kBlockM * static_cast<size_t>(I)) + a256(mb * ceil_div(I, 512) * kSfAtomBytes) + 4096;
 }
 
-int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, int K, const uint8_t* w1q,
-                         const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout,
-                         void* out_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
-                         int32_t* err, void* stream) {
+static int ep_expert_forward(const RecordSource& src, int R, int H, int I, int El, int K, const uint8_t* w1q,
+                             const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout,
+                             void* out_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
+                             int32_t* err, void* stream) {
   if (R < 0 || H <= 0 || H % 256 || I <= 0 || I % 128 || El < 1 || K < 1 || K > 32)
     return set_last_error(SM_EINVAL, "ep expert: bad shape R=%d H=%d I=%d El=%d K=%d", R, H, I, El, K);
   if (!expert_frequency || !err) return set_last_error(SM_EINVAL, "ep expert: null pointer");
@@ -310,8 +377,7 @@ int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, in
   uint8_t* aq = take(static_cast<size_t>(mb) * kBlockM * I);
   uint8_t* asf = take(static_cast<size_t>(mb) * ceil_div(I, 512) * kSfAtomBytes);
   if (used > workspace_bytes) return set_last_error(SM_EINVAL, "ep expert: workspace too small");
-  const int rb = sm_ep_record_bytes(H, K);
-  ep_recv_unpack_kernel<<<static_cast<int>((TK + 255) / 256), 256, 0, st>>>(records, R, H, K, rb, idx, scores);
+  ep_recv_unpack_kernel<<<static_cast<int>((TK + 255) / 256), 256, 0, st>>>(src, R, H, K, idx, scores);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess)
     e = launch_route_hist_holes(idx, static_cast<int>(TK), kTileTokens * K, El, n_tiles, tile_counts, err, st);
@@ -322,7 +388,7 @@ int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, in
     e = launch_route_scatter(idx, nullptr, static_cast<int>(TK), K, kTileTokens * K, El, n_tiles, tile_counts, off,
                              s_scatter, s_rev, x_gather, st);
   if (e == cudaSuccess) {
-    ep_pack_fp8_kernel<<<(R + 7) / 8, 256, 0, st>>>(records, R, H, K, El, rb, idx, s_rev, off, off_pad, xq, xsf);
+    ep_pack_fp8_kernel<<<(R + 7) / 8, 256, 0, st>>>(src, R, H, K, El, idx, s_rev, off, off_pad, xq, xsf);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) e = cudaMemsetAsync(out_rows, 0, static_cast<size_t>(R) * H * 2, st);
@@ -344,10 +410,7 @@ int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, in
     g.out_sf = asf;
     g.concat = concat_layout;
     g.err = err;
-    int dev = 0, nsm = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    g.num_sms = nsm > 0 ? nsm : 148;
+    g.num_sms = gemm_grid_sms();
     g.tokens = R;
     e = launch_moe_up(g, st);
     if (e == cudaSuccess) {
@@ -371,12 +434,102 @@ int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, in
   return ep_status(e, "ep expert forward");
 }
 
-int sm_ep_combine(const void* ret_rows, const int32_t* ret_row, int T, int K, int H, void* out, void* stream) {
+int sm_ep_expert_forward(const uint8_t* records, int R, int H, int I, int El, int K, const uint8_t* w1q,
+                         const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout,
+                         void* out_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
+                         int32_t* err, void* stream) {
+  RecordSource src{};
+  src.base[0] = records;
+  src.seg_off[0] = 0;
+  src.start[0] = 0;
+  src.start[1] = R;
+  src.W = 1;
+  src.rb = sm_ep_record_bytes(H, K);
+  return ep_expert_forward(src, R, H, I, El, K, w1q, w1_sf, w2q, w2_sf, concat_layout, out_rows, expert_frequency,
+                           workspace, workspace_bytes, err, stream);
+}
+
+int sm_ep_expert_forward_p2p(const void* const* peer_send_bases, const int32_t* seg_off, const int32_t* recv_counts,
+                             int W, int H, int I, int El, int K, const uint8_t* w1q, const uint8_t* w1_sf,
+                             const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout, void* out_rows,
+                             int32_t* expert_frequency, void* workspace, size_t workspace_bytes, int32_t* err,
+                             void* stream) {
+  if (W < 1 || W > kMaxRanks || !peer_send_bases || !seg_off || !recv_counts)
+    return set_last_error(SM_EINVAL, "ep expert p2p: W must be in [1, %d] with W peer bases", kMaxRanks);
+  RecordSource src{};
+  int R = 0;
+  for (int s = 0; s < W; ++s) {
+    if (recv_counts[s] < 0 || seg_off[s] < 0) return set_last_error(SM_EINVAL, "ep expert p2p: negative count");
+    src.base[s] = static_cast<const uint8_t*>(peer_send_bases[s]);
+    src.seg_off[s] = seg_off[s];
+    src.start[s] = R;
+    R += recv_counts[s];
+  }
+  src.start[W] = R;
+  src.W = W;
+  src.rb = sm_ep_record_bytes(H, K);
+  return ep_expert_forward(src, R, H, I, El, K, w1q, w1_sf, w2q, w2_sf, concat_layout, out_rows, expert_frequency,
+                           workspace, workspace_bytes, err, stream);
+}
+
+static int ep_combine(const RowSource& rs, const int32_t* ret_row, int T, int K, int H, void* out, void* stream) {
   if (T < 0 || K < 1 || K > 32 || H <= 0 || H % 8) return set_last_error(SM_EINVAL, "ep combine: bad shape");
   if (T == 0) return SM_OK;
-  ep_combine_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(ret_rows), ret_row, T, K, H, static_cast<__nv_bfloat16*>(out));
+  ep_combine_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(rs, ret_row, T, K, H,
+                                                                      static_cast<__nv_bfloat16*>(out));
   return ep_status(cudaGetLastError(), "ep combine");
 }
+
+int sm_ep_combine(const void* ret_rows, const int32_t* ret_row, int T, int K, int H, void* out, void* stream) {
+  RowSource rs{};
+  rs.base[0] = static_cast<const __nv_bfloat16*>(ret_rows);
+  rs.send_off[0] = 0;
+  rs.send_off[1] = 1 << 30;
+  rs.recv_start[0] = 0;
+  rs.W = 1;
+  return ep_combine(rs, ret_row, T, K, H, out, stream);
+}
+
+int sm_ep_combine_p2p(const void* const* peer_out_bases, const int32_t* send_counts, const int32_t* recv_start,
+                      int W, const int32_t* ret_row, int T, int K, int H, void* out, void* stream) {
+  if (W < 1 || W > kMaxRanks || !peer_out_bases || !send_counts || !recv_start)
+    return set_last_error(SM_EINVAL, "ep combine p2p: W must be in [1, %d] with W peer bases", kMaxRanks);
+  RowSource rs{};
+  int acc = 0;
+  for (int d = 0; d < W; ++d) {
+    rs.base[d] = static_cast<const __nv_bfloat16*>(peer_out_bases[d]);
+    rs.send_off[d] = acc;
+    rs.recv_start[d] = recv_start[d];
+    acc += send_counts[d];
+  }
+  rs.send_off[W] = acc;
+  rs.W = W;
+  return ep_combine(rs, ret_row, T, K, H, out, stream);
+}
+
+// ---- CUDA IPC buffers shared between the ranks of one node (peer loads over NVLink) ----------
+int sm_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return set_last_error(SM_EINVAL, "ipc alloc: bad arguments");
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return ep_status(e, "ipc alloc");
+  e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return ep_status(e, "ipc handle");
+  }
+  return SM_OK;
+}
+
+int sm_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return set_last_error(SM_EINVAL, "ipc open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return ep_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "ipc open");
+}
+
+int sm_ipc_close(void* ptr) { return ep_status(cudaIpcCloseMemHandle(ptr), "ipc close"); }
+
+int sm_ipc_free(void* ptr) { return ep_status(cudaFree(ptr), "ipc free"); }
 
 }  // extern "C"

@@ -385,7 +385,23 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+static int g_sm_reserve = 0;
+
+int gemm_grid_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (n <= 0) n = 148;
+  const int r = g_sm_reserve < n ? g_sm_reserve : n - 1;
+  return n - (r > 0 ? r : 0);
+}
+
 cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st) { return launch_gemm<true>(g, st); }
 cudaError_t launch_moe_down(const GemmArgs& g, cudaStream_t st) { return launch_gemm<false>(g, st); }
 
 }  // namespace smb
+
+extern "C" int sm_set_gemm_sm_reserve(int n) {
+  smb::g_sm_reserve = n < 0 ? 0 : n;
+  return 0;
+}

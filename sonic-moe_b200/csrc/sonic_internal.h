@@ -77,6 +77,10 @@ struct GemmArgs {
   int n_slices;  // set by the launcher
 };
 
+// SMs the persistent GEMMs may occupy: all of the current device's, minus the number reserved with
+// sm_set_gemm_sm_reserve (left free for communication kernels that run at the same time).
+int gemm_grid_sms();
+
 cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st);
 cudaError_t launch_moe_down(const GemmArgs& g, cudaStream_t st);
 

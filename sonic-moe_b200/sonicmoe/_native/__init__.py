@@ -64,6 +64,16 @@ SIGNATURES = {
         [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P, _P],
     ),
     "sm_ep_combine": (_I, [_P, _P, _I, _I, _I, _P, _P]),
+    "sm_set_gemm_sm_reserve": (_I, [_I]),
+    "sm_ep_expert_forward_p2p": (
+        _I,
+        [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P, _P],
+    ),
+    "sm_ep_combine_p2p": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _P, _P]),
+    "sm_ipc_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "sm_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "sm_ipc_close": (_I, [_P]),
+    "sm_ipc_free": (_I, [_P]),
     "sm_route_plan": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "sm_quant_pack": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),

@@ -65,6 +65,51 @@ def test_ep_emulated_ranks(W, T, H, I, E, K):
     assert rel_fro(o_all.float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
 
 
+@pytest.mark.parametrize("W,T,H,I,E,K", [(4, 200, 512, 256, 16, 4), (3, 150, 256, 128, 12, 8)])
+def test_ep_p2p_kernels_emulated_ranks(W, T, H, I, E, K):
+    """The peer-memory stages with W buffers on one GPU: the expert stage reads each source's
+    segment out of that source's send buffer, the combine reads each partial row out of the
+    destination's output rows -- the same address arithmetic the IPC-mapped peers use."""
+    import torch.nn.functional as F
+
+    from sonicmoe.ep import NativeStages
+    from sonicmoe.ops import weight_prep
+
+    x, rw, w1, w2 = make_layer_inputs(W * T, H, I, E, seed=3 * W + T)
+    dev = torch.device("cuda", 0)
+    xg, rwg = x.to(dev), rw.to(dev)
+    El = E // W
+    st = NativeStages()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    rb = st.record_bytes(H, K)
+    send = [torch.empty(T * min(K, W), rb, dtype=torch.uint8, device=dev) for _ in range(W)]
+    outs = [torch.empty(W * T, H, dtype=torch.bfloat16, device=dev) for _ in range(W)]
+    states = []
+    for r in range(W):
+        xr = xg[r * T:(r + 1) * T].contiguous()
+        states.append(st.dispatch(xr, F.linear(xr, rwg), E, K, W, r, True, False, err, records=send[r]))
+    C = [s_.send_counts.cpu().tolist() for s_ in states]
+    freqs = []
+    for d in range(W):
+        w1p = weight_prep(w1[d * El:(d + 1) * El].to(dev))
+        w2p = weight_prep(w2[d * El:(d + 1) * El].to(dev))
+        recv_counts = [C[s_][d] for s_ in range(W)]
+        seg_off = [sum(C[s_][:d]) for s_ in range(W)]
+        freqs.append(st.expert_p2p([b.data_ptr() for b in send], seg_off, recv_counts, H, I, El, K, w1p, w2p,
+                                   outs[d].data_ptr(), err, dev))
+    o_all = []
+    for s_ in range(W):
+        recv_start = [sum(C[q][d] for q in range(s_)) for d in range(W)]
+        o_all.append(st.combine_p2p([o.data_ptr() for o in outs], C[s_], recv_start, states[s_].ret_row, T, K, H, dev))
+    o_all = torch.cat(o_all)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    logits = torch.cat([s_.router_logits for s_ in states]).float().cpu().numpy()
+    o_ref, _, idx = fp8_oracle(x.float().numpy(), logits, w1.float().numpy(), w2.float().numpy(), K)
+    np.testing.assert_array_equal(torch.cat(freqs).cpu().numpy(), np.bincount(idx.reshape(-1), minlength=E))
+    assert rel_fro(o_all.float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -73,7 +118,7 @@ def _free_port():
     return p
 
 
-def _nccl_worker(rank, W, port, q, T, H, I, E, K):
+def _nccl_worker(rank, W, port, q, T, H, I, E, K, transport):
     import datetime
     import sys
 
@@ -94,16 +139,20 @@ def _nccl_worker(rank, W, port, q, T, H, I, E, K):
         x, rw, w1, w2 = mk(W * T, H, I, E, seed=77)
         El = E // W
         moe = ExpertParallelMoE(rw.to(dev), w1[rank * El:(rank + 1) * El].to(dev),
-                                w2[rank * El:(rank + 1) * El].to(dev), E, K)
-        out, logits, freq = moe.forward(x[rank * T:(rank + 1) * T].to(dev))
+                                w2[rank * El:(rank + 1) * El].to(dev), E, K, transport=transport, max_tokens=T,
+                                hidden_size=H)
+        for _ in range(2):  # twice: the shared buffers are reused across forwards
+            out, logits, freq = moe.forward(x[rank * T:(rank + 1) * T].to(dev))
         torch.cuda.synchronize()
         q.put((rank, out.float().cpu().numpy(), logits.float().cpu().numpy(), freq.cpu().numpy()))
+        moe.close()
     finally:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def test_ep_nccl_multi_gpu():
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
+def test_ep_multi_gpu(transport):
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs >= 2 GPUs")
@@ -114,7 +163,7 @@ def test_ep_nccl_multi_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, W, port, q, T, H, I, E, K)) for r in range(W)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, W, port, q, T, H, I, E, K, transport)) for r in range(W)]
     for p in procs:
         p.start()
     res = {}
