@@ -14,7 +14,8 @@ of a tile live in one 512-byte atom.
 """
 import numpy as np
 
-BLOCK_M = 128
+BLOCK_M = 128  # rows of one block of the padded layout
+PAD_M = 128  # experts are padded to multiples of this
 
 
 def tc_metadata(topk_indices, E: int):
@@ -50,12 +51,13 @@ def general_metadata(sorted_token_idx, expert_idx, T: int, E: int):
 
 
 def padded_layout(freq):
-    """Per-expert 128-row padded offsets.
+    """Padded expert-major layout: every expert's rows start on a 128-row block and are padded to a
+    multiple of PAD_M rows (so an expert always owns whole pairs of blocks).
 
     Returns (off_pad [E+1] int32 in rows, blk_expert [n_blocks] int32, n_blocks).
     """
     freq = np.asarray(freq).astype(np.int64)
-    nblk = (freq + BLOCK_M - 1) // BLOCK_M
+    nblk = (freq + PAD_M - 1) // PAD_M * (PAD_M // BLOCK_M)
     blk_off = np.zeros(len(freq) + 1, dtype=np.int64)
     blk_off[1:] = np.cumsum(nblk)
     blk_expert = np.repeat(np.arange(len(freq), dtype=np.int32), nblk)

@@ -68,7 +68,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-
 // Bounded wait for the phase with the given parity.  Returns false (and records `where` in the
 // global error word) after kWaitTimeoutNs, or as soon as another thread or CTA has recorded an
 // error, so that every role of every CTA leaves its loops instead of spinning forever.
@@ -98,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, uin
 }
 
 // --------------------------------------------------------------------------------------------
-// TMA (tiled, no multicast) and bulk copies, completing on an mbarrier
+// TMA (tiled, one destination CTA) and bulk copies, completing on an mbarrier
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             uint64_t policy) {
   asm volatile(
@@ -106,6 +105,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
       : "memory");
+}
+// Tiled store shared -> global (bulk async-group of the issuing thread; coordinates >= 0).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
 }
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

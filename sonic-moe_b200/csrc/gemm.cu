@@ -38,8 +38,11 @@ constexpr int kSfaBytes = kSfAtomBytes;
 constexpr int kSfbBytes = 2 * kSfAtomBytes;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemAcc = 0, kTmemSfa = 256, kTmemSfb = 260;
-constexpr int kNumBars = 2 * 4 + 4;  // full/empty per stage (at most 4 stages) + 4
+constexpr int kNumBars = 2 * 4 + 5;  // full/empty per stage (at most 4 stages) + 5
 constexpr int kRowChunkBytes = 128;  // down epilogue: one thread's 64 bf16 of one output row
+// Staging slots are 144 bytes apart: a warp's 32 slots then start in 8 different 16-byte bank
+// groups, so its 16-byte stores are 4-way (the minimum for 512 bytes) instead of 32-way conflicted.
+constexpr int kSlotStride = 144;
 
 // Shared-memory layout per epilogue kind.  The up projection keeps a 4-stage ring; the down
 // projection gives one stage up for 64 KB of per-thread staging from which its output rows are
@@ -52,7 +55,8 @@ struct GemmSmem {
   static constexpr int kOffSfa = kOffB + kStages * kBBytes;
   static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
   static constexpr int kOffStage = kOffSfb + kStages * kSfbBytes;
-  static constexpr int kStageBytes = kUp ? 0 : kEpiWarps * 32 * kRowChunkBytes;
+  // up: one 128 x 128-byte e4m3 output tile (128B-swizzled, TMA-stored); down: per-thread slots
+  static constexpr int kStageBytes = kUp ? kBlockM * 128 : kEpiWarps * 32 * kSlotStride;
   static constexpr int kOffBar = kOffStage + kStageBytes;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAmax = (kOffTmemHolder + 4 + 15) / 16 * 16;
@@ -60,7 +64,7 @@ struct GemmSmem {
   static constexpr int kBytes = kOffAmax + kAmaxFloats * 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
   static_assert(kAlloc <= 232448, "shared memory budget");
-  static_assert(kOffStage % 128 == 0, "staging alignment");
+  static_assert(kOffStage % (kUp ? 1024 : 128) == 0, "staging alignment (128B-swizzled TMA store for up)");
 };
 
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
@@ -82,10 +86,124 @@ __device__ __forceinline__ void tile_coords(int tile, int n_blocks, int ntn, int
   nt = slice * nts + (r - mb * nts);
 }
 
+// What one epilogue thread needs to know about its row of a tile: the dependent loads block ->
+// expert -> offsets -> scatter index -> score, issued after the accumulator has been released.
+struct RowMeta {
+  int mb, nt, e;
+  int p;      // padded row
+  int valid;  // a real (token, expert) entry, not padding
+  int tok;    // down: token whose output row receives the reduction
+  float sc;   // down: its router score
+};
+
+template <bool kUp>
+__device__ __forceinline__ RowMeta load_row_meta(const GemmArgs& g, int tile, int n_blocks, int ntn, int r) {
+  RowMeta m;
+  tile_coords(tile, n_blocks, ntn, g.n_slices, m.mb, m.nt);
+  m.e = g.blk_expert[m.mb];
+  m.p = m.mb * kBlockM + r;
+  const int rel = m.p - g.off_pad[m.e];
+  m.valid = rel < g.freq[m.e];
+  m.tok = 0;
+  m.sc = 0.0f;
+  if constexpr (!kUp) {
+    if (m.valid) {
+      const int rs = rel + g.off[m.e];
+      m.tok = g.x_gather[rs];
+      m.sc = g.scores[g.s_scatter[rs]];
+    }
+  }
+  return m;
+}
+
+// Epilogue of one accumulator tile: this thread holds row r (0..127) of the tile's 128-row block,
+// output columns [64 cc, 64 cc + 64) of its n-tile in v (f32 bits).  Returns false if a bounded
+// wait gave up.
+//   up   : a = silu(gate) * up over the thread's 32 SwiGLU outputs, the row's amax over the 128
+//          outputs of the tile (four threads, exchanged through shared memory), 1x128 requant.
+//   down : scale by the entry's router score, stage 128 bytes of bf16 in this thread's slot and
+//          bulk-reduce them into the token's output row.
+template <bool kUp>
+__device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const uint32_t (&v)[64], const RowMeta& m, int r,
+                                              int cc, int ew, int lane, int tcount, float* s_amax, uint64_t* amax_bar,
+                                              uint64_t* store_bar, uint8_t* sStage, const CUtensorMap* tmap_out,
+                                              uint64_t pol_out) {
+  const bool valid = m.valid != 0;
+  const int p = m.p, mb = m.mb, nt = m.nt;
+  if constexpr (kUp) {
+    float o[32];
+    float am = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float gt = __uint_as_float(g.concat ? v[j] : v[2 * j]);
+      const float up = __uint_as_float(g.concat ? v[32 + j] : v[2 * j + 1]);
+      o[j] = valid ? silu_f(gt) * up : 0.0f;
+      am = fmaxf(am, fabsf(o[j]));
+    }
+    float* amax_buf = s_amax + (tcount & 1) * (4 * kBlockM);
+    amax_buf[cc * kBlockM + r] = am;
+    // the store issuer first makes sure the previous tile's TMA store has read the staging tile;
+    // nobody writes the staging tile before this barrier completes
+    if (ew == 0 && lane == 0) bulk_wait_read0();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(amax_bar);
+    if (!mbar_wait(amax_bar, tcount & 1, g.err, kErrTimeoutEpilogue)) return false;
+    am = fmaxf(fmaxf(amax_buf[r], amax_buf[kBlockM + r]), fmaxf(amax_buf[2 * kBlockM + r], amax_buf[3 * kBlockM + r]));
+    const int e8 = scale_exp_of_amax(am);
+    const float inv = exp2_neg(e8);
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      w[i] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(o[4 * i], inv), __fmul_rn(o[4 * i + 1], inv))) |
+             (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(o[4 * i + 2], inv), __fmul_rn(o[4 * i + 3], inv))) << 16);
+    }
+    const int I2 = g.N / 2;
+    // row r of the staging tile, 16-byte chunks 2cc and 2cc+1 at their 128B-swizzled positions
+    uint8_t* srow = sStage + r * 128;
+    *reinterpret_cast<uint4*>(srow + (((2 * cc) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(srow + (((2 * cc + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(store_bar);
+    if (ew == 0 && lane == 0) {
+      if (!mbar_wait(store_bar, tcount & 1, g.err, kErrTimeoutEpilogue)) return false;
+      tma_store_2d(tmap_out, sStage, nt * kBlockM, mb * kBlockM);
+      bulk_commit();
+    }
+    if (cc == 0) {
+      const int KG2 = (I2 / kBlockK + 3) / 4;
+      g.out_sf[(static_cast<size_t>(mb) * KG2 + nt / 4) * kSfAtomBytes + 16 * (r % 32) + 4 * (r / 32) + (nt % 4)] =
+          static_cast<uint8_t>(e8 + 127);
+    }
+  } else {
+    // The slot is reused only after the previous bulk reduction has finished reading it.
+    uint8_t* slot = sStage + (ew * 32 + lane) * kSlotStride;
+    bulk_wait_read0();
+    if (valid) {
+      const float sc = m.sc;
+#pragma unroll
+      for (int j = 0; j < 64; j += 8) {
+        uint4 w;
+        w.x = pack_bf16x2(sc * __uint_as_float(v[j]), sc * __uint_as_float(v[j + 1]));
+        w.y = pack_bf16x2(sc * __uint_as_float(v[j + 2]), sc * __uint_as_float(v[j + 3]));
+        w.z = pack_bf16x2(sc * __uint_as_float(v[j + 4]), sc * __uint_as_float(v[j + 5]));
+        w.w = pack_bf16x2(sc * __uint_as_float(v[j + 6]), sc * __uint_as_float(v[j + 7]));
+        *reinterpret_cast<uint4*>(slot + 2 * j) = w;
+      }
+      fence_proxy_async_smem();
+      __nv_bfloat16* dst =
+          static_cast<__nv_bfloat16*>(g.out_bf16) + static_cast<size_t>(m.tok) * g.N + nt * kBN + cc * 64;
+      bulk_reduce_add_bf16(dst, slot, kRowChunkBytes, pol_out);
+      bulk_commit();
+    }
+  }
+  return true;
+}
+
 template <bool kUp>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                    const GemmArgs g) {
+                    const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g) {
   using L = GemmSmem<kUp>;
   constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -102,7 +220,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tmem_full = bars + 2 * kStages;
   uint64_t* tmem_empty = tmem_full + 1;
   uint64_t* drain = tmem_full + 2;
-  uint64_t* amax_bar = tmem_full + 3;  // all epilogue threads: row amax partials written
+  uint64_t* amax_bar = tmem_full + 3;   // up: every epilogue warp has written its row amax partials
+  uint64_t* store_bar = tmem_full + 4;  // up: every epilogue warp has written its part of the output tile
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kOffTmemHolder);
   float* s_amax = reinterpret_cast<float*>(smem + L::kOffAmax);
 
@@ -117,10 +236,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(tmem_full, 1);
     mbar_init(tmem_empty, kEpiWarps);
     mbar_init(drain, 1);
-    mbar_init(amax_bar, kEpiWarps * 32);
+    mbar_init(amax_bar, kEpiWarps);
+    mbar_init(store_bar, kEpiWarps);
     fence_mbar_init();
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
+    if (kUp) prefetch_tmap(&tmap_out);
   }
   if (warp == 2) {
     tmem_alloc(tmem_holder, kTmemCols);
@@ -232,9 +353,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int tcount = 0;
     const uint64_t pol_out = policy_evict_last();
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tcount) {
-      int mb, nt;
-      tile_coords(tile, n_blocks, ntn, g.n_slices, mb, nt);
-      const int e = g.blk_expert[mb];
       if (!mbar_wait(tmem_full, tcount & 1, g.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       uint32_t v[64];
@@ -250,72 +368,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tmem_empty);
 
-      const int p = mb * kBlockM + r;
-      const int rel = p - g.off_pad[e];
-      const bool valid = rel < g.freq[e];
-      if constexpr (kUp) {
-        float o[32];
-        float am = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float gt = __uint_as_float(g.concat ? v[j] : v[2 * j]);
-          const float up = __uint_as_float(g.concat ? v[32 + j] : v[2 * j + 1]);
-          o[j] = valid ? silu_f(gt) * up : 0.0f;
-          am = fmaxf(am, fabsf(o[j]));
-        }
-        float* amax_buf = s_amax + (tcount & 1) * (4 * kBlockM);
-        amax_buf[cc * kBlockM + r] = am;
-        mbar_arrive(amax_bar);
-        if (!mbar_wait(amax_bar, tcount & 1, g.err, kErrTimeoutEpilogue)) break;
-        am = fmaxf(fmaxf(amax_buf[r], amax_buf[kBlockM + r]), fmaxf(amax_buf[2 * kBlockM + r], amax_buf[3 * kBlockM + r]));
-        const int e8 = scale_exp_of_amax(am);
-        const float inv = exp2_neg(e8);
-        uint32_t w[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          w[i] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(o[4 * i], inv), __fmul_rn(o[4 * i + 1], inv))) |
-                 (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(o[4 * i + 2], inv), __fmul_rn(o[4 * i + 3], inv)))
-                  << 16);
-        }
-        const int I2 = g.N / 2;
-        uint8_t* dst = g.out_q + static_cast<size_t>(p) * I2 + nt * kBlockM + cc * 32;
-        reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        if (cc == 0) {
-          const int KG2 = (I2 / kBlockK + 3) / 4;
-          g.out_sf[(static_cast<size_t>(mb) * KG2 + nt / 4) * kSfAtomBytes + 16 * (r % 32) + 4 * (r / 32) + (nt % 4)] =
-              static_cast<uint8_t>(e8 + 127);
-        }
-      } else {
-        // Scale the row chunk, stage it in this thread's own 128 bytes of shared memory and let
-        // the TMA unit add it into the token's output row (one line-sized bulk reduction instead
-        // of eight 16-byte vector atomics).  The slot is reused only after the previous bulk
-        // reduction has finished reading it.
-        uint8_t* slot = sStage + (ew * 32 + lane) * kRowChunkBytes;
-        bulk_wait_read0();
-        if (valid) {
-          const int rs = rel + g.off[e];
-          const int f = g.s_scatter[rs];
-          const int tok = g.x_gather[rs];
-          const float sc = g.scores[f];
-#pragma unroll
-          for (int j = 0; j < 64; j += 8) {
-            uint4 w;
-            w.x = pack_bf16x2(sc * __uint_as_float(v[j]), sc * __uint_as_float(v[j + 1]));
-            w.y = pack_bf16x2(sc * __uint_as_float(v[j + 2]), sc * __uint_as_float(v[j + 3]));
-            w.z = pack_bf16x2(sc * __uint_as_float(v[j + 4]), sc * __uint_as_float(v[j + 5]));
-            w.w = pack_bf16x2(sc * __uint_as_float(v[j + 6]), sc * __uint_as_float(v[j + 7]));
-            *reinterpret_cast<uint4*>(slot + 2 * j) = w;
-          }
-          fence_proxy_async_smem();
-          __nv_bfloat16* dst =
-              static_cast<__nv_bfloat16*>(g.out_bf16) + static_cast<size_t>(tok) * g.N + nt * kBN + cc * 64;
-          bulk_reduce_add_bf16(dst, slot, kRowChunkBytes, pol_out);
-          bulk_commit();
-        }
-      }
+      // the accumulator is released: the row's metadata loads overlap the next tile's main loop
+      const RowMeta meta = load_row_meta<kUp>(g, tile, n_blocks, ntn, r);
+      if (!epilogue_tile<kUp>(g, v, meta, r, cc, ew, lane, tcount, s_amax, amax_bar, store_bar, sStage, &tmap_out,
+                              pol_out))
+        break;
     }
-    if constexpr (!kUp) bulk_wait_all();
+    bulk_wait_all();  // outstanding reductions / output stores have finished with shared memory
   }
   __syncthreads();
   if (warp == 2) {
@@ -355,6 +414,18 @@ static bool make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Column slices of the down projection: the largest slice whose bf16 output slab (tokens x slice
+// columns) fits the L2 budget, so the reductions of one slice land in L2.
+static int down_slices(const GemmArgs& g) {
+  const int ntn = g.N / kBN;
+  long long budget = 80ll << 20;
+  if (const char* env = getenv("SONIC_B200_DOWN_SLAB_MB")) budget = atoll(env) << 20;
+  int slices = 1;
+  while (slices < ntn && static_cast<long long>(g.tokens) * (g.N / slices) * 2 > budget && ntn % (slices * 2) == 0)
+    slices *= 2;
+  return slices;
+}
+
 template <bool kUp>
 static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
   const long long max_blocks = g.a_rows / kBlockM;
@@ -363,6 +434,9 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, g.a, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.Kd), kBlockM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tb, g.b, static_cast<uint64_t>(g.E) * g.N, static_cast<uint64_t>(g.Kd), kBN)) return cudaErrorInvalidValue;
+  CUtensorMap to = ta;  // the down projection has no tiled output
+  if (kUp && !make_tmap(&to, g.out_q, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.N / 2), kBlockM))
+    return cudaErrorInvalidValue;
   auto kern = moe_gemm_kernel<kUp>;
   constexpr int kSmemAlloc = GemmSmem<kUp>::kAlloc;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
@@ -370,18 +444,8 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
   const int grid = static_cast<int>(max_tiles < g.num_sms ? max_tiles : g.num_sms);
   GemmArgs ga = g;
   ga.n_slices = 1;
-  if (!kUp) {
-    // Largest column slice whose bf16 output slab (tokens x slice) fits the L2 budget.
-    const int ntn = g.N / kBN;
-    long long budget = 160ll << 20;
-    if (const char* env = getenv("SONIC_B200_DOWN_SLAB_MB")) budget = atoll(env) << 20;
-    int slices = 1;
-    while (slices < ntn && static_cast<long long>(g.tokens) * (g.N / slices) * 2 > budget &&
-           ntn % (slices * 2) == 0)
-      slices *= 2;
-    ga.n_slices = slices;
-  }
-  kern<<<grid, kGemmThreads, kSmemAlloc, st>>>(ta, tb, ga);
+  if (!kUp) ga.n_slices = down_slices(g);
+  kern<<<grid, kGemmThreads, kSmemAlloc, st>>>(ta, tb, to, ga);
   return cudaGetLastError();
 }
 

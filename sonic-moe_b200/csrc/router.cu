@@ -292,14 +292,14 @@ __global__ void __launch_bounds__(kScanThreads)
     }
   }
   __syncthreads();
-  // (2) exclusive scans over experts of freq and of ceil(freq / 128); each thread owns a
+  // (2) exclusive scans over experts of freq and of the padded block counts; each thread owns a
   // contiguous chunk of experts
   const int per = (E + kScanThreads - 1) / kScanThreads;
   const int e0 = threadIdx.x * per;
   int a = 0, b = 0;
   for (int e = e0; e < min(E, e0 + per); ++e) {
     a += s_freq[e];
-    b += (s_freq[e] + kBlockM - 1) / kBlockM;
+    b += padded_blocks_of(s_freq[e]);
   }
   int ia = a, ib = b;
 #pragma unroll
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(kScanThreads)
   int rb = ib - b + (warp > 0 ? s_wsum[1][warp - 1] : 0);
   for (int e = e0; e < min(E, e0 + per); ++e) {
     const int f = s_freq[e];
-    const int nb = (f + kBlockM - 1) / kBlockM;
+    const int nb = padded_blocks_of(f);
     off[e] = ra;
     off_pad[e] = rb * kBlockM;
     for (int k = 0; k < nb; ++k) blk_expert[rb + k] = e;

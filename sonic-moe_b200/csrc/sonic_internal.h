@@ -9,7 +9,9 @@
 namespace smb {
 
 constexpr int kTileTokens = 128;  // tokens per routing tile (router histogram / scatter)
-constexpr int kBlockM = 128;      // GEMM tile height; experts are padded to multiples of it
+constexpr int kBlockM = 128;      // rows of one block of the padded layout (one CTA's GEMM rows)
+constexpr int kPadRows = 128;     // experts are padded to multiples of this
+constexpr int kBlocksPerPad = kPadRows / kBlockM;
 constexpr int kBlockK = 128;      // K extent of one pipeline stage (= one scale-factor group)
 constexpr int kSfAtomBytes = 512; // 128 rows x 4 K-blocks of UE8M0 scale factors
 
@@ -20,10 +22,14 @@ int set_last_error(int code, const char* fmt, ...);
 
 inline int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
-// Upper bound on the number of 128-row blocks of the padded expert layout.
+// Blocks of 128 rows that an expert with f rows occupies in the padded layout (always even).
+__host__ __device__ inline int padded_blocks_of(int f) { return kBlocksPerPad * ((f + kPadRows - 1) / kPadRows); }
+
+// Upper bound on the number of 128-row blocks of the padded expert layout: each non-empty expert
+// adds fewer than kBlocksPerPad blocks of padding.
 inline int max_padded_blocks(long long TK, int E) {
   const long long nonempty = TK < E ? TK : E;
-  return static_cast<int>((TK + kBlockM - 1) / kBlockM + nonempty);
+  return static_cast<int>((TK + kBlockM - 1) / kBlockM + kBlocksPerPad * nonempty);
 }
 
 cudaError_t launch_router_topk(const void* logits, int dtype, int T, int E, int K, int sot, int renorm,
