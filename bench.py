@@ -169,19 +169,24 @@ def run_ep(args, rank, world, local_rank):
     t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = t.item() / args.steps
-    # end to end through the public API with pinned host buffers
+    # end to end through the public API with pinned host buffers (copies overlapped with the
+    # forward on their own streams, as in the 1-GPU e2e leg)
+    from sonicmoe.pipeline import OverlappedHostRunner
+
     x_host = x.cpu().pin_memory()
     o_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x)
+    runner = OverlappedHostRunner(lambda xd: moe.forward(xd)[0], (T, H), x.dtype, dev, depth=2)
     steps_e2e = max(3, min(args.steps, 10))
+    for _ in range(2):
+        runner.submit(x_host, o_host)
+    runner.drain()
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps_e2e):
-        xd.copy_(x_host, non_blocking=True)
-        o, _, _ = moe.forward(xd)
-        o_host.copy_(o, non_blocking=True)
+        runner.submit(x_host, o_host)
+    runner.drain()
     e1.record()
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) / steps_e2e], device=dev)
@@ -355,33 +360,40 @@ def time_gemm_stages(x, rw, w1p, w2p, K, reps):
 
 
 def time_e2e(x, rw, w1, w2, K, dev, steps):
+    """Public-API forward on batches that live in pinned host memory: every step copies its input
+    host->device and its output device->host inside the timed region.  The copies run on their own
+    streams (sonicmoe.pipeline.OverlappedHostRunner), so step i+1's input copy and step i-1's
+    output copy overlap step i's forward."""
     import torch
 
     from sonicmoe.functional import moe_TC_softmax_topk_layer
+    from sonicmoe.pipeline import OverlappedHostRunner
 
     T, H = x.shape
     x_host = x.cpu().pin_memory()
     o_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
     w1v, w2v = w1.permute(1, 2, 0), w2.permute(1, 2, 0)
-    xd = torch.empty_like(x)
 
-    def step():
-        xd.copy_(x_host, non_blocking=True)
+    def fwd(xd):
         o, _, _ = moe_TC_softmax_topk_layer(xd, rw, w1v, None, w2v, None, K, None, is_inference_mode_enabled=True)
-        o_host.copy_(o, non_blocking=True)
+        return o
 
-    for _ in range(2):
-        step()
+    runner = OverlappedHostRunner(fwd, (T, H), x.dtype, dev, depth=2)
+    for _ in range(3):
+        runner.submit(x_host, o_host)
+    runner.drain()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(steps):
-        step()
+        runner.submit(x_host, o_host)
+    runner.drain()
     ev1.record()
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / steps
     nbytes = x.numel() * x.element_size()
-    return {"ms_step": ms, "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": T * H * 2}
+    return {"ms_step": ms, "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": T * H * 2,
+            "overlap": "H2D / forward / D2H on three streams, 2 batches in flight"}
 
 
 def cpu_reference(T_sample, reps, threads=None, weights=None):
