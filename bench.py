@@ -429,6 +429,92 @@ def cpu_reference(T_sample, reps, threads=None, weights=None):
     return T / sec, cores, sample, sec
 
 
+SIDE_WORKLOADS = {
+    # name: (T, H, I, E, K, description)
+    "c3": (16384, 2048, 768, 128, 8, "config 3 (Qwen3-style): top-k over softmax + renorm, concatenated w1"),
+    "c5_64": (64, 4096, 1536, 128, 8, "config 5 (decode, T=64): Zipf(1.2) routing via moe_general_routing_inputs"),
+    "c5_512": (512, 4096, 1536, 128, 8, "config 5 (decode, T=512): Zipf(1.2) routing via moe_general_routing_inputs"),
+}
+
+
+def run_side_workload(args):
+    """One of the benchmark's other configurations on one GPU (not the headline line): the public
+    functional call replayed from a CUDA graph.  Config 3 is tensor-bound (TFLOP/s against the
+    measured FP8 peak); decode is bound by the expert weight bytes it streams (GB/s against the
+    measured HBM copy bandwidth)."""
+    import numpy as np
+    import torch
+
+    from sonicmoe import ops
+    from sonicmoe.functional import moe_general_routing_inputs, moe_TC_softmax_topk_layer
+
+    T, H, I, E, K, desc = SIDE_WORKLOADS[args.workload]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1111)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w1 = (torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w1v, w2v = w1.permute(1, 2, 0), w2.permute(1, 2, 0)
+    if args.workload == "c3":
+        def forward():
+            moe_TC_softmax_topk_layer(x, rw, w1v, None, w2v, None, K, None, is_inference_mode_enabled=True,
+                                      is_softmax_over_topk=False, norm_topk_probs=True, concat_layout=True)
+        active = E
+    else:
+        rs = np.random.RandomState(1111)
+        rank = np.empty(E)
+        rank[rs.permutation(E)] = np.arange(1, E + 1)
+        p = rank ** -1.2
+        logits = torch.from_numpy((rs.randn(T, E) + np.log(p / p.sum())).astype(np.float32)).to(dev)
+        scores, idx = ops.router_topk(logits, K)  # routed once, outside the timed region
+        active = int((torch.bincount(idx.reshape(-1).long(), minlength=E) > 0).sum().item())
+        sc = scores.reshape(-1).contiguous()
+        tok = torch.arange(T, dtype=torch.int32, device=dev).repeat_interleave(K)
+        ex = idx.reshape(-1).to(torch.int32).contiguous()
+
+        def forward():
+            moe_general_routing_inputs(x, sc, tok, ex, w1v, None, w2v, None, E, None, is_inference_mode_enabled=True)
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            forward()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            forward()
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    peaks, src = measured_peaks()
+    line = {"workload": desc, "T": T, "H": H, "I": I, "E": E, "K": K, "ms_step": ms, "tokens_per_s": T / (ms / 1e3),
+            "steps": args.steps, "clocks": clk.summary()}
+    if args.workload == "c3":
+        tf = flops_fwd(T, H, I, K) / (ms / 1e3) / 1e12
+        line["roofline"] = {"bound": "tensor", "achieved": tf, "peak": 2 * peaks["bf16_tflops"], "unit": "TFLOP/s",
+                            "frac": tf / (2 * peaks["bf16_tflops"]), "peak_source": src}
+    else:
+        # e4m3 weights of the experts the batch touches, plus their 128x128 scale bytes
+        wbytes = active * (3 * H * I + 3 * H * I // (128 * 128))
+        gbs = wbytes / (ms / 1e3) / 1e9
+        line["active_experts"] = active
+        line["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                            "frac": gbs / peaks["hbm_gbs"], "traffic_basis": "expert weight bytes per forward",
+                            "peak_source": src}
+    del graph
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -437,6 +523,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=CFG["T"], help="tokens per GPU (profiling of smaller cases)")
+    ap.add_argument("--workload", choices=["c2"] + sorted(SIDE_WORKLOADS), default="c2",
+                    help="c2 = the headline configuration (default, the contract line); the others time the "
+                         "benchmark's remaining configurations on one GPU")
     ap.add_argument("--profile", action="store_true",
                     help="only run warmup + steps eager forwards (no graph, baselines or extra timing), "
                          "for ncu captures; prints nothing")
@@ -444,6 +533,9 @@ def main():
     CFG["T"] = args.tokens
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload != "c2":
+        run_side_workload(args)
+        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))

@@ -18,6 +18,10 @@
 ``fp8_oracle``  -- ``expert_loop`` on fake-quantised operands: x dequantised from its 1x128 e4m3
     groups, w1/w2 from their 128x128 blocks, the SwiGLU output re-quantised 1x128 and dequantised
     before the down projection (the "reference FP8 path" the north star's 1e-2 bound refers to).
+
+``fp8_oracle_rows``  -- the same math for a subset of tokens, given their routing, quantising only
+    the experts they touch: the check at full configuration sizes, where the whole layer on the
+    CPU would take hours.
 """
 import numpy as np
 import torch
@@ -151,6 +155,39 @@ def fp8_general_oracle(x, router_scores, token_idx, expert_idx, w1, w2, concat_l
         aq, as_ = quant.quant_1x128(a.float().numpy())
         ad = torch.as_tensor(quant.dequant_1x128(aq, as_)).double()
         o.index_add_(0, tok[sel], (ad @ w2t[e].T) * sc[sel, None])
+    return o
+
+
+def fp8_oracle_rows(x_rows, scores_rows, idx_rows, expert_weights, concat_layout=False):
+    """Fake-quantised FP8 layer output [n, H] (float64) of n tokens.
+
+    x_rows: [n, H] activations (bf16 values as float32); scores_rows / idx_rows: [n, K] routing of
+    those tokens (K may be ragged by padding idx with -1); expert_weights(e) -> (w1_e [2I, H],
+    w2_e [H, I]) float32 in the caller's layout.  Each touched expert is quantised once with the
+    same 128x128 blocks as the whole-layer oracle, so per row the result equals ``fp8_oracle``'s.
+    """
+    x_rows = np.asarray(x_rows, dtype=np.float32)
+    idx_rows = np.asarray(idx_rows)
+    scores_rows = np.asarray(scores_rows, dtype=np.float32)
+    xq, xs = quant.quant_1x128(x_rows)
+    xt = torch.as_tensor(quant.dequant_1x128(xq, xs)).double()
+    n, H = x_rows.shape
+    o = torch.zeros((n, H), dtype=torch.float64)
+    for e in np.unique(idx_rows[idx_rows >= 0]):
+        w1e, w2e = expert_weights(int(e))
+        w1e = np.asarray(w1e, dtype=np.float32)[None]
+        w2e = np.asarray(w2e, dtype=np.float32)[None]
+        w1t = torch.as_tensor(quant.dequant_128x128(*quant.quant_128x128(w1e))[0]).double()
+        w2t = torch.as_tensor(quant.dequant_128x128(*quant.quant_128x128(w2e))[0]).double()
+        I = w1t.shape[0] // 2
+        t_idx, k_idx = np.nonzero(idx_rows == e)
+        t_idx = torch.as_tensor(t_idx).long()
+        h = xt[t_idx] @ w1t.T
+        a = F.silu(h[:, :I]) * h[:, I:] if concat_layout else swiglu_interleaved(h)
+        aq, as_ = quant.quant_1x128(a.float().numpy())
+        ad = torch.as_tensor(quant.dequant_1x128(aq, as_)).double()
+        sc = torch.as_tensor(scores_rows[t_idx.numpy(), k_idx]).double()
+        o.index_add_(0, t_idx, (ad @ w2t.T) * sc[:, None])
     return o
 
 

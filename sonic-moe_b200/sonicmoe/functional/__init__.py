@@ -19,7 +19,7 @@ Differences from the reference, all explicit errors: biases and activations othe
 raise ``NotImplementedError`` (the FP8 engine implements the bias-free SwiGLU layer); the forward
 is inference-only (no autograd graph is recorded).
 """
-from collections import OrderedDict
+import weakref
 
 import torch
 import torch.nn.functional as F
@@ -37,8 +37,18 @@ __all__ = [
     "Fp8ExpertWeights",
 ]
 
-_WEIGHT_CACHE: "OrderedDict[tuple, Fp8ExpertWeights]" = OrderedDict()
-_WEIGHT_CACHE_SIZE = 8
+# Prepared FP8 weights, per tensor that owns the weight's storage (the root of its view chain):
+# id(owner) -> (weak reference to owner, {layout: (state, prepared)}).  An entry is dropped when its
+# tensor is freed, so a new weight tensor that happens to be allocated at a freed one's address can
+# never see the old tensor's FP8 copy.  (Tensors cannot be weak dictionary keys: their == is
+# elementwise.)
+_WEIGHT_CACHE: dict = {}
+
+
+def _forget(key: int, ref) -> None:
+    entry = _WEIGHT_CACHE.get(key)
+    if entry is not None and entry[0] is ref:
+        del _WEIGHT_CACHE[key]
 
 
 def _as_expert_major(w: torch.Tensor) -> torch.Tensor:
@@ -46,24 +56,38 @@ def _as_expert_major(w: torch.Tensor) -> torch.Tensor:
     return w.permute(2, 0, 1)
 
 
+def _storage_owner(t: torch.Tensor) -> torch.Tensor:
+    while t._base is not None:
+        t = t._base
+    return t
+
+
 def prepare_fp8_weights(w, concat_glu: bool = False) -> Fp8ExpertWeights:
     """e4m3 + 128x128 UE8M0 version of an expert weight given in the reference's (N, K, E) view.
 
-    Cached on (storage pointer, version counter, shape, strides, layout), so repeated forwards with
-    unchanged weights quantise once.
+    Cached on the tensor that owns the weight's storage, for its current (data pointer, version
+    counter, shape, strides, layout): repeated forwards with unchanged weights quantise once, an
+    in-place update or a storage swap re-quantises, and the entry is dropped with the tensor.
     """
     if isinstance(w, Fp8ExpertWeights):
         return w
-    key = (w.data_ptr(), w._version, tuple(w.shape), tuple(w.stride()), bool(concat_glu), w.dtype)
-    hit = _WEIGHT_CACHE.get(key)
-    if hit is not None:
-        _WEIGHT_CACHE.move_to_end(key)
-        return hit
+    owner = _storage_owner(w)
+    layout = (tuple(w.shape), tuple(w.stride()), bool(concat_glu), w.dtype)
+    state = (w.data_ptr(), w._version)
+    entry = _WEIGHT_CACHE.get(id(owner))
+    per_owner = entry[1] if entry is not None and entry[0]() is owner else None
+    if per_owner is not None:
+        hit = per_owner.get(layout)
+        if hit is not None and hit[0] == state:
+            return hit[1]
     with torch.no_grad():
         prepared = ops.weight_prep(_as_expert_major(w.detach()), concat_glu=concat_glu)
-    _WEIGHT_CACHE[key] = prepared
-    while len(_WEIGHT_CACHE) > _WEIGHT_CACHE_SIZE:
-        _WEIGHT_CACHE.popitem(last=False)
+    if per_owner is None:
+        key = id(owner)
+        ref = weakref.ref(owner, lambda r, k=key: _forget(k, r))
+        per_owner = {}
+        _WEIGHT_CACHE[key] = (ref, per_owner)
+    per_owner[layout] = (state, prepared)  # only the newest version of each layout is kept
     return prepared
 
 

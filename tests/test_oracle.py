@@ -214,3 +214,19 @@ def test_fp8_oracle_close_to_dense():
     od = layer.expert_loop(x, w1, w2, sc, idx, concat_layout=False)
     err = layer.rel_fro(o8, od)
     assert 0.0 < err < 0.15
+
+
+def test_fp8_oracle_rows_matches_whole_layer_oracle():
+    """The per-token oracle used at full configuration sizes equals the whole-layer oracle on the
+    rows it computes (interleaved and concatenated w1)."""
+    rs = np.random.RandomState(11)
+    T, H, I, E, K = 24, 256, 128, 6, 3
+    x = rs.randn(T, H).astype(np.float32)
+    logits = rs.randn(T, E).astype(np.float32)
+    w1 = (rs.randn(E, 2 * I, H) * 0.02).astype(np.float32)
+    w2 = (rs.randn(E, H, I) * 0.02).astype(np.float32)
+    for concat in (False, True):
+        o, scores, idx = layer.fp8_oracle(x, logits, w1, w2, K, concat_layout=concat)
+        rows = np.array([0, 5, 17, 23])
+        sub = layer.fp8_oracle_rows(x[rows], scores[rows], idx[rows], lambda e: (w1[e], w2[e]), concat)
+        np.testing.assert_allclose(sub.numpy(), o.numpy()[rows], rtol=1e-12, atol=1e-12)
