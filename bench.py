@@ -153,7 +153,8 @@ def run_ep(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
     x, rw, w1p, w2p = build_ep_workload(dev, rank, world, T, H, I, E, K)
-    moe = ExpertParallelMoE(rw, w1p, w2p, E, K, max_tokens=T, hidden_size=H)
+    moe = ExpertParallelMoE(rw, w1p, w2p, E, K, max_tokens=T, hidden_size=H, chunks=args.ep_chunks,
+                            reserve_sms=args.ep_reserve_sms, transport=args.ep_transport)
     for _ in range(args.warmup):
         moe.forward(x)
     torch.cuda.synchronize()
@@ -523,6 +524,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=CFG["T"], help="tokens per GPU (profiling of smaller cases)")
+    ap.add_argument("--ep-transport", choices=["p2p", "copy", "nccl"], default=None,
+                    help="N>1: expert-parallel transport (default: the layer's)")
+    ap.add_argument("--ep-chunks", type=int, default=None,
+                    help="N>1: token chunks of the pipelined expert-parallel forward (default: the layer's)")
+    ap.add_argument("--ep-reserve-sms", type=int, default=None,
+                    help="N>1: SMs the GEMMs leave to the overlapped dispatch/combine (default: the layer's)")
     ap.add_argument("--workload", choices=["c2"] + sorted(SIDE_WORKLOADS), default="c2",
                     help="c2 = the headline configuration (default, the contract line); the others time the "
                          "benchmark's remaining configurations on one GPU")

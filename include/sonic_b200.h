@@ -269,6 +269,13 @@ int sm_ipc_open(const void* handle, void** ptr);
 int sm_ipc_close(void* ptr);
 int sm_ipc_free(void* ptr);
 
+/* Stream-ordered copy of `bytes` between two device addresses, either of which may be a peer's
+ * buffer mapped with sm_ipc_open.  Carried out by the copy engines over NVLink, so it occupies no
+ * SMs and overlaps kernels running on other streams; the expert-parallel "copy" transport moves
+ * each rank's record segments and returned partial rows with one such copy per peer segment.
+ * No counterpart in the reference. */
+int sm_copy_d2d_async(void* dst, const void* src, size_t bytes, void* stream);
+
 /* Leave n SMs of each device out of the persistent GEMM grids (process-wide setting, default 0), so
  * that communication kernels launched alongside (the expert-parallel all-to-alls) find free SMs.
  * No counterpart in the reference. */

@@ -532,4 +532,11 @@ int sm_ipc_close(void* ptr) { return ep_status(cudaIpcCloseMemHandle(ptr), "ipc 
 
 int sm_ipc_free(void* ptr) { return ep_status(cudaFree(ptr), "ipc free"); }
 
+int sm_copy_d2d_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return SM_OK;
+  if (!dst || !src) return set_last_error(SM_EINVAL, "copy: null pointer");
+  return ep_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)),
+                   "copy d2d");
+}
+
 }  // extern "C"

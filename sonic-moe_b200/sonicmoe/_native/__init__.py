@@ -74,6 +74,7 @@ SIGNATURES = {
     "sm_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "sm_ipc_close": (_I, [_P]),
     "sm_ipc_free": (_I, [_P]),
+    "sm_copy_d2d_async": (_I, [_P, _P, _SZ, _P]),
     "sm_route_plan": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "sm_quant_pack": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),

@@ -6,7 +6,12 @@ Two transports move the records and partial rows between the ranks of one node:
   mapped by all ranks; the receiver's pack kernel and the owner's combine kernel read them with
   peer loads over NVLink, so no separate all-to-all copies the data.  NCCL carries only the
   per-destination counts (an all-gather that also orders the stages) and one tiny all-reduce.
+* ``"copy"``: the same shared buffers, but record segments and partial rows cross NVLink as plain
+  device-to-device copies (copy engines, no SMs) into local buffers, pipelined over token chunks.
 * ``"nccl"``: ``all_to_all_single`` of the records and of the partial rows.
+
+With ``chunks > 1`` every transport pipelines the forward over token chunks on separate streams
+(dispatch / transfer / combine of one chunk under the expert GEMMs of its neighbour).
 
 No counterpart in the reference (it is single-GPU; expert parallelism is listed as future work in
 its blog).  One process per GPU; rank d of W owns the contiguous global experts
@@ -123,8 +128,9 @@ class NativeStages:
         )
         return freq
 
-    def combine_p2p(self, peer_out, send_counts, recv_start, ret_row, T, K, H, device):
-        out = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+    def combine_p2p(self, peer_out, send_counts, recv_start, ret_row, T, K, H, device, out=None):
+        if out is None:
+            out = torch.empty(T, H, dtype=torch.bfloat16, device=device)
         nat.call(
             "sm_ep_combine_p2p", self._ptrs(peer_out), self._ints(send_counts), self._ints(recv_start),
             len(peer_out), _ptr(ret_row), T, K, H, _ptr(out), _stream(),
@@ -192,7 +198,7 @@ class ExpertParallelMoE:
     def __init__(self, router_w, w1_local, w2_local, num_experts: int, top_k: int, group=None,
                  softmax_over_topk: bool = True, norm_topk_probs: bool = False, concat_layout: bool = False,
                  stages=None, reserve_sms: int = None, transport: str = None, max_tokens: int = None,
-                 hidden_size: int = None):
+                 hidden_size: int = None, chunks: int = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -206,24 +212,46 @@ class ExpertParallelMoE:
         if norm_topk_probs and softmax_over_topk:
             raise ValueError("`norm_topk_prob` only works with softmax-then-topk")
         self.stages = stages if stages is not None else NativeStages()
-        if stages is None:
-            # SMs the GEMMs leave free for communication kernels running alongside (default none)
-            nat.call("sm_set_gemm_sm_reserve", 0 if reserve_sms is None else reserve_sms)
         if transport is None:
             transport = "p2p" if (stages is None and self.world > 1) else "nccl"
-        if transport not in ("p2p", "nccl"):
+        if transport not in ("p2p", "copy", "nccl"):
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
+        if chunks is None:
+            # one chunk measured fastest at 2 and 4 GPUs (config 2): a second chunk's fixed expert-stage
+            # cost exceeds the transfer time it hides (see the overlap paths below)
+            chunks = 1
+        if chunks < 1:
+            raise ValueError("chunks must be >= 1")
+        self.chunks = int(chunks)
+        if stages is None:
+            # SMs the persistent GEMMs leave free for the dispatch / combine kernels and NCCL that run
+            # alongside them when the forward is pipelined over chunks
+            if reserve_sms is None:
+                reserve_sms = 0
+            nat.call("sm_set_gemm_sm_reserve", reserve_sms)
         self._send_buf = self._out_buf = None
-        if transport == "p2p":
+        self._streams = None
+        self._copy_streams = None
+        if transport in ("p2p", "copy"):
             if max_tokens is None or hidden_size is None:
                 raise ValueError("the p2p transport needs max_tokens and hidden_size to size its shared buffers")
             self.max_tokens = int(max_tokens)
             rb = self.stages.record_bytes(hidden_size, top_k)
-            self._send_cap = self.max_tokens * min(top_k, self.world)
-            self._out_cap = self.world * self.max_tokens
-            self._send_buf = IpcBuffer(max(self._send_cap, 1) * rb, group)
-            self._out_buf = IpcBuffer(max(self._out_cap, 1) * hidden_size * 2, group)
+            # one region per chunk in each shared buffer: chunk c of every rank lives at the same offset
+            self._chunk_tokens = -(-self.max_tokens // self.chunks)
+            self._send_cap = self._chunk_tokens * min(top_k, self.world)  # records per chunk region
+            self._out_cap = self.world * self._chunk_tokens  # partial rows per chunk region
+            self._send_chunk_bytes = max(self._send_cap, 1) * rb
+            self._out_chunk_bytes = max(self._out_cap, 1) * hidden_size * 2
+            self._send_buf = IpcBuffer(self.chunks * self._send_chunk_bytes, group)
+            self._out_buf = IpcBuffer(self.chunks * self._out_chunk_bytes, group)
+            if transport == "copy":
+                # local landing buffers: the records of every source, the partial rows of every owner
+                dev = torch.device("cuda", torch.cuda.current_device())
+                self._recv_local = torch.empty(self.chunks, max(self._out_cap, 1), rb, dtype=torch.uint8, device=dev)
+                self._ret_local = torch.empty(self.chunks, max(self._send_cap, 1), hidden_size, dtype=torch.bfloat16,
+                                              device=dev)
         self.router_w = router_w
         prep = (lambda w, c: w) if stages is not None else (lambda w, c: w if isinstance(w, Fp8ExpertWeights)
                                                             else weight_prep(w, concat_glu=c))
@@ -260,49 +288,247 @@ class ExpertParallelMoE:
             self._out_buf.free()
             self._send_buf = self._out_buf = None
 
+    def _exchange_counts(self, st, stream, device):
+        """Collective on `stream`: every rank's per-destination record counts of one chunk (and, since
+        a rank's all-gather runs after its dispatch, the guarantee that every send region of the
+        chunk is complete), validated and agreed on all ranks.  Returns (C[s][d], ready event)."""
+        W = self.world
+        with torch.cuda.stream(stream):
+            allc = torch.empty(W * W, dtype=torch.int32, device=device)
+            dist.all_gather_into_tensor(allc, st.send_counts, group=self.group)
+            C = allc.view(W, W).cpu().tolist()  # C[s][d]: records of this chunk from s to d
+            me = self.rank
+            msg = check_counts(C[me], [C[s_][me] for s_ in range(W)], self._send_cap)
+            if not msg and sum(C[s_][me] for s_ in range(W)) > self._out_cap:
+                msg = f"{sum(C[s_][me] for s_ in range(W))} received records exceed the output region ({self._out_cap})"
+            ok = self._agree(msg == "", device)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        if not ok:
+            raise RuntimeError(f"expert-parallel exchange aborted on every rank: {msg or 'a peer rank failed its check'}")
+        return C, ev
+
     def _forward_p2p(self, x: torch.Tensor):
+        """Peer-memory forward, pipelined over `self.chunks` token chunks on three streams:
+
+          main (high priority)  router, then per chunk: expert stage (records pulled from the peers'
+                                send regions, FP8 GEMMs, partial rows into this rank's output region),
+                                then an all-reduce that orders every rank's rows before any combine
+          dispatch              chunks 1.. : top-k + records, then their count exchange
+          combine               per chunk, after its all-reduce: each token pulls its partial rows
+
+        so the dispatch of chunk c+1 and the combine of chunk c-1 run while chunk c's GEMMs hold the
+        SMs they do not reserve.  Every rank issues the same collectives in the same order.
+        """
         T, H = x.shape
-        W, K, me = self.world, self.K, self.rank
+        W, K, me, Cn = self.world, self.K, self.rank, self.chunks
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the shared buffers")
-        err = torch.zeros(1, dtype=torch.int32, device=x.device)
-        logits = F.linear(x, self.router_w.to(x.dtype))
+        dev = x.device
+        caller = torch.cuda.current_stream(dev)
+        if self._streams is None:
+            self._streams = (torch.cuda.Stream(dev, priority=-1), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        s_main, s_disp, s_comb = self._streams
+        s_main.wait_stream(caller)
         rb = self.stages.record_bytes(H, K)
-        records = _RawRows(self._send_buf.ptr, self._send_cap, rb)
-        st = self.stages.dispatch(x, logits, self.E, K, W, me, self.sot, self.norm, err, records=records)
-        # counts of every rank (and a barrier: every send buffer is complete once this returns)
-        allc = torch.empty(W * W, dtype=torch.int32, device=x.device)
-        dist.all_gather_into_tensor(allc, st.send_counts, group=self.group)
-        C = allc.view(W, W).cpu().tolist()  # C[s][d]: records from s to d
-        recv_counts = [C[s][me] for s in range(W)]
-        seg_off = [sum(C[s][:me]) for s in range(W)]
-        msg = check_counts(C[me], recv_counts, self._send_cap)
-        if not msg and sum(recv_counts) > self._out_cap:
-            msg = f"{sum(recv_counts)} received records exceed the output buffer ({self._out_cap})"
-        if not self._agree(msg == "", x.device):
-            raise RuntimeError(f"expert-parallel exchange aborted on every rank: {msg or 'a peer rank failed its check'}")
-        freq = self.stages.expert_p2p(self._send_buf.peers, seg_off, recv_counts, H, self.I, self.El, K, self.w1,
-                                      self.w2, self._out_buf.ptr, err, x.device)
-        # every rank's output rows are complete once this returns
-        dist.all_reduce(err, group=self.group)
-        recv_start = [sum(C[s][d] for s in range(me)) for d in range(W)]
-        out = self.stages.combine_p2p(self._out_buf.peers, C[me], recv_start, st.ret_row, T, K, H, x.device)
+        Tc = -(-T // Cn) if T else 0
+        spans = [(min(T, c * Tc), min(T, (c + 1) * Tc)) for c in range(Cn)]
+        with torch.cuda.stream(s_main):
+            logits = F.linear(x, self.router_w.to(x.dtype))
+            out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+            errs = torch.zeros(Cn, dtype=torch.int32, device=dev)
+            freq = torch.zeros(self.El, dtype=torch.int32, device=dev)
+            ev_logits = torch.cuda.Event()
+            ev_logits.record(s_main)
+        states = []
+        for c, (a, b) in enumerate(spans):
+            s = s_main if c == 0 else s_disp
+            with torch.cuda.stream(s):
+                s.wait_event(ev_logits)
+                records = _RawRows(self._send_buf.ptr + c * self._send_chunk_bytes, self._send_cap, rb)
+                states.append(self.stages.dispatch(x[a:b], logits[a:b], self.E, K, W, me, self.sot, self.norm,
+                                                   errs[c:c + 1], records=records))
+        counts = [None] * Cn
+        counts[0] = self._exchange_counts(states[0], s_main, dev)
+        for c in range(Cn):
+            C, ev = counts[c]
+            a, b = spans[c]
+            with torch.cuda.stream(s_main):
+                s_main.wait_event(ev)
+                recv_counts = [C[s_][me] for s_ in range(W)]
+                seg_off = [sum(C[s_][:me]) for s_ in range(W)]
+                f = self.stages.expert_p2p([p + c * self._send_chunk_bytes for p in self._send_buf.peers], seg_off,
+                                           recv_counts, H, self.I, self.El, K, self.w1, self.w2,
+                                           self._out_buf.ptr + c * self._out_chunk_bytes, errs[c:c + 1], dev)
+                freq += f
+            if c + 1 < Cn:  # the host waits for chunk c+1's dispatch while chunk c computes
+                counts[c + 1] = self._exchange_counts(states[c + 1], s_disp, dev)
+            with torch.cuda.stream(s_main):
+                dist.all_reduce(errs[c:c + 1], group=self.group)  # every rank's chunk-c rows are complete
+                ev_rows = torch.cuda.Event()
+                ev_rows.record(s_main)
+            with torch.cuda.stream(s_comb):
+                s_comb.wait_event(ev_rows)
+                states[c].ret_row.record_stream(s_comb)
+                recv_start = [sum(C[q][d] for q in range(me)) for d in range(W)]
+                self.stages.combine_p2p([p + c * self._out_chunk_bytes for p in self._out_buf.peers], C[me],
+                                        recv_start, states[c].ret_row, b - a, K, H, dev, out=out[a:b])
+        ev_done = torch.cuda.Event()
+        ev_done.record(s_comb)
+        caller.wait_event(ev_done)
+        caller.wait_stream(s_main)
+        for t in (logits, out, freq):
+            t.record_stream(caller)
         return out, logits, freq
 
-    # ---- forward -----------------------------------------------------------------------------
+    def _forward_copy(self, x: torch.Tensor):
+        """Copy-engine forward: the peer buffers of the p2p transport, but the record segments and
+        the returned partial rows cross NVLink as plain device-to-device copies (one per peer
+        segment, on one stream per peer) into local buffers, so the transfers occupy no SMs and run
+        under the expert GEMMs of the neighbouring chunks:
+
+          main (high priority)  router, dispatch of every chunk, one exchange of all chunks' counts,
+                                then per chunk: expert stage on the landed records, all-reduce
+          copy stream per peer  all chunks' record segments from that peer (right after the
+                                counts), then, per chunk after its all-reduce, the partial rows that
+                                peer computed for this rank's records
+          combine               per chunk: the fp32 sum of each token's partial rows (local reads)
+        """
+        T, H = x.shape
+        W, K, me, Cn = self.world, self.K, self.rank, self.chunks
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the shared buffers")
+        dev = x.device
+        lib = nat.load()
+        caller = torch.cuda.current_stream(dev)
+        if self._streams is None:
+            self._streams = (torch.cuda.Stream(dev, priority=-1), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+            self._copy_streams = [torch.cuda.Stream(dev) for _ in range(W)]
+        s_main, _, s_comb = self._streams
+        rb = self.stages.record_bytes(H, K)
+        Tc = -(-T // Cn) if T else 0
+        spans = [(min(T, c * Tc), min(T, (c + 1) * Tc)) for c in range(Cn)]
+        s_main.wait_stream(caller)
+        with torch.cuda.stream(s_main):
+            logits = F.linear(x, self.router_w.to(x.dtype))
+            out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+            errs = torch.zeros(Cn, dtype=torch.int32, device=dev)
+            freq = torch.zeros(self.El, dtype=torch.int32, device=dev)
+            states = []
+            for c, (a, b) in enumerate(spans):
+                records = _RawRows(self._send_buf.ptr + c * self._send_chunk_bytes, self._send_cap, rb)
+                states.append(self.stages.dispatch(x[a:b], logits[a:b], self.E, K, W, me, self.sot, self.norm,
+                                                   errs[c:c + 1], records=records))
+            # counts of every chunk, every rank (the all-gather also orders every rank's dispatch
+            # before any copy out of its send regions)
+            mine = torch.stack([st.send_counts for st in states]).contiguous()  # [Cn, W]
+            allc = torch.empty(W * Cn * W, dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(allc, mine.view(-1), group=self.group)
+            A = allc.view(W, Cn, W).cpu().tolist()  # A[s][c][d]: records of chunk c from s to d
+            msg = ""
+            for c in range(Cn):
+                sent, recv = A[me][c], [A[q][c][me] for q in range(W)]
+                msg = msg or check_counts(sent, recv, self._send_cap)
+                if not msg and sum(recv) > self._out_cap:
+                    msg = f"{sum(recv)} received records exceed the output region ({self._out_cap})"
+            ok = self._agree(msg == "", dev)
+            ev_counts = torch.cuda.Event()
+            ev_counts.record(s_main)
+        if not ok:
+            raise RuntimeError(f"expert-parallel exchange aborted on every rank: {msg or 'a peer rank failed its check'}")
+
+        def copy(dst, src, nbytes, stream):
+            nat.call("sm_copy_d2d_async", dst, src, nbytes, stream.cuda_stream)
+
+        # records in: every chunk, every remote source, enqueued now
+        in_events, bases, seg_offs = [], [], []
+        for c in range(Cn):
+            evs, base, seg, landed = [], [], [], 0
+            for q in range(W):
+                n = A[q][c][me]
+                if q == me:  # this rank's own segment is read in place
+                    base.append(self._send_buf.ptr + c * self._send_chunk_bytes)
+                    seg.append(sum(A[me][c][:me]))
+                    continue
+                dst = self._recv_local[c].data_ptr() + landed * rb
+                base.append(dst)
+                seg.append(0)
+                if n > 0:
+                    cs = self._copy_streams[q]
+                    cs.wait_event(ev_counts)
+                    src = self._send_buf.peers[q] + c * self._send_chunk_bytes + sum(A[q][c][:me]) * rb
+                    copy(dst, src, n * rb, cs)
+                    ev = torch.cuda.Event()
+                    ev.record(cs)
+                    evs.append(ev)
+                landed += n
+            in_events.append(evs)
+            bases.append(base)
+            seg_offs.append(seg)
+        for c in range(Cn):
+            a, b = spans[c]
+            with torch.cuda.stream(s_main):
+                for ev in in_events[c]:
+                    s_main.wait_event(ev)
+                recv_counts = [A[q][c][me] for q in range(W)]
+                f = self.stages.expert_p2p(bases[c], seg_offs[c], recv_counts, H, self.I, self.El, K, self.w1,
+                                           self.w2, self._out_buf.ptr + c * self._out_chunk_bytes, errs[c:c + 1], dev)
+                freq += f
+                dist.all_reduce(errs[c:c + 1], group=self.group)  # every rank's chunk-c rows are complete
+                ev_rows = torch.cuda.Event()
+                ev_rows.record(s_main)
+            # partial rows out of every peer's output region for this rank's chunk-c records
+            ret = self._ret_local[c]
+            out_evs, row_bases, recv_start, off = [], [], [], 0
+            for d in range(W):
+                n = A[me][c][d]
+                first = sum(A[q][c][d] for q in range(me))  # this rank's rows in d's region
+                if d == me:
+                    row_bases.append(self._out_buf.ptr + c * self._out_chunk_bytes)
+                    recv_start.append(first)
+                else:
+                    row_bases.append(ret.data_ptr())
+                    recv_start.append(off)
+                    if n > 0:
+                        cs = self._copy_streams[d]
+                        cs.wait_event(ev_rows)
+                        copy(ret.data_ptr() + off * H * 2,
+                             self._out_buf.peers[d] + c * self._out_chunk_bytes + first * H * 2, n * H * 2, cs)
+                        ev = torch.cuda.Event()
+                        ev.record(cs)
+                        out_evs.append(ev)
+                off += n
+            with torch.cuda.stream(s_comb):
+                s_comb.wait_event(ev_rows)
+                for ev in out_evs:
+                    s_comb.wait_event(ev)
+                states[c].ret_row.record_stream(s_comb)
+                self.stages.combine_p2p(row_bases, A[me][c], recv_start, states[c].ret_row, b - a, K, H, dev,
+                                        out=out[a:b])
+        ev_done = torch.cuda.Event()
+        ev_done.record(s_comb)
+        caller.wait_event(ev_done)
+        caller.wait_stream(s_main)
+        for t in (logits, out, freq):
+            t.record_stream(caller)
+        return out, logits, freq
+
     def forward(self, x: torch.Tensor, chunks: int = None):
         """This rank's tokens [T, H] -> (out [T, H] bf16, router_logits [T, E], local expert counts [E/W]).
 
-        The tokens are processed in `chunks` slices (default: 2 with more than one rank): while
-        chunk c runs through the expert GEMMs, the records of chunk c+1 and the partial rows of
-        chunk c-1 are exchanged on NCCL's stream.
+        The tokens are processed in chunks (the constructor's `chunks`, or this call's for the
+        NCCL transport): while chunk c runs through the expert GEMMs, the records of chunk c+1 and
+        the partial rows of chunk c-1 move between the ranks (NCCL's stream, or the dispatch and
+        combine streams of the peer-memory transport).
         """
         if self.transport == "p2p":
             return self._forward_p2p(x)
+        if self.transport == "copy":
+            return self._forward_copy(x)
         T, H = x.shape
         W, K = self.world, self.K
         if chunks is None:
-            chunks = 1
+            chunks = self.chunks
         chunks = max(1, min(chunks, T)) if T > 0 else 1
         err = torch.zeros(1, dtype=torch.int32, device=x.device)
         logits = F.linear(x, self.router_w.to(x.dtype))

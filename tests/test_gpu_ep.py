@@ -118,7 +118,7 @@ def _free_port():
     return p
 
 
-def _nccl_worker(rank, W, port, q, T, H, I, E, K, transport):
+def _nccl_worker(rank, W, port, q, T, H, I, E, K, transport, chunks):
     import datetime
     import sys
 
@@ -140,7 +140,7 @@ def _nccl_worker(rank, W, port, q, T, H, I, E, K, transport):
         El = E // W
         moe = ExpertParallelMoE(rw.to(dev), w1[rank * El:(rank + 1) * El].to(dev),
                                 w2[rank * El:(rank + 1) * El].to(dev), E, K, transport=transport, max_tokens=T,
-                                hidden_size=H)
+                                hidden_size=H, chunks=chunks)
         for _ in range(2):  # twice: the shared buffers are reused across forwards
             out, logits, freq = moe.forward(x[rank * T:(rank + 1) * T].to(dev))
         torch.cuda.synchronize()
@@ -151,8 +151,11 @@ def _nccl_worker(rank, W, port, q, T, H, I, E, K, transport):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["p2p", "nccl"])
-def test_ep_multi_gpu(transport):
+@pytest.mark.parametrize("transport,chunks", [("p2p", 1), ("p2p", 2), ("p2p", 3), ("copy", 1), ("copy", 2),
+                                              ("copy", 3), ("nccl", 1), ("nccl", 2)])
+def test_ep_multi_gpu(transport, chunks):
+    """W processes, one per GPU.  chunks > 1 runs the pipelined forward (dispatch, expert stage and
+    combine of different token chunks on different streams); chunks=3 leaves the last chunk short."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs >= 2 GPUs")
@@ -163,7 +166,8 @@ def test_ep_multi_gpu(transport):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, W, port, q, T, H, I, E, K, transport)) for r in range(W)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, W, port, q, T, H, I, E, K, transport, chunks))
+             for r in range(W)]
     for p in procs:
         p.start()
     res = {}
