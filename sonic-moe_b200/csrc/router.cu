@@ -90,14 +90,23 @@ __device__ __forceinline__ float load_f32<float>(const float* p) {
   return *p;
 }
 
-constexpr int kRouterWarps = 8;
 
 // PL: per-lane register capacity (>= ceil(E/32) rounded to the lane vector); KMAX >= K.
+// Warps per 128-token tile: narrow rows (<= 8 values per lane) use 32 warps (4 rows each, the next
+// row's logits loaded while the current one is scored); wide rows keep register pressure down
+// with 8 warps.
+template <int PL>
+struct RouterShape {
+  static constexpr int kWarps = PL <= 8 ? 32 : 8;
+  static constexpr bool kPrefetch = PL <= 8;
+};
+
 template <typename InT, int PL, int KMAX>
-__global__ void __launch_bounds__(kRouterWarps * 32)
+__global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
     router_topk_kernel(const InT* __restrict__ logits, int T, int E, int K, int vec, int softmax_over_topk,
                        int renorm, float* __restrict__ scores, int32_t* __restrict__ indices,
                        int32_t* __restrict__ tile_counts, int n_tiles) {
+  constexpr int kWarps = RouterShape<PL>::kWarps;
   extern __shared__ int32_t s_hist[];  // [E] when tile_counts != nullptr
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -111,22 +120,34 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
   while ((1 << log_n) < E) ++log_n;
   const uint32_t mask = (1u << log_n) - 1u;
   const int steps = (E + 32 * vec - 1) / (32 * vec);
-
-  for (int r = warp; r < kTileTokens; r += kRouterWarps) {
-    const int row = row0 + r;
-    if (row >= T) break;
+  // lane's i-th element is column (i / vec) * 32 * vec + lane * vec + i % vec
+  auto col_of = [&](int i) -> int {
+    const int j = i / vec;
+    const int c = j * 32 * vec + lane * vec + (i - j * vec);
+    return (j < steps && c < E) ? c : -1;
+  };
+  auto load_row = [&](int row, float* dst) {
     const InT* src = logits + static_cast<size_t>(row) * E;
-    // lane's i-th element is column (i / vec) * 32 * vec + lane * vec + i % vec
-    auto col_of = [&](int i) -> int {
-      const int j = i / vec;
-      const int c = j * 32 * vec + lane * vec + (i - j * vec);
-      return (j < steps && c < E) ? c : -1;
-    };
-    float v[PL];
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
       const int c = col_of(i);
-      v[i] = (c >= 0) ? load_f32<InT>(src + c) : 0.0f;
+      dst[i] = (c >= 0) ? load_f32<InT>(src + c) : 0.0f;
+    }
+  };
+  float vn[PL];
+  if (RouterShape<PL>::kPrefetch && warp < kTileTokens && row0 + warp < T) load_row(row0 + warp, vn);
+
+  for (int r = warp; r < kTileTokens; r += kWarps) {
+    const int row = row0 + r;
+    if (row >= T) break;
+    float v[PL];
+    if (RouterShape<PL>::kPrefetch) {
+#pragma unroll
+      for (int i = 0; i < PL; ++i) v[i] = vn[i];
+      const int rn = row + kWarps;
+      if (r + kWarps < kTileTokens && rn < T) load_row(rn, vn);
+    } else {
+      load_row(row, v);
     }
     if (!softmax_over_topk) {
       // log-softmax over the full row (topk.py:284-339): max, then sum of exp(x - max) in lane
@@ -160,8 +181,8 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
         key[i] = order_key((__float_as_uint(v[i]) & ~mask) | enc);
       }
     }
-    // K rounds of warp arg-max over unique keys
-    uint32_t sel[KMAX];
+    // K rounds of warp arg-max over unique keys; lane k keeps the k-th selection
+    uint32_t mysel = 0u;
 #pragma unroll
     for (int k = 0; k < KMAX; ++k) {
       if (k < K) {
@@ -172,57 +193,35 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
 #pragma unroll
         for (int i = 0; i < PL; ++i)
           if (key[i] == wmax) key[i] = 0u;
-        sel[k] = wmax;
+        if (lane == k) mysel = wmax;
       }
     }
-    // decode (topk.py:365-375) and score (topk.py:377-401)
-    float val[KMAX];
-    int idx[KMAX];
-#pragma unroll
-    for (int k = 0; k < KMAX; ++k) {
-      if (k < K) {
-        const uint32_t bits = order_key_inv(sel[k]);
-        const uint32_t enc = bits & mask;
-        val[k] = __uint_as_float(bits & ~mask);
-        idx[k] = static_cast<int>((val[k] >= 0.0f) ? (~enc & mask) : enc);
-      }
-    }
+    // decode (topk.py:365-375) and score (topk.py:377-401) on lane k for selection k; the K-term
+    // sum is accumulated in selection order on every lane from the lanes' exps (same operations,
+    // same order as a sequential loop over k)
+    const bool act = lane < K;
+    const uint32_t bits = order_key_inv(mysel);
+    const uint32_t enc = bits & mask;
+    float val = __uint_as_float(bits & ~mask);
+    const int idx = static_cast<int>((val >= 0.0f) ? (~enc & mask) : enc);
+    float e;
     if (softmax_over_topk) {
-      float vmax = val[0];
+      float vmax = act ? val : -__int_as_float(0x7f800000);
 #pragma unroll
-      for (int k = 1; k < KMAX; ++k)
-        if (k < K) vmax = fmaxf(vmax, val[k]);
-      float s = 0.0f;
-#pragma unroll
-      for (int k = 0; k < KMAX; ++k)
-        if (k < K) {
-          val[k] = rt_exp(__fsub_rn(val[k], vmax));
-          s = __fadd_rn(s, val[k]);
-        }
-#pragma unroll
-      for (int k = 0; k < KMAX; ++k)
-        if (k < K) val[k] = __fdiv_rn(val[k], s);
+      for (int o = 16; o >= 1; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+      e = act ? rt_exp(__fsub_rn(val, vmax)) : 0.0f;
     } else {
-      float s = 0.0f;
-#pragma unroll
-      for (int k = 0; k < KMAX; ++k)
-        if (k < K) {
-          val[k] = rt_exp(val[k]);
-          s = __fadd_rn(s, val[k]);
-        }
-      if (renorm) {
-#pragma unroll
-        for (int k = 0; k < KMAX; ++k)
-          if (k < K) val[k] = __fdiv_rn(val[k], s);
-      }
+      e = act ? rt_exp(val) : 0.0f;
     }
+    float s = 0.0f;
 #pragma unroll
-    for (int k = 0; k < KMAX; ++k) {
-      if (k < K && lane == (k & 31)) {
-        scores[static_cast<size_t>(row) * K + k] = val[k];
-        indices[static_cast<size_t>(row) * K + k] = idx[k];
-        if (tile_counts) atomicAdd(&s_hist[idx[k]], 1);
-      }
+    for (int k = 0; k < KMAX; ++k)
+      if (k < K) s = __fadd_rn(s, __shfl_sync(0xffffffffu, e, k));
+    if (softmax_over_topk || renorm) e = __fdiv_rn(e, s);
+    if (act) {
+      scores[static_cast<size_t>(row) * K + lane] = e;
+      indices[static_cast<size_t>(row) * K + lane] = idx;
+      if (tile_counts) atomicAdd(&s_hist[idx], 1);
     }
   }
   if (tile_counts) {
@@ -410,8 +409,8 @@ static cudaError_t launch_router_t(const void* logits, int T, int E, int K, int 
   const size_t smem = tile_counts ? static_cast<size_t>(E) * sizeof(int32_t) : 0;
   auto kern = router_topk_kernel<InT, PL, KMAX>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  kern<<<n_tiles, kRouterWarps * 32, smem, st>>>(static_cast<const InT*>(logits), T, E, K, vec, sot, renorm, scores,
-                                                 idx, tile_counts, n_tiles);
+  kern<<<n_tiles, RouterShape<PL>::kWarps * 32, smem, st>>>(static_cast<const InT*>(logits), T, E, K, vec, sot,
+                                                             renorm, scores, idx, tile_counts, n_tiles);
   return cudaGetLastError();
 }
 
