@@ -416,12 +416,16 @@ static bool make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t 
 
 // Column slices of the down projection: the largest slice whose bf16 output slab (tokens x slice
 // columns) fits the L2 budget, so the reductions of one slice land in L2.
+// Every slice re-reads all of A, so at most 4 slices: measured best both for the 268 MB token
+// output of config 2 (4 slices of 67 MB) and for the ~1 GB of partial rows an expert-parallel rank
+// reduces into at 4 GPUs (4 slices beat 16).
 static int down_slices(const GemmArgs& g) {
   const int ntn = g.N / kBN;
   long long budget = 80ll << 20;
   if (const char* env = getenv("SONIC_B200_DOWN_SLAB_MB")) budget = atoll(env) << 20;
   int slices = 1;
-  while (slices < ntn && static_cast<long long>(g.tokens) * (g.N / slices) * 2 > budget && ntn % (slices * 2) == 0)
+  while (slices < ntn && slices < 4 && static_cast<long long>(g.tokens) * (g.N / slices) * 2 > budget &&
+         ntn % (slices * 2) == 0)
     slices *= 2;
   return slices;
 }
