@@ -3,11 +3,12 @@
 // One persistent kernel, two epilogues:
 //   up   : h = A x W1[e]^T over a 128x256 tile (A = packed e4m3 tokens, 1x128 UE8M0 scales;
 //          W1 = e4m3 weights, 128x128 UE8M0 scales), then a = silu(gate) * up and the 1x128
-//          requantisation of `a` to e4m3 + UE8M0, written in the padded expert-major layout the
-//          down projection reads.  (Reference: functional/__init__.py:260-275, QuACK gemm_act.)
-//   down : y = a x W2[e]^T over a 128x256 tile, then o[token] += score * y as bf16 vector
-//          atomics straight into the token-major output, i.e. the top-k weighted combine of
-//          functional/forward.py:64-85 fused into the GEMM epilogue.
+//          requantisation of `a` to e4m3 + UE8M0, staged in shared memory and written by one TMA
+//          tensor store per tile into the padded expert-major layout the down projection reads.
+//          (Reference: functional/__init__.py:260-275, QuACK gemm_act.)
+//   down : y = a x W2[e]^T over a 128x256 tile, then o[token] += score * y as TMA bulk bf16
+//          reductions (one 128-byte row chunk per thread) straight into the token-major output,
+//          i.e. the top-k weighted combine of functional/forward.py:64-85 fused into the epilogue.
 //
 // Tiles: 128 rows of one expert (the padded layout never mixes experts in a tile) x 256 output
 // columns, K consumed 128 at a time.  Roles per CTA (640 threads, one CTA per SM):
@@ -18,8 +19,9 @@
 //   warps 4-19  epilogue: warp w reads TMEM lanes 32*(w%4)..+31, columns chunk (w-4)/4, releases
 //               the accumulator as soon as it sits in registers, then computes and stores while
 //               the next tile's main loop runs.
-// Tile schedule: static round robin over (m-block, n-tile), n fastest; the number of m-blocks is
-// read from device memory, so empty experts cost nothing and no host synchronisation is needed.
+// Tile schedule: static round robin over (m-block, n-tile), n fastest (the down projection in up to
+// 4 column slices); the number of m-blocks is read from device memory, so empty experts cost
+// nothing and no host synchronisation is needed.
 // Every mbarrier wait is bounded (2 s); on a timeout the kernel records an error code, drains its
 // outstanding copies and MMAs with short bounded waits, frees tensor memory and returns.
 #include <cstdlib>
@@ -44,9 +46,9 @@ constexpr int kRowChunkBytes = 128;  // down epilogue: one thread's 64 bf16 of o
 // groups, so its 16-byte stores are 4-way (the minimum for 512 bytes) instead of 32-way conflicted.
 constexpr int kSlotStride = 144;
 
-// Shared-memory layout per epilogue kind.  The up projection keeps a 4-stage ring; the down
-// projection gives one stage up for 64 KB of per-thread staging from which its output rows are
-// reduced into global memory by TMA bulk reductions.
+// Shared-memory layout per epilogue kind.  The up projection keeps a 4-stage ring plus a 16 KB
+// output tile; the down projection gives one stage up for 72 KB of per-thread staging from which
+// its output rows are reduced into global memory by TMA bulk reductions.
 template <bool kUp>
 struct GemmSmem {
   static constexpr int kStages = kUp ? 4 : 3;
