@@ -213,14 +213,19 @@ class ExpertParallelMoE:
             raise ValueError("`norm_topk_prob` only works with softmax-then-topk")
         self.stages = stages if stages is not None else NativeStages()
         if transport is None:
-            transport = "p2p" if (stages is None and self.world > 1) else "nccl"
+            # measured at config 2: peer loads win up to 4 ranks; at 8 the exchanged volume is large
+            # enough that copy-engine transfers hidden under the GEMMs of 4 chunks win
+            if stages is None and self.world > 1:
+                transport = "copy" if self.world >= 8 else "p2p"
+            else:
+                transport = "nccl"
         if transport not in ("p2p", "copy", "nccl"):
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
         if chunks is None:
-            # one chunk measured fastest at 2 and 4 GPUs (config 2): a second chunk's fixed expert-stage
-            # cost exceeds the transfer time it hides (see the overlap paths below)
-            chunks = 1
+            # 2 and 4 ranks: one chunk (a chunk's fixed expert-stage cost exceeds the transfer time
+            # it hides); 8 ranks with copy-engine transfers: 4 chunks (7.37 vs 9.54 ms at config 2)
+            chunks = 4 if (transport == "copy" and self.world >= 8 and (max_tokens or 0) >= 4096) else 1
         if chunks < 1:
             raise ValueError("chunks must be >= 1")
         self.chunks = int(chunks)
