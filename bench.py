@@ -192,6 +192,10 @@ def run_ep(args, rank, world, local_rank):
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) / steps_e2e], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    # NVLink bytes into the busiest rank per forward (records from peers + partial rows back)
+    bx = torch.tensor([float(moe.last_exchange["bytes_in"]) if moe.last_exchange else 0.0], device=dev)
+    dist.all_reduce(bx, op=dist.ReduceOp.MAX)
+    transport, chunks = moe.transport, moe.chunks
     moe.close()
     return {
         "ms_step": ms_step,
@@ -199,6 +203,9 @@ def run_ep(args, rank, world, local_rank):
         "tflops_per_gpu": flops_fwd(T, H, I, K) / (ms_step / 1e3) / 1e12,
         "e2e": {"ms_step": t.item(), "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2},
         "clocks": clk.summary(),
+        "nvlink_bytes_in": bx.item(),
+        "transport": transport,
+        "chunks": chunks,
     }
 
 
@@ -600,6 +607,23 @@ def main():
                     "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]},
             "clocks": res["clocks"],
         }
+        # roofline of a compute + exchange step: the slower of the tensor work at the sustained FP8
+        # peak (the step runs back to back for the whole timed region) and the NVLink bytes into the
+        # busiest rank at the measured 770 GB/s per direction; frac = that target / measured step
+        peaks, peak_src = measured_peaks()
+        fp8_sust = 2.0 * float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1590.0)))
+        t_tensor = flops_fwd(T, H, I, K) / (fp8_sust * 1e12) * 1e3
+        t_link = res["nvlink_bytes_in"] / 770e9 * 1e3
+        target = max(t_tensor, t_link)
+        line["roofline"] = {
+            "bound": "tensor" if t_tensor >= t_link else "nvlink", "achieved": res["tflops_per_gpu"],
+            "peak": fp8_sust, "unit": "TFLOP/s", "frac": target / res["ms_step"], "traffic": None,
+            "target_ms": target, "tensor_ms": t_tensor, "nvlink_ms": t_link,
+            "nvlink_bytes_in_per_rank": res["nvlink_bytes_in"],
+            "basis": "fused compute+exchange: target = max(FLOPs / (2 x sustained bf16 of " + peak_src +
+                     "), NVLink bytes into the busiest rank / 770 GB/s); frac = target / measured step",
+        }
+        line["config"]["transport"] = f"{res['transport']}, {res['chunks']} chunk(s)"
         print(json.dumps(line))
         return
     res = run_ours(args, rank, world, local_rank)

@@ -236,6 +236,7 @@ class ExpertParallelMoE:
                 reserve_sms = 0
             nat.call("sm_set_gemm_sm_reserve", reserve_sms)
         self._send_buf = self._out_buf = None
+        self.last_exchange = None
         self._streams = None
         self._copy_streams = None
         if transport in ("p2p", "copy"):
@@ -292,6 +293,12 @@ class ExpertParallelMoE:
             self._send_buf.free()
             self._out_buf.free()
             self._send_buf = self._out_buf = None
+
+    def _note_exchange(self, records_in_remote: int, records_out_remote: int, H: int, rb: int):
+        """Bytes this rank received over NVLink in the last forward: records from other ranks, and
+        the partial rows other ranks computed for this rank's records (roofline of the exchange)."""
+        self.last_exchange = {"records_in_remote": records_in_remote, "rows_back_remote": records_out_remote,
+                              "bytes_in": records_in_remote * rb + records_out_remote * H * 2}
 
     def _exchange_counts(self, st, stream, device):
         """Collective on `stream`: every rank's per-destination record counts of one chunk (and, since
@@ -384,6 +391,8 @@ class ExpertParallelMoE:
         caller.wait_stream(s_main)
         for t in (logits, out, freq):
             t.record_stream(caller)
+        self._note_exchange(sum(C_[q][me] for C_, _ in counts for q in range(W) if q != me),
+                            sum(C_[me][d] for C_, _ in counts for d in range(W) if d != me), H, rb)
         return out, logits, freq
 
     def _forward_copy(self, x: torch.Tensor):
@@ -516,6 +525,8 @@ class ExpertParallelMoE:
         caller.wait_stream(s_main)
         for t in (logits, out, freq):
             t.record_stream(caller)
+        self._note_exchange(sum(A[q][c][me] for c in range(Cn) for q in range(W) if q != me),
+                            sum(A[me][c][d] for c in range(Cn) for d in range(W) if d != me), H, rb)
         return out, logits, freq
 
     def forward(self, x: torch.Tensor, chunks: int = None):
@@ -582,6 +593,9 @@ class ExpertParallelMoE:
             self._wait(pending_ret[c])
             outs.append(self.stages.combine(ret[c][:sum(sc[c])], states[c].ret_row, bounds[c + 1] - bounds[c], K, H))
         out = torch.cat(outs) if chunks > 1 else outs[0]
+        me = self.rank
+        self._note_exchange(sum(rc[c][q] for c in range(chunks) for q in range(W) if q != me),
+                            sum(sc[c][d] for c in range(chunks) for d in range(W) if d != me), H, rb)
         return out, logits, freq
 
     def _a2a_async(self, out, inp, out_splits, in_splits):
