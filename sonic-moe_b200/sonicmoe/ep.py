@@ -214,7 +214,7 @@ class ExpertParallelMoE:
         self.stages = stages if stages is not None else NativeStages()
         if transport is None:
             # measured at config 2: peer loads win up to 4 ranks; at 8 the exchanged volume is large
-            # enough that copy-engine transfers hidden under the GEMMs of 4 chunks win
+            # enough that copy-engine transfers hidden under the GEMMs of 6 chunks win
             if stages is None and self.world > 1:
                 transport = "copy" if self.world >= 8 else "p2p"
             else:
@@ -224,8 +224,9 @@ class ExpertParallelMoE:
         self.transport = transport
         if chunks is None:
             # 2 and 4 ranks: one chunk (a chunk's fixed expert-stage cost exceeds the transfer time
-            # it hides); 8 ranks with copy-engine transfers: 4 chunks (7.37 vs 9.54 ms at config 2)
-            chunks = 4 if (transport == "copy" and self.world >= 8 and (max_tokens or 0) >= 4096) else 1
+            # it hides); 8 ranks with copy-engine transfers: 6 chunks (7.01 ms at config 2, vs 7.37
+            # with 4 or 8 chunks and 9.54 for one-chunk peer loads)
+            chunks = 6 if (transport == "copy" and self.world >= 8 and (max_tokens or 0) >= 4096) else 1
         if chunks < 1:
             raise ValueError("chunks must be >= 1")
         self.chunks = int(chunks)
