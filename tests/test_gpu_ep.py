@@ -152,10 +152,11 @@ def _nccl_worker(rank, W, port, q, T, H, I, E, K, transport, chunks):
 
 
 @pytest.mark.parametrize("transport,chunks", [("p2p", 1), ("p2p", 2), ("p2p", 3), ("copy", 1), ("copy", 2),
-                                              ("copy", 3), ("nccl", 1), ("nccl", 2)])
+                                              ("copy", 3), ("copy", 6), ("nccl", 1), ("nccl", 2)])
 def test_ep_multi_gpu(transport, chunks):
     """W processes, one per GPU.  chunks > 1 runs the pipelined forward (dispatch, expert stage and
-    combine of different token chunks on different streams); chunks=3 leaves the last chunk short."""
+    combine of different token chunks on different streams); chunks=3 and 6 leave the last chunk
+    short (6 is the copy transport's default at 8 ranks)."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs >= 2 GPUs")
