@@ -602,7 +602,8 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
             "config": dict(config, parallelism=f"ep{world}", experts_per_rank=E // world,
                            timing="eager steps (host reads record counts), CUDA events, max over ranks"),
-            "tflops_per_gpu": res["tflops_per_gpu"], "gpu_launches": 14 * args.steps,
+            # per chunk: dispatch 6 kernels, expert stage 7, combine 1 (router logits are cuBLAS)
+            "tflops_per_gpu": res["tflops_per_gpu"], "gpu_launches": 14 * res["chunks"] * args.steps,
             "e2e": {"value": world * T / (e2e["ms_step"] / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]},
             "clocks": res["clocks"],
