@@ -201,8 +201,11 @@ def make_c1(MoE, KernelBackendMoE, ActivationType):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SONICMOE_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SONICMOE_REFERENCE"),
+                    help="checkout of the reference sonic-moe (or set SONICMOE_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference checkout with --reference or SONICMOE_REFERENCE")
     os.chdir(args.reference)  # so that `tests.metadata_test` resolves to the reference's tests
     MoE, KernelBackendMoE, ActivationType, ref_forward, ref_meta = _import_reference(args.reference)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
