@@ -281,6 +281,12 @@ int sm_copy_d2d_async(void* dst, const void* src, size_t bytes, void* stream);
  * No counterpart in the reference. */
 int sm_set_gemm_sm_reserve(int n);
 
+/* Self-test of the bounded waits (no counterpart in the reference): launches one kernel that waits
+ * on a barrier nothing arrives on; the wait gives up after the library's bound (2 s), writes 105
+ * into *err (if it held 0) and the kernel returns, leaving the context usable -- the same path by
+ * which a lost arrival inside a GEMM becomes an error status instead of a hung GPU. */
+int sm_selftest_bounded_wait(int32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,6 +20,7 @@ enum DevError : int {
   kErrTimeoutMma = 102,
   kErrTimeoutEpilogue = 103,
   kErrTimeoutDrain = 104,
+  kErrSelfTestWait = 105,  // sm_selftest_bounded_wait: the expected give-up
   kErrBadExpert = 201,
 };
 

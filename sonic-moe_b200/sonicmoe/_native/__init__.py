@@ -65,6 +65,7 @@ SIGNATURES = {
     ),
     "sm_ep_combine": (_I, [_P, _P, _I, _I, _I, _P, _P]),
     "sm_set_gemm_sm_reserve": (_I, [_I]),
+    "sm_selftest_bounded_wait": (_I, [_P, _P]),
     "sm_ep_expert_forward_p2p": (
         _I,
         [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P, _P],
