@@ -57,6 +57,12 @@ def _worker(rank, port, bad_rank, q):
         xs = x[rank * T_PER_RANK:(rank + 1) * T_PER_RANK].float()
         try:
             out, logits, freq = moe.forward(xs.to(torch.bfloat16))
+            # exchange accounting behind the multi-GPU roofline: bytes this rank received from the
+            # other rank = its records x record bytes + the partial rows of this rank's records
+            ex = moe.last_exchange
+            rb = FakeStages().record_bytes(H, K)
+            assert ex["bytes_in"] == ex["records_in_remote"] * rb + ex["rows_back_remote"] * H * 2
+            assert ex["records_in_remote"] > 0 and ex["rows_back_remote"] > 0
             q.put((rank, "ok", out.float().numpy(), logits.float().numpy()))
         except RuntimeError as e:
             q.put((rank, "error", str(e), None))
