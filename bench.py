@@ -531,7 +531,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=CFG["T"], help="tokens per GPU (profiling of smaller cases)")
-    ap.add_argument("--ep-transport", choices=["p2p", "copy", "nccl"], default=None,
+    ap.add_argument("--ep-transport", choices=["p2p", "copy", "nccl", "home"], default=None,
                     help="N>1: expert-parallel transport (default: the layer's)")
     ap.add_argument("--ep-chunks", type=int, default=None,
                     help="N>1: token chunks of the pipelined expert-parallel forward (default: the layer's)")
@@ -602,8 +602,10 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
             "config": dict(config, parallelism=f"ep{world}", experts_per_rank=E // world,
                            timing="eager steps (host reads record counts), CUDA events, max over ranks"),
-            # per chunk: dispatch 6 kernels, expert stage 7, combine 1 (router logits are cuBLAS)
-            "tflops_per_gpu": res["tflops_per_gpu"], "gpu_launches": 14 * res["chunks"] * args.steps,
+            # per chunk: dispatch 6 kernels, expert stage 7, combine 1 (router logits are cuBLAS); home
+            # transport per forward: top-k 1, routing plan 3, records 5, up stage 6, down 1
+            "tflops_per_gpu": res["tflops_per_gpu"],
+            "gpu_launches": (16 if res["transport"] == "home" else 14 * res["chunks"]) * args.steps,
             "e2e": {"value": world * T / (e2e["ms_step"] / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]},
             "clocks": res["clocks"],

@@ -22,6 +22,7 @@ enum DevError : int {
   kErrTimeoutDrain = 104,
   kErrSelfTestWait = 105,  // sm_selftest_bounded_wait: the expected give-up
   kErrBadExpert = 201,
+  kErrBadReturnRow = 202,  // an up-projection row whose home rank / row lies outside the home buffers
 };
 
 // A single wait never legitimately lasts more than a few milliseconds; 2 s means a bug.

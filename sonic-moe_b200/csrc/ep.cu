@@ -5,8 +5,11 @@
 // A dispatch record carries one token to one destination rank (a token routed to several experts
 // of the same rank travels once):
 //   [ H bytes e4m3 row | H/128 UE8M0 scale bytes | pad to 16 | K int32 local expert ids |
-//     K float32 scores | pad to 16 ]
-// Expert slots not on the destination rank hold -1 / 0.  The metadata starts on a 16-byte boundary
+//     K float32 scores | K int32 home rows | pad to 16 ]
+// Expert slots not on the destination rank hold -1 / 0 / -1.  A home row is the entry's row in the
+// padded expert-major layout of the token's own rank (set by sm_ep_dispatch_records from that
+// rank's routing plan, else -1): the expert-parallel variant that runs the down projection at home
+// returns the entry's intermediate row there.  The metadata starts on a 16-byte boundary
 // (meta_offset) so its 4-byte fields are aligned whatever H is.
 //
 // ep_dest_kernel       -- per (token, k): destination rank if k is the first entry of that rank for
@@ -15,6 +18,7 @@
 //                         its records at their dispatch positions (rank-major, token order)
 // ep_recv_unpack_kernel-- local expert ids / scores of the received records as [R, K] arrays
 // ep_pack_fp8_kernel   -- copy received e4m3 rows + scales into the padded expert-major layout
+//                         (and, for the home-down variant, each row's return destination)
 // ep_combine_kernel    -- owner side: o[t] = sum of the returned partial rows of token t (fp32)
 #include <cstring>
 
@@ -26,7 +30,7 @@ namespace smb {
 
 __host__ __device__ constexpr int ep_meta_offset(int H) { return (H + H / kBlockK + 15) / 16 * 16; }
 
-constexpr int kMaxRanks = 16;
+constexpr int kMaxRanks = kMaxEpRanks;
 
 // Where received record j lives: in the send buffer of source rank s (possibly another GPU's memory,
 // reached by peer loads) at record index seg_off[s] + (j - start[s]), for start[s] <= j < start[s+1].
@@ -39,9 +43,14 @@ struct RecordSource {
   int rb;
 };
 
-__device__ __forceinline__ const uint8_t* record_ptr(const RecordSource& rs, int j) {
+__device__ __forceinline__ int record_src(const RecordSource& rs, int j) {
   int s = 0;
   while (s + 1 < rs.W && j >= rs.start[s + 1]) ++s;
+  return s;
+}
+
+__device__ __forceinline__ const uint8_t* record_ptr(const RecordSource& rs, int j) {
+  const int s = record_src(rs, j);
   return rs.base[s] + static_cast<size_t>(rs.seg_off[s] + (j - rs.start[s])) * rs.rb;
 }
 
@@ -89,7 +98,8 @@ __global__ void __launch_bounds__(256)
     ep_send_pack_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, const int32_t* __restrict__ idx,
                         const float* __restrict__ scores, int K, int El, const int32_t* __restrict__ dest,
                         const int32_t* __restrict__ pos, int record_bytes, uint8_t* __restrict__ records,
-                        int32_t* __restrict__ ret_row) {
+                        int32_t* __restrict__ ret_row, const int32_t* __restrict__ home_s_rev,
+                        const int32_t* __restrict__ home_off, const int32_t* __restrict__ home_off_pad) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
@@ -135,10 +145,14 @@ __global__ void __launch_bounds__(256)
     if (p < 0) continue;
     uint8_t* rec = records + static_cast<size_t>(p) * record_bytes + ep_meta_offset(H);
     if (lane < K) {
-      const int e = idx[t * K + lane];
+      const int f = t * K + lane;
+      const int e = idx[f];
       const bool mine = (e / El) == d;
       reinterpret_cast<int32_t*>(rec)[lane] = mine ? e - d * El : -1;
-      reinterpret_cast<float*>(rec + 4 * K)[lane] = mine ? scores[t * K + lane] : 0.0f;
+      reinterpret_cast<float*>(rec + 4 * K)[lane] = mine ? scores[f] : 0.0f;
+      // the entry's row in the padded layout of this (home) rank's own routing plan
+      reinterpret_cast<int32_t*>(rec + 8 * K)[lane] =
+          (mine && home_s_rev) ? home_s_rev[f] - home_off[e] + home_off_pad[e] : -1;
     }
   }
 }
@@ -161,7 +175,8 @@ constexpr int kPackChunks = 8;  // 16-byte loads per lane per pass (H <= 4096 in
 __global__ void __launch_bounds__(256)
     ep_pack_fp8_kernel(const RecordSource rs, int R, int H, int K, int El, const int32_t* __restrict__ idx_local,
                        const int32_t* __restrict__ s_rev, const int32_t* __restrict__ off,
-                       const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq, uint8_t* __restrict__ xsf) {
+                       const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq, uint8_t* __restrict__ xsf,
+                       int32_t* __restrict__ ret_dst) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = blockIdx.x * 8 + warp;
   if (j >= R) return;
@@ -172,6 +187,11 @@ __global__ void __launch_bounds__(256)
     if (e >= 0 && e < El) my_dst = s_rev[f] - off[e] + off_pad[e];
   }
   const uint8_t* rec = record_ptr(rs, j);
+  if (ret_dst != nullptr && my_dst >= 0) {
+    // where the up projection returns this entry's intermediate row: source rank | its home row
+    const int hr = __ldcg(reinterpret_cast<const int32_t*>(rec + ep_meta_offset(H) + 8 * K) + lane);
+    ret_dst[my_dst] = (hr >= 0 && hr < (1 << kHomeShift)) ? (record_src(rs, j) << kHomeShift) | hr : -1;
+  }
   const int G = H / kBlockK;
   const int KG = (G + 3) / 4;
   const uint8_t sfb = (lane < G) ? __ldcg(rec + H + lane) : 0;
@@ -268,7 +288,7 @@ int ep_status(cudaError_t e, const char* what) {
 
 extern "C" {
 
-int sm_ep_record_bytes(int H, int K) { return (ep_meta_offset(H) + 8 * K + 15) / 16 * 16; }
+int sm_ep_record_bytes(int H, int K) { return (ep_meta_offset(H) + 12 * K + 15) / 16 * 16; }
 
 size_t sm_ep_dispatch_workspace_bytes(int T, int E, int K, int W) {
   const long long TK = static_cast<long long>(T) * K;
@@ -277,17 +297,13 @@ size_t sm_ep_dispatch_workspace_bytes(int T, int E, int K, int W) {
          a256(4) + 4096;
 }
 
-int sm_ep_dispatch_prepare(const void* x, const void* router_logits, int T, int H, int E, int K, int W, int rank,
-                           int softmax_over_topk, int norm_topk_probs, uint8_t* records, int32_t* ret_row,
-                           int32_t* send_counts, float* topk_scores, int32_t* topk_indices, void* workspace,
-                           size_t workspace_bytes, int32_t* err, void* stream) {
-  (void)rank;
-  if (T < 0 || H <= 0 || H % 256 || E < 1 || W < 1 || E % W || K < 1 || K > 32 || K > E)
-    return set_last_error(SM_EINVAL, "ep dispatch: bad shape T=%d H=%d E=%d K=%d W=%d", T, H, E, K, W);
-  if (!send_counts || !err || (T > 0 && (!x || !router_logits || !records || !ret_row || !topk_scores ||
-                                         !topk_indices)))
-    return set_last_error(SM_EINVAL, "ep dispatch: null pointer");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+// Records of this rank's routed tokens: destination of each entry, rank-major dispatch order (the
+// token-choice metadata over "experts" = destination ranks, duplicate (token, rank) entries as
+// holes), then one warp per token quantises it and writes its records.
+static int ep_dispatch_records(const void* x, int T, int H, int E, int K, int W, const float* topk_scores,
+                               const int32_t* topk_indices, const int32_t* home_s_rev, const int32_t* home_off,
+                               const int32_t* home_off_pad, uint8_t* records, int32_t* ret_row, int32_t* send_counts,
+                               void* workspace, size_t workspace_bytes, int32_t* err, cudaStream_t st) {
   const int El = E / W;
   const long long TK = static_cast<long long>(T) * K;
   const int n_tiles = ceil_div(T, kTileTokens);
@@ -309,15 +325,8 @@ int sm_ep_dispatch_prepare(const void* x, const void* router_logits, int T, int 
   int32_t* blk = reinterpret_cast<int32_t*>(take((static_cast<size_t>(max_padded_blocks(TK, W)) + 2) * 4));
   int32_t* nblk = reinterpret_cast<int32_t*>(take(4));
   if (used > workspace_bytes) return set_last_error(SM_EINVAL, "ep dispatch: workspace too small");
-  if (T == 0) return ep_status(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * W, st), "ep dispatch");
-  cudaError_t e = launch_router_topk(router_logits, kDtypeBF16, T, E, K, softmax_over_topk, norm_topk_probs,
-                                     topk_scores, topk_indices, nullptr, st);
-  if (e == cudaSuccess) {
-    ep_dest_kernel<<<(T + 255) / 256, 256, 0, st>>>(topk_indices, T, K, El, dest);
-    e = cudaGetLastError();
-  }
-  // rank-major dispatch order: the token-choice metadata over "experts" = destination ranks, with
-  // duplicate (token, rank) entries as holes
+  ep_dest_kernel<<<(T + 255) / 256, 256, 0, st>>>(topk_indices, T, K, El, dest);
+  cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess)
     e = launch_route_hist_holes(dest, static_cast<int>(TK), kTileTokens * K, W, n_tiles, tile_counts, err, st);
   if (e == cudaSuccess)
@@ -328,10 +337,49 @@ int sm_ep_dispatch_prepare(const void* x, const void* router_logits, int T, int 
   if (e == cudaSuccess) {
     ep_send_pack_kernel<<<(T + 7) / 8, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, topk_indices,
                                                      topk_scores, K, El, dest, pos, sm_ep_record_bytes(H, K), records,
-                                                     ret_row);
+                                                     ret_row, home_s_rev, home_off, home_off_pad);
     e = cudaGetLastError();
   }
   return ep_status(e, "ep dispatch");
+}
+
+static int check_dispatch_args(int T, int H, int E, int K, int W) {
+  if (T < 0 || H <= 0 || H % 256 || E < 1 || W < 1 || W > kMaxRanks || E % W || K < 1 || K > 32 || K > E)
+    return set_last_error(SM_EINVAL, "ep dispatch: bad shape T=%d H=%d E=%d K=%d W=%d", T, H, E, K, W);
+  return SM_OK;
+}
+
+int sm_ep_dispatch_prepare(const void* x, const void* router_logits, int T, int H, int E, int K, int W, int rank,
+                           int softmax_over_topk, int norm_topk_probs, uint8_t* records, int32_t* ret_row,
+                           int32_t* send_counts, float* topk_scores, int32_t* topk_indices, void* workspace,
+                           size_t workspace_bytes, int32_t* err, void* stream) {
+  (void)rank;
+  if (int rc = check_dispatch_args(T, H, E, K, W)) return rc;
+  if (!send_counts || !err || (T > 0 && (!x || !router_logits || !records || !ret_row || !topk_scores ||
+                                         !topk_indices)))
+    return set_last_error(SM_EINVAL, "ep dispatch: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0) return ep_status(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * W, st), "ep dispatch");
+  cudaError_t e = launch_router_topk(router_logits, kDtypeBF16, T, E, K, softmax_over_topk, norm_topk_probs,
+                                     topk_scores, topk_indices, nullptr, st);
+  if (e != cudaSuccess) return ep_status(e, "ep dispatch");
+  return ep_dispatch_records(x, T, H, E, K, W, topk_scores, topk_indices, nullptr, nullptr, nullptr, records, ret_row,
+                             send_counts, workspace, workspace_bytes, err, st);
+}
+
+int sm_ep_dispatch_records(const void* x, int T, int H, int E, int K, int W, const float* topk_scores,
+                           const int32_t* topk_indices, const int32_t* home_s_rev, const int32_t* home_off,
+                           const int32_t* home_off_pad, uint8_t* records, int32_t* ret_row, int32_t* send_counts,
+                           void* workspace, size_t workspace_bytes, int32_t* err, void* stream) {
+  if (int rc = check_dispatch_args(T, H, E, K, W)) return rc;
+  if (!send_counts || !err || (T > 0 && (!x || !records || !ret_row || !topk_scores || !topk_indices)))
+    return set_last_error(SM_EINVAL, "ep dispatch: null pointer");
+  if ((home_s_rev == nullptr) != (home_off == nullptr) || (home_off == nullptr) != (home_off_pad == nullptr))
+    return set_last_error(SM_EINVAL, "ep dispatch: the home plan needs s_rev, off and off_pad together");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0) return ep_status(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * W, st), "ep dispatch");
+  return ep_dispatch_records(x, T, H, E, K, W, topk_scores, topk_indices, home_s_rev, home_off, home_off_pad, records,
+                             ret_row, send_counts, workspace, workspace_bytes, err, st);
 }
 
 size_t sm_ep_expert_workspace_bytes(int R, int H, int I, int El, int K) {
@@ -340,13 +388,27 @@ size_t sm_ep_expert_workspace_bytes(int R, int H, int I, int El, int K) {
   return a256(TK * 4) * 5 + a256(static_cast<size_t>(El) * (ceil_div(R, kTileTokens) + 1) * 4) +
          a256(static_cast<size_t>(El + 1) * 4) * 2 + a256((mb + 2) * 4) + a256(4) +
          a256(mb * kBlockM * static_cast<size_t>(H)) + a256(mb * ceil_div(H, 512) * kSfAtomBytes) +
-         a256(mb * kBlockM * static_cast<size_t>(I)) + a256(mb * ceil_div(I, 512) * kSfAtomBytes) + 4096;
+         a256(mb * kBlockM * static_cast<size_t>(I)) + a256(mb * ceil_div(I, 512) * kSfAtomBytes) +
+         a256(mb * kBlockM * sizeof(int32_t)) + 4096;
 }
 
+// Where the home-down variant's up projection sends its rows: rank h's intermediate rows / scale
+// atoms (peer pointers) and the row capacity every home buffer has.
+struct HomeReturn {
+  uint8_t* q[kMaxRanks];
+  uint8_t* sf[kMaxRanks];
+  long long rows;
+  int W;
+};
+
+// The expert stage: local routing metadata over the received records, the pack into the padded
+// layout, the up projection, then either the down projection with the per-record combine into
+// out_rows, or (home != nullptr) nothing more -- the up projection has returned every row to its
+// token's home rank.
 static int ep_expert_forward(const RecordSource& src, int R, int H, int I, int El, int K, const uint8_t* w1q,
                              const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout,
                              void* out_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
-                             int32_t* err, void* stream) {
+                             int32_t* err, void* stream, const HomeReturn* home = nullptr) {
   if (R < 0 || H <= 0 || H % 256 || I <= 0 || I % 128 || El < 1 || K < 1 || K > 32)
     return set_last_error(SM_EINVAL, "ep expert: bad shape R=%d H=%d I=%d El=%d K=%d", R, H, I, El, K);
   if (!expert_frequency || !err) return set_last_error(SM_EINVAL, "ep expert: null pointer");
@@ -376,9 +438,12 @@ static int ep_expert_forward(const RecordSource& src, int R, int H, int I, int E
   uint8_t* xsf = take(static_cast<size_t>(mb) * ceil_div(H, 512) * kSfAtomBytes);
   uint8_t* aq = take(static_cast<size_t>(mb) * kBlockM * I);
   uint8_t* asf = take(static_cast<size_t>(mb) * ceil_div(I, 512) * kSfAtomBytes);
+  int32_t* ret_dst = reinterpret_cast<int32_t*>(take(static_cast<size_t>(mb) * kBlockM * sizeof(int32_t)));
   if (used > workspace_bytes) return set_last_error(SM_EINVAL, "ep expert: workspace too small");
   ep_recv_unpack_kernel<<<static_cast<int>((TK + 255) / 256), 256, 0, st>>>(src, R, H, K, idx, scores);
   cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && home)
+    e = cudaMemsetAsync(ret_dst, 0xFF, static_cast<size_t>(mb) * kBlockM * sizeof(int32_t), st);
   if (e == cudaSuccess)
     e = launch_route_hist_holes(idx, static_cast<int>(TK), kTileTokens * K, El, n_tiles, tile_counts, err, st);
   if (e == cudaSuccess)
@@ -388,10 +453,11 @@ static int ep_expert_forward(const RecordSource& src, int R, int H, int I, int E
     e = launch_route_scatter(idx, nullptr, static_cast<int>(TK), K, kTileTokens * K, El, n_tiles, tile_counts, off,
                              s_scatter, s_rev, x_gather, st);
   if (e == cudaSuccess) {
-    ep_pack_fp8_kernel<<<(R + 7) / 8, 256, 0, st>>>(src, R, H, K, El, idx, s_rev, off, off_pad, xq, xsf);
+    ep_pack_fp8_kernel<<<(R + 7) / 8, 256, 0, st>>>(src, R, H, K, El, idx, s_rev, off, off_pad, xq, xsf,
+                                                    home ? ret_dst : nullptr);
     e = cudaGetLastError();
   }
-  if (e == cudaSuccess) e = cudaMemsetAsync(out_rows, 0, static_cast<size_t>(R) * H * 2, st);
+  if (e == cudaSuccess && !home) e = cudaMemsetAsync(out_rows, 0, static_cast<size_t>(R) * H * 2, st);
   if (e == cudaSuccess) {
     GemmArgs g{};
     g.a = xq;
@@ -412,8 +478,19 @@ static int ep_expert_forward(const RecordSource& src, int R, int H, int I, int E
     g.err = err;
     g.num_sms = gemm_grid_sms();
     g.tokens = R;
+    if (home) {
+      g.out_q = nullptr;
+      g.out_sf = nullptr;
+      g.ret_dst = ret_dst;
+      for (int h = 0; h < home->W; ++h) {
+        g.home_q[h] = home->q[h];
+        g.home_sf[h] = home->sf[h];
+      }
+      g.home_rows = home->rows;
+      g.n_homes = home->W;
+    }
     e = launch_moe_up(g, st);
-    if (e == cudaSuccess) {
+    if (e == cudaSuccess && !home) {
       GemmArgs d = g;
       d.a = aq;
       d.a_sf = asf;
@@ -470,6 +547,38 @@ int sm_ep_expert_forward_p2p(const void* const* peer_send_bases, const int32_t* 
   src.rb = sm_ep_record_bytes(H, K);
   return ep_expert_forward(src, R, H, I, El, K, w1q, w1_sf, w2q, w2_sf, concat_layout, out_rows, expert_frequency,
                            workspace, workspace_bytes, err, stream);
+}
+
+int sm_ep_expert_up_p2p(const void* const* peer_send_bases, const int32_t* seg_off, const int32_t* recv_counts,
+                        int W, int H, int I, int El, int K, const uint8_t* w1q, const uint8_t* w1_sf,
+                        int concat_layout, void* const* home_q_bases, void* const* home_sf_bases,
+                        long long home_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
+                        int32_t* err, void* stream) {
+  if (W < 1 || W > kMaxRanks || !peer_send_bases || !seg_off || !recv_counts || !home_q_bases || !home_sf_bases)
+    return set_last_error(SM_EINVAL, "ep expert up p2p: W must be in [1, %d] with W peer and home bases", kMaxRanks);
+  if (home_rows < 0 || home_rows > (1ll << kHomeShift))
+    return set_last_error(SM_EINVAL, "ep expert up p2p: home_rows %lld outside [0, 2^%d]", home_rows, kHomeShift);
+  RecordSource src{};
+  HomeReturn home{};
+  int R = 0;
+  for (int s = 0; s < W; ++s) {
+    if (recv_counts[s] < 0 || seg_off[s] < 0) return set_last_error(SM_EINVAL, "ep expert up p2p: negative count");
+    if (!home_q_bases[s] || !home_sf_bases[s] || reinterpret_cast<uintptr_t>(home_q_bases[s]) % 16)
+      return set_last_error(SM_EINVAL, "ep expert up p2p: home buffers must be non-null and 16-byte aligned");
+    src.base[s] = static_cast<const uint8_t*>(peer_send_bases[s]);
+    src.seg_off[s] = seg_off[s];
+    src.start[s] = R;
+    R += recv_counts[s];
+    home.q[s] = static_cast<uint8_t*>(home_q_bases[s]);
+    home.sf[s] = static_cast<uint8_t*>(home_sf_bases[s]);
+  }
+  src.start[W] = R;
+  src.W = W;
+  src.rb = sm_ep_record_bytes(H, K);
+  home.rows = home_rows;
+  home.W = W;
+  return ep_expert_forward(src, R, H, I, El, K, w1q, w1_sf, nullptr, nullptr, concat_layout, nullptr,
+                           expert_frequency, workspace, workspace_bytes, err, stream, &home);
 }
 
 static int ep_combine(const RowSource& rs, const int32_t* ret_row, int T, int K, int H, void* out, void* stream) {

@@ -6,6 +6,9 @@
 //          requantisation of `a` to e4m3 + UE8M0, staged in shared memory and written by one TMA
 //          tensor store per tile into the padded expert-major layout the down projection reads.
 //          (Reference: functional/__init__.py:260-275, QuACK gemm_act.)
+//          Expert parallel with the down projection at the tokens' home ranks: each requantised
+//          row goes straight from registers into its home rank's padded layout (peer stores over
+//          NVLink, tile by tile under the main loop of the next tile) instead of the local tile.
 //   down : y = a x W2[e]^T over a 128x256 tile, then o[token] += score * y as TMA bulk bf16
 //          reductions (one 128-byte row chunk per thread) straight into the token-major output,
 //          i.e. the top-k weighted combine of functional/forward.py:64-85 fused into the epilogue.
@@ -94,7 +97,7 @@ struct RowMeta {
   int mb, nt, e;
   int p;      // padded row
   int valid;  // a real (token, expert) entry, not padding
-  int tok;    // down: token whose output row receives the reduction
+  int tok;    // down: token whose output row receives the reduction; up, expert parallel: ret_dst[p]
   float sc;   // down: its router score
 };
 
@@ -108,7 +111,9 @@ __device__ __forceinline__ RowMeta load_row_meta(const GemmArgs& g, int tile, in
   m.valid = rel < g.freq[m.e];
   m.tok = 0;
   m.sc = 0.0f;
-  if constexpr (!kUp) {
+  if constexpr (kUp) {
+    if (g.ret_dst != nullptr) m.tok = m.valid ? g.ret_dst[m.p] : -1;
+  } else {
     if (m.valid) {
       const int rs = rel + g.off[m.e];
       m.tok = g.x_gather[rs];
@@ -160,6 +165,30 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const uint32_t 
              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(o[4 * i + 2], inv), __fmul_rn(o[4 * i + 3], inv))) << 16);
     }
     const int I2 = g.N / 2;
+    if (g.ret_dst != nullptr) {
+      // expert parallel: the thread's 32 bytes of the row (and, from the first column warp, the
+      // row's scale byte) go straight to the token's home rank -- plain 16-byte peer stores, no
+      // staging tile; the home's down projection reads them after a cross-rank barrier
+      if (valid) {
+        const int dst = m.tok;
+        const int home = dst >> kHomeShift;
+        const long long ph = dst & ((1 << kHomeShift) - 1);
+        if (dst < 0 || home >= g.n_homes || ph >= g.home_rows) {
+          atomicCAS(g.err, 0, kErrBadReturnRow);
+        } else {
+          uint8_t* drow = g.home_q[home] + ph * I2 + nt * 128 + cc * 32;
+          *reinterpret_cast<uint4*>(drow) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(drow + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+          if (cc == 0) {
+            const long long KG2 = (I2 / kBlockK + 3) / 4;
+            const int rr = static_cast<int>(ph % kBlockM);
+            g.home_sf[home][((ph / kBlockM) * KG2 + nt / 4) * kSfAtomBytes + 16 * (rr % 32) + 4 * (rr / 32) +
+                            (nt % 4)] = static_cast<uint8_t>(e8 + 127);
+          }
+        }
+      }
+      return true;
+    }
     // row r of the staging tile, 16-byte chunks 2cc and 2cc+1 at their 128B-swizzled positions
     uint8_t* srow = sStage + r * 128;
     *reinterpret_cast<uint4*>(srow + (((2 * cc) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -378,6 +407,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                               pol_out))
         break;
     }
+    // rows stored into other GPUs' memory are performed system-wide before the kernel completes
+    if (kUp && g.ret_dst != nullptr) __threadfence_system();
     bulk_wait_all();  // outstanding reductions / output stores have finished with shared memory
   }
   __syncthreads();
@@ -442,8 +473,11 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, g.a, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.Kd), kBlockM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tb, g.b, static_cast<uint64_t>(g.E) * g.N, static_cast<uint64_t>(g.Kd), kBN)) return cudaErrorInvalidValue;
-  CUtensorMap to = ta;  // the down projection has no tiled output
-  if (kUp && !make_tmap(&to, g.out_q, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.N / 2), kBlockM))
+  CUtensorMap to = ta;  // the down projection and the expert-parallel up projection have no tiled output
+  if (kUp && g.ret_dst == nullptr &&
+      !make_tmap(&to, g.out_q, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.N / 2), kBlockM))
+    return cudaErrorInvalidValue;
+  if (kUp && g.ret_dst != nullptr && (g.n_homes < 1 || g.n_homes > kMaxEpRanks || g.home_rows < 0))
     return cudaErrorInvalidValue;
   auto kern = moe_gemm_kernel<kUp>;
   constexpr int kSmemAlloc = GemmSmem<kUp>::kAlloc;

@@ -14,6 +14,8 @@ constexpr int kPadRows = 128;     // experts are padded to multiples of this
 constexpr int kBlocksPerPad = kPadRows / kBlockM;
 constexpr int kBlockK = 128;      // K extent of one pipeline stage (= one scale-factor group)
 constexpr int kSfAtomBytes = 512; // 128 rows x 4 K-blocks of UE8M0 scale factors
+constexpr int kMaxEpRanks = 16;   // ranks of one expert-parallel group (peer pointers passed by value)
+constexpr int kHomeShift = 27;    // return destination = (home rank << kHomeShift) | row on that rank
 
 enum Dtype : int { kDtypeBF16 = 0, kDtypeF16 = 1, kDtypeF32 = 2 };
 
@@ -77,6 +79,15 @@ struct GemmArgs {
   const int32_t* x_gather;
   const float* scores;
   void* out_bf16;
+  // up projection, expert parallel with the down projection at the tokens' home ranks: instead of
+  // out_q / out_sf, padded row p goes to row (ret_dst[p] & (2^kHomeShift - 1)) of the intermediate
+  // home_q[h] [home_rows, N/2] and its scale atoms home_sf[h] on rank h = ret_dst[p] >> kHomeShift
+  // (peer memory; plain stores).  Null ret_dst: the local output of the single-GPU layer.
+  const int32_t* ret_dst;
+  uint8_t* home_q[kMaxEpRanks];
+  uint8_t* home_sf[kMaxEpRanks];
+  long long home_rows;
+  int n_homes;
   int* err;
   int num_sms;
   int tokens;    // T (rows of the token-major output), for the down projection's slice choice

@@ -22,6 +22,7 @@ ERR_NAMES = {
     103: "epilogue wait timed out",
     104: "drain wait timed out",
     201: "expert index outside [0, E)",
+    202: "up-projection row without a valid home row (home-down expert parallel)",
 }
 
 _P = ctypes.c_void_p
@@ -71,6 +72,14 @@ SIGNATURES = {
         [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P, _P],
     ),
     "sm_ep_combine_p2p": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _P, _P]),
+    "sm_ep_dispatch_records": (
+        _I,
+        [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P],
+    ),
+    "sm_ep_expert_up_p2p": (
+        _I,
+        [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _LL, _P, _P, _SZ, _P, _P],
+    ),
     "sm_ipc_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),
     "sm_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "sm_ipc_close": (_I, [_P]),

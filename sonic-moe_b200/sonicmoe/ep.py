@@ -1,6 +1,6 @@
 """Expert-parallel FP8 MoE layer forward: experts sharded over the ranks of a process group.
 
-Two transports move the records and partial rows between the ranks of one node:
+Four transports move the records and returned rows between the ranks of one node:
 
 * ``"p2p"`` (default on GPUs): every rank's send buffer and output rows live in CUDA IPC memory
   mapped by all ranks; the receiver's pack kernel and the owner's combine kernel read them with
@@ -9,6 +9,12 @@ Two transports move the records and partial rows between the ranks of one node:
 * ``"copy"``: the same shared buffers, but record segments and partial rows cross NVLink as plain
   device-to-device copies (copy engines, no SMs) into local buffers, pipelined over token chunks.
 * ``"nccl"``: ``all_to_all_single`` of the records and of the partial rows.
+* ``"home"``: the records move as in ``"p2p"``, but an expert's owner runs only the up projection,
+  whose epilogue stores each entry's e4m3 intermediate row (I + I/128 bytes) straight into the
+  padded layout of the token's own rank over NVLink; that rank then runs the down projection with
+  the fused top-k combine over its own routing plan, with every expert's w2 replicated on every
+  rank (gathered once at construction).  No partial rows and no combine pass: at config 2 with 8
+  ranks 0.24 GB instead of 1.2 GB comes back to each rank per forward.
 
 With ``chunks > 1`` every transport pipelines the forward over token chunks on separate streams
 (dispatch / transfer / combine of one chunk under the expert GEMMs of its neighbour).
@@ -39,7 +45,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import _native as nat
-from .ops import Fp8ExpertWeights, _need, _ptr, _stream, _workspace, weight_prep
+from .ops import Fp8ExpertWeights, _need, _ptr, _stream, _workspace, max_padded_blocks, weight_prep
 
 
 @dataclass
@@ -125,6 +131,42 @@ class NativeStages:
             "sm_ep_expert_forward_p2p", self._ptrs(peer_send), self._ints(seg_off), self._ints(recv_counts), W, H, I,
             El, K, _ptr(w1.q), _ptr(w1.sf), _ptr(w2.q), _ptr(w2.sf), int(w1.concat_glu), out_ptr, _ptr(freq),
             _ptr(ws), ws.numel(), _ptr(err), _stream(),
+        )
+        return freq
+
+    # ---- home-down stages ----------------------------------------------------------------------
+    def dispatch_records(self, x, scores, idx, plan, E, W, err, records=None):
+        """Records from an already computed top-k; with `plan` (this rank's RoutePlan over all E
+        experts) every record carries its entries' rows in this rank's padded layout."""
+        T, H = x.shape
+        K = idx.shape[1]
+        rb = self.record_bytes(H, K)
+        dev = x.device
+        if records is None:
+            records = torch.empty(max(T * min(K, W), 1), rb, dtype=torch.uint8, device=dev)
+        ret_row = torch.empty(T * K, dtype=torch.int32, device=dev)
+        send_counts = torch.empty(W, dtype=torch.int32, device=dev)
+        ws = _workspace(self.lib.sm_ep_dispatch_workspace_bytes(T, E, K, W), dev)
+        nat.call(
+            "sm_ep_dispatch_records", _ptr(x), T, H, E, K, W, _ptr(scores), _ptr(idx),
+            _ptr(plan.s_rev if plan else None), _ptr(plan.off if plan else None),
+            _ptr(plan.off_pad if plan else None), _ptr(records), _ptr(ret_row), _ptr(send_counts), _ptr(ws),
+            ws.numel(), _ptr(err), _stream(),
+        )
+        return DispatchState(T, K, None, scores, idx, records, ret_row, send_counts)
+
+    def expert_up_p2p(self, peer_send, seg_off, recv_counts, H, I, El, K, w1, home_q, home_sf, home_rows, err,
+                      device):
+        """Up projection of the received records; each row is stored into its source rank's
+        intermediate home_q[s] / home_sf[s] (peer pointers).  Returns the local expert counts."""
+        W = len(peer_send)
+        R = sum(recv_counts)
+        freq = torch.empty(El, dtype=torch.int32, device=device)
+        ws = _workspace(self.lib.sm_ep_expert_workspace_bytes(R, H, I, El, K), device)
+        nat.call(
+            "sm_ep_expert_up_p2p", self._ptrs(peer_send), self._ints(seg_off), self._ints(recv_counts), W, H, I, El,
+            K, _ptr(w1.q), _ptr(w1.sf), int(w1.concat_glu), self._ptrs(home_q), self._ptrs(home_sf), int(home_rows),
+            _ptr(freq), _ptr(ws), ws.numel(), _ptr(err), _stream(),
         )
         return freq
 
@@ -219,8 +261,10 @@ class ExpertParallelMoE:
                 transport = "copy" if self.world >= 8 else "p2p"
             else:
                 transport = "nccl"
-        if transport not in ("p2p", "copy", "nccl"):
+        if transport not in ("p2p", "copy", "nccl", "home"):
             raise ValueError(f"unknown transport {transport!r}")
+        if transport == "home" and stages is not None:
+            raise ValueError("the home transport runs the native stages only")
         self.transport = transport
         if chunks is None:
             # 2 and 4 ranks: one chunk (a chunk's fixed expert-stage cost exceeds the transfer time
@@ -229,6 +273,8 @@ class ExpertParallelMoE:
             chunks = 6 if (transport == "copy" and self.world >= 8 and (max_tokens or 0) >= 4096) else 1
         if chunks < 1:
             raise ValueError("chunks must be >= 1")
+        if transport == "home" and chunks != 1:
+            raise ValueError("the home transport runs one chunk per forward")
         self.chunks = int(chunks)
         if stages is None:
             # SMs the persistent GEMMs leave free for the dispatch / combine kernels and NCCL that run
@@ -240,7 +286,8 @@ class ExpertParallelMoE:
         self.last_exchange = None
         self._streams = None
         self._copy_streams = None
-        if transport in ("p2p", "copy"):
+        self._home_buf = None
+        if transport in ("p2p", "copy", "home"):
             if max_tokens is None or hidden_size is None:
                 raise ValueError("the p2p transport needs max_tokens and hidden_size to size its shared buffers")
             self.max_tokens = int(max_tokens)
@@ -252,7 +299,8 @@ class ExpertParallelMoE:
             self._send_chunk_bytes = max(self._send_cap, 1) * rb
             self._out_chunk_bytes = max(self._out_cap, 1) * hidden_size * 2
             self._send_buf = IpcBuffer(self.chunks * self._send_chunk_bytes, group)
-            self._out_buf = IpcBuffer(self.chunks * self._out_chunk_bytes, group)
+            if transport != "home":
+                self._out_buf = IpcBuffer(self.chunks * self._out_chunk_bytes, group)
             if transport == "copy":
                 # local landing buffers: the records of every source, the partial rows of every owner
                 dev = torch.device("cuda", torch.cuda.current_device())
@@ -268,6 +316,28 @@ class ExpertParallelMoE:
         if shp[0] != self.El:
             raise ValueError(f"w1_local holds {shp[0]} experts, expected {self.El}")
         self.I = shp[1] // 2
+        if transport == "home":
+            self._setup_home(hidden_size)
+
+    def _setup_home(self, H):
+        """Replicate w2 over the group and map every rank's intermediate buffer: rows of the
+        padded layout of up to max_tokens * K entries over all E experts, e4m3 + scale atoms."""
+        I, W = self.I, self.world
+        if tuple(self.w2.shape) != (self.El, H, I):
+            raise ValueError(f"w2_local has shape {tuple(self.w2.shape)}, expected {(self.El, H, I)}")
+        if W > 1:
+            q = torch.empty((W * self.El,) + tuple(self.w2.q.shape[1:]), dtype=torch.uint8, device=self.w2.q.device)
+            sf = torch.empty((W * self.El,) + tuple(self.w2.sf.shape[1:]), dtype=torch.uint8, device=self.w2.sf.device)
+            dist.all_gather_into_tensor(q, self.w2.q.contiguous(), group=self.group)
+            dist.all_gather_into_tensor(sf, self.w2.sf.contiguous(), group=self.group)
+            self.w2_full = Fp8ExpertWeights(q, sf, False)
+        else:
+            self.w2_full = self.w2
+        self._home_rows = max_padded_blocks(self.max_tokens * self.K, self.E) * 128
+        self._home_q_bytes = -(-self._home_rows * I // 256) * 256
+        self._home_sf_shape = (self._home_rows // 128, -(-I // 512), 512)
+        sf_bytes = self._home_sf_shape[0] * self._home_sf_shape[1] * 512
+        self._home_buf = IpcBuffer(self._home_q_bytes + max(sf_bytes, 16), self.group)
 
     # ---- collectives -------------------------------------------------------------------------
     def _a2a(self, out, inp, out_splits=None, in_splits=None):
@@ -285,21 +355,30 @@ class ExpertParallelMoE:
     def close(self):
         """Unmap and free the shared buffers (collective: call on every rank)."""
         if self._send_buf is not None:
+            bufs = [b for b in (self._send_buf, self._out_buf, self._home_buf) if b is not None]
             torch.cuda.synchronize()
-            dist.barrier(group=self.group)  # nobody reads a peer buffer any more
-            self._send_buf.unmap()
-            self._out_buf.unmap()
+            dist.barrier(group=self.group)  # nobody reads or writes a peer buffer any more
+            for b in bufs:
+                b.unmap()
             torch.cuda.synchronize()
             dist.barrier(group=self.group)  # every peer mapping is gone
-            self._send_buf.free()
-            self._out_buf.free()
-            self._send_buf = self._out_buf = None
+            for b in bufs:
+                b.free()
+            self._send_buf = self._out_buf = self._home_buf = None
 
     def _note_exchange(self, records_in_remote: int, records_out_remote: int, H: int, rb: int):
         """Bytes this rank received over NVLink in the last forward: records from other ranks, and
         the partial rows other ranks computed for this rank's records (roofline of the exchange)."""
         self.last_exchange = {"records_in_remote": records_in_remote, "rows_back_remote": records_out_remote,
                               "bytes_in": records_in_remote * rb + records_out_remote * H * 2}
+
+    def _note_exchange_home(self, records_in_remote: int, entries_back_remote, rb: int):
+        """Home transport: records from other ranks plus the e4m3 intermediate rows (I bytes + I/128
+        scale bytes) other ranks computed for this rank's entries; the count of those entries stays
+        a device tensor until read."""
+        row = self.I + self.I // 128
+        self.last_exchange = {"records_in_remote": records_in_remote, "entries_back_remote": entries_back_remote,
+                              "bytes_in": entries_back_remote.double() * row + records_in_remote * rb}
 
     def _exchange_counts(self, st, stream, device):
         """Collective on `stream`: every rank's per-destination record counts of one chunk (and, since
@@ -394,6 +473,59 @@ class ExpertParallelMoE:
             t.record_stream(caller)
         self._note_exchange(sum(C_[q][me] for C_, _ in counts for q in range(W) if q != me),
                             sum(C_[me][d] for C_, _ in counts for d in range(W) if d != me), H, rb)
+        return out, logits, freq
+
+    def _forward_home(self, x: torch.Tensor):
+        """Home-down forward, all on one high-priority stream:
+
+          router, top-k, this rank's routing plan over all E experts, records carrying each
+          entry's row in that plan's padded layout
+          count exchange (all-gather; also: every rank's records are complete, and every rank has
+                          finished the down projection that read its intermediate last forward)
+          up stage       records pulled from the peers' send buffers, up GEMM whose epilogue
+                          stores each row into its token's home intermediate (peer stores)
+          all-reduce     of the error word: every rank's rows have landed in every home
+          down stage     down GEMM + top-k combine over this rank's own plan, replicated w2
+        """
+        from . import ops
+
+        T, H = x.shape
+        W, K, me = self.world, self.K, self.rank
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the shared buffers")
+        dev = x.device
+        caller = torch.cuda.current_stream(dev)
+        if self._streams is None:
+            self._streams = (torch.cuda.Stream(dev, priority=-1), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        s_main = self._streams[0]
+        s_main.wait_stream(caller)
+        rb = self.stages.record_bytes(H, K)
+        with torch.cuda.stream(s_main):
+            logits = F.linear(x, self.router_w.to(x.dtype))
+            errs = torch.zeros(1, dtype=torch.int32, device=dev)
+            scores, idx = ops.router_topk(logits, K, self.sot, self.norm)
+            plan = ops.route_plan(idx, self.E, errs)
+            records = _RawRows(self._send_buf.ptr, self._send_cap, rb)
+            st = self.stages.dispatch_records(x, scores, idx, plan, self.E, W, errs, records=records)
+        C, _ = self._exchange_counts(st, s_main, dev)
+        with torch.cuda.stream(s_main):
+            recv_counts = [C[q][me] for q in range(W)]
+            seg_off = [sum(C[q][:me]) for q in range(W)]
+            home_q = list(self._home_buf.peers)
+            home_sf = [p + self._home_q_bytes for p in home_q]
+            freq = self.stages.expert_up_p2p(self._send_buf.peers, seg_off, recv_counts, H, self.I, self.El, K,
+                                             self.w1, home_q, home_sf, self._home_rows, errs, dev)
+            if W > 1:
+                dist.all_reduce(errs, group=self.group)  # every rank's rows have landed in every home
+            out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+            aq = _RawRows(self._home_buf.ptr, self._home_rows, self.I)
+            asf = _RawRows(self._home_buf.ptr + self._home_q_bytes, self._home_sf_shape[0], 1024)
+            ops.moe_down_combine(aq, asf, self.w2_full, plan, scores.view(-1), T, errs, out=out)
+            remote = (idx // self.El != me).sum()
+        caller.wait_stream(s_main)
+        for t in (logits, out, freq, remote):
+            t.record_stream(caller)
+        self._note_exchange_home(sum(C[q][me] for q in range(W) if q != me), remote, rb)
         return out, logits, freq
 
     def _forward_copy(self, x: torch.Tensor):
@@ -542,6 +674,8 @@ class ExpertParallelMoE:
             return self._forward_p2p(x)
         if self.transport == "copy":
             return self._forward_copy(x)
+        if self.transport == "home":
+            return self._forward_home(x)
         T, H = x.shape
         W, K = self.world, self.K
         if chunks is None:

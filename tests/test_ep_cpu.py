@@ -112,3 +112,18 @@ def test_check_counts():
     assert check_counts([1, 2], [3, 4], 10) == ""
     assert "negative" in check_counts([1, -1], [0, 0], 10)
     assert "exceed" in check_counts([6, 6], [0, 0], 10)
+
+
+def test_home_transport_arguments():
+    """The home transport needs the native stages (its up stage stores into peer memory) and runs
+    one chunk per forward; both are rejected before any buffer is allocated."""
+    from _ep_fakes import FakeStages
+    from sonicmoe.ep import ExpertParallelMoE
+
+    x, rw, w1, w2 = _inputs()
+    with pytest.raises(ValueError, match="native stages"):
+        ExpertParallelMoE(rw, w1, w2, E, K, stages=FakeStages(), transport="home")
+    with pytest.raises(ValueError, match="one chunk"):
+        ExpertParallelMoE(rw, w1, w2, E, K, transport="home", chunks=2)
+    with pytest.raises(ValueError, match="unknown transport"):
+        ExpertParallelMoE(rw, w1, w2, E, K, stages=FakeStages(), transport="bogus")

@@ -110,6 +110,80 @@ def test_ep_p2p_kernels_emulated_ranks(W, T, H, I, E, K):
     assert rel_fro(o_all.float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
 
 
+def _home_emulated(W, T, H, I, E, K, seed, corrupt=False):
+    """Home-down stages with W virtual ranks on one GPU: every owner's up GEMM stores its rows into
+    the W separate home buffers (the peer-store address arithmetic), then every home runs the down
+    projection over its own plan with all experts' w2."""
+    import torch.nn.functional as F
+
+    from sonicmoe import ops
+    from sonicmoe.ep import NativeStages
+    from sonicmoe.ops import weight_prep
+
+    x, rw, w1, w2 = make_layer_inputs(W * T, H, I, E, seed=seed)
+    dev = torch.device("cuda", 0)
+    xg, rwg = x.to(dev), rw.to(dev)
+    El = E // W
+    st = NativeStages()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    rb = st.record_bytes(H, K)
+    home_rows = ops.max_padded_blocks(T * K, E) * 128
+    send = [torch.empty(T * min(K, W), rb, dtype=torch.uint8, device=dev) for _ in range(W)]
+    home_q = [torch.empty(home_rows, I, dtype=torch.uint8, device=dev) for _ in range(W)]
+    home_sf = [torch.zeros(home_rows // 128, -(-I // 512), 512, dtype=torch.uint8, device=dev) for _ in range(W)]
+    states, plans, logits = [], [], []
+    for r in range(W):
+        xr = xg[r * T:(r + 1) * T].contiguous()
+        lg = F.linear(xr, rwg)
+        scores, idx = ops.router_topk(lg, K, True, False)
+        plan = ops.route_plan(idx, E, err)
+        states.append(st.dispatch_records(xr, scores, idx, plan, E, W, err, records=send[r]))
+        plans.append(plan)
+        logits.append(lg)
+    C = [s_.send_counts.cpu().tolist() for s_ in states]
+    if corrupt:
+        # one record of rank 0 names a home row past the end of the home buffer
+        meta = (H + H // 128 + 15) // 16 * 16 + 8 * K
+        row = send[0][0, meta:meta + 4 * K].view(torch.int32)
+        row[:] = torch.where(row >= 0, torch.full_like(row, home_rows + 5), row)
+    w2_full = weight_prep(w2.to(dev))
+    freqs = []
+    for d in range(W):
+        w1p = weight_prep(w1[d * El:(d + 1) * El].to(dev))
+        recv_counts = [C[s_][d] for s_ in range(W)]
+        seg_off = [sum(C[s_][:d]) for s_ in range(W)]
+        freqs.append(st.expert_up_p2p([b.data_ptr() for b in send], seg_off, recv_counts, H, I, El, K, w1p,
+                                      [q.data_ptr() for q in home_q], [f.data_ptr() for f in home_sf], home_rows,
+                                      err, dev))
+    outs = []
+    for r in range(W):
+        o = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+        ops.moe_down_combine(home_q[r], home_sf[r], w2_full, plans[r], states[r].topk_scores.view(-1), T, err, out=o)
+        outs.append(o)
+    torch.cuda.synchronize()
+    return x, w1, w2, torch.cat(outs), torch.cat(logits), torch.cat(freqs), err.item()
+
+
+@pytest.mark.parametrize("W,T,H,I,E,K", [(4, 200, 512, 256, 16, 4), (3, 150, 256, 128, 12, 8),
+                                         (2, 333, 256, 384, 8, 8)])
+def test_ep_home_kernels_emulated_ranks(W, T, H, I, E, K):
+    """Up projection at the experts' owners with its rows stored into the tokens' home buffers,
+    down projection + combine at home: same output as the single-GPU layer's oracle."""
+    x, w1, w2, o_all, logits, freq, e = _home_emulated(W, T, H, I, E, K, seed=5 * W + T)
+    assert e == 0
+    o_ref, _, idx = fp8_oracle(x.float().numpy(), logits.float().cpu().numpy(), w1.float().numpy(),
+                               w2.float().numpy(), K)
+    np.testing.assert_array_equal(freq.cpu().numpy(), np.bincount(idx.reshape(-1), minlength=E))
+    assert rel_fro(o_all.float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
+
+
+def test_ep_home_bad_return_row_is_reported():
+    """A record whose home row lies past the home buffer: the up epilogue drops those rows and
+    writes error 202 instead of storing outside the buffer."""
+    *_, e = _home_emulated(2, 64, 256, 128, 8, 4, seed=9, corrupt=True)
+    assert e == 202
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -152,7 +226,7 @@ def _nccl_worker(rank, W, port, q, T, H, I, E, K, transport, chunks):
 
 
 @pytest.mark.parametrize("transport,chunks", [("p2p", 1), ("p2p", 2), ("p2p", 3), ("copy", 1), ("copy", 2),
-                                              ("copy", 3), ("copy", 6), ("nccl", 1), ("nccl", 2)])
+                                              ("copy", 3), ("copy", 6), ("nccl", 1), ("nccl", 2), ("home", 1)])
 def test_ep_multi_gpu(transport, chunks):
     """W processes, one per GPU.  chunks > 1 runs the pipelined forward (dispatch, expert stage and
     combine of different token chunks on different streams); chunks=3 and 6 leave the last chunk
