@@ -2,14 +2,14 @@
 
 Four transports move the records and returned rows between the ranks of one node:
 
-* ``"p2p"`` (default on GPUs): every rank's send buffer and output rows live in CUDA IPC memory
+* ``"p2p"``: every rank's send buffer and output rows live in CUDA IPC memory
   mapped by all ranks; the receiver's pack kernel and the owner's combine kernel read them with
   peer loads over NVLink, so no separate all-to-all copies the data.  NCCL carries only the
   per-destination counts (an all-gather that also orders the stages) and one tiny all-reduce.
 * ``"copy"``: the same shared buffers, but record segments and partial rows cross NVLink as plain
   device-to-device copies (copy engines, no SMs) into local buffers, pipelined over token chunks.
 * ``"nccl"``: ``all_to_all_single`` of the records and of the partial rows.
-* ``"home"``: the records move as in ``"p2p"``, but an expert's owner runs only the up projection,
+* ``"home"`` (default on GPUs, see ``default_transport``): the records move as in ``"p2p"``, but an expert's owner runs only the up projection,
   whose epilogue stores each entry's e4m3 intermediate row (I + I/128 bytes) straight into the
   padded layout of the token's own rank over NVLink; that rank then runs the down projection with
   the fused top-k combine over its own routing plan, with every expert's w2 replicated on every
@@ -229,6 +229,23 @@ def check_counts(send_counts, recv_counts, capacity: int) -> str:
     return ""
 
 
+def default_transport(world: int, native: bool = True, chunks: int = None) -> str:
+    """Transport chosen when the caller names none.
+
+    Measured at config 2 with 2 ranks: the home-down transport 4.08 ms per forward against 4.34 for
+    peer loads with the down projection at the owners (the bytes back per rank are 6x smaller for
+    e4m3 intermediate rows than for bf16 partial rows, and the home's down projection reduces into
+    its own T output rows instead of one partial row per received record).  A caller that asks
+    for chunks > 1 gets the chunked transports of the earlier measurements instead (peer loads up
+    to 4 ranks, copy-engine transfers from 8); device-stage stand-ins (tests) take NCCL.
+    """
+    if not native or world <= 1:
+        return "nccl"
+    if chunks is None or chunks == 1:
+        return "home"
+    return "copy" if world >= 8 else "p2p"
+
+
 class ExpertParallelMoE:
     """FP8 SwiGLU MoE layer whose experts are sharded over `group` (torch.distributed, NCCL).
 
@@ -255,12 +272,7 @@ class ExpertParallelMoE:
             raise ValueError("`norm_topk_prob` only works with softmax-then-topk")
         self.stages = stages if stages is not None else NativeStages()
         if transport is None:
-            # measured at config 2: peer loads win up to 4 ranks; at 8 the exchanged volume is large
-            # enough that copy-engine transfers hidden under the GEMMs of 6 chunks win
-            if stages is None and self.world > 1:
-                transport = "copy" if self.world >= 8 else "p2p"
-            else:
-                transport = "nccl"
+            transport = default_transport(self.world, native=stages is None, chunks=chunks)
         if transport not in ("p2p", "copy", "nccl", "home"):
             raise ValueError(f"unknown transport {transport!r}")
         if transport == "home" and stages is not None:

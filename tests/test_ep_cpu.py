@@ -127,3 +127,16 @@ def test_home_transport_arguments():
         ExpertParallelMoE(rw, w1, w2, E, K, transport="home", chunks=2)
     with pytest.raises(ValueError, match="unknown transport"):
         ExpertParallelMoE(rw, w1, w2, E, K, stages=FakeStages(), transport="bogus")
+
+
+def test_default_transport():
+    """One process or device-stage stand-ins: NCCL; several GPUs: the home-down transport, unless
+    the caller asks for a chunked forward (peer loads, or copy engines from 8 ranks)."""
+    from sonicmoe.ep import default_transport
+
+    assert default_transport(1) == "nccl"
+    assert default_transport(8, native=False) == "nccl"
+    assert default_transport(2) == "home" and default_transport(8) == "home"
+    assert default_transport(4, chunks=1) == "home"
+    assert default_transport(4, chunks=2) == "p2p"
+    assert default_transport(8, chunks=6) == "copy"
