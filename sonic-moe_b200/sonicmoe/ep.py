@@ -229,6 +229,22 @@ def check_counts(send_counts, recv_counts, capacity: int) -> str:
     return ""
 
 
+def check_count_matrix(C, send_cap: int, out_cap: int, me: int) -> str:
+    """Validation of a whole all-gathered count matrix C[s][d] (records from s to d), identical on
+    every rank that holds the same C: the first failing rank's message (prefixed with the rank
+    when it is not `me`), or ''.  Every rank therefore raises together without a second
+    collective to agree on the verdict."""
+    W = len(C)
+    for r in range(W):
+        recv = [C[s][r] for s in range(W)]
+        msg = check_counts(C[r], recv, send_cap)
+        if not msg and sum(recv) > out_cap:
+            msg = f"{sum(recv)} received records exceed the output region ({out_cap})"
+        if msg:
+            return msg if r == me else f"a peer rank ({r}) failed its check: {msg}"
+    return ""
+
+
 def default_transport(world: int, native: bool = True, chunks: int = None) -> str:
     """Transport chosen when the caller names none.
 
@@ -395,21 +411,18 @@ class ExpertParallelMoE:
     def _exchange_counts(self, st, stream, device):
         """Collective on `stream`: every rank's per-destination record counts of one chunk (and, since
         a rank's all-gather runs after its dispatch, the guarantee that every send region of the
-        chunk is complete), validated and agreed on all ranks.  Returns (C[s][d], ready event)."""
+        chunk is complete), validated on every rank over the whole matrix, so that all ranks reach
+        the same verdict with no further collective.  Returns (C[s][d], ready event)."""
         W = self.world
         with torch.cuda.stream(stream):
             allc = torch.empty(W * W, dtype=torch.int32, device=device)
             dist.all_gather_into_tensor(allc, st.send_counts, group=self.group)
             C = allc.view(W, W).cpu().tolist()  # C[s][d]: records of this chunk from s to d
-            me = self.rank
-            msg = check_counts(C[me], [C[s_][me] for s_ in range(W)], self._send_cap)
-            if not msg and sum(C[s_][me] for s_ in range(W)) > self._out_cap:
-                msg = f"{sum(C[s_][me] for s_ in range(W))} received records exceed the output region ({self._out_cap})"
-            ok = self._agree(msg == "", device)
+            msg = check_count_matrix(C, self._send_cap, self._out_cap, self.rank)
             ev = torch.cuda.Event()
             ev.record(stream)
-        if not ok:
-            raise RuntimeError(f"expert-parallel exchange aborted on every rank: {msg or 'a peer rank failed its check'}")
+        if msg:
+            raise RuntimeError(f"expert-parallel exchange aborted on every rank: {msg}")
         return C, ev
 
     def _forward_p2p(self, x: torch.Tensor):
@@ -585,16 +598,13 @@ class ExpertParallelMoE:
             dist.all_gather_into_tensor(allc, mine.view(-1), group=self.group)
             A = allc.view(W, Cn, W).cpu().tolist()  # A[s][c][d]: records of chunk c from s to d
             msg = ""
-            for c in range(Cn):
-                sent, recv = A[me][c], [A[q][c][me] for q in range(W)]
-                msg = msg or check_counts(sent, recv, self._send_cap)
-                if not msg and sum(recv) > self._out_cap:
-                    msg = f"{sum(recv)} received records exceed the output region ({self._out_cap})"
-            ok = self._agree(msg == "", dev)
+            for c in range(Cn):  # the whole matrix on every rank: the same verdict everywhere
+                msg = msg or check_count_matrix([[A[q][c][d] for d in range(W)] for q in range(W)],
+                                                self._send_cap, self._out_cap, me)
             ev_counts = torch.cuda.Event()
             ev_counts.record(s_main)
-        if not ok:
-            raise RuntimeError(f"expert-parallel exchange aborted on every rank: {msg or 'a peer rank failed its check'}")
+        if msg:
+            raise RuntimeError(f"expert-parallel exchange aborted on every rank: {msg}")
 
         def copy(dst, src, nbytes, stream):
             nat.call("sm_copy_d2d_async", dst, src, nbytes, stream.cuda_stream)

@@ -140,3 +140,19 @@ def test_default_transport():
     assert default_transport(4, chunks=1) == "home"
     assert default_transport(4, chunks=2) == "p2p"
     assert default_transport(8, chunks=6) == "copy"
+
+
+def test_check_count_matrix_same_verdict_on_every_rank():
+    """Every rank validates the whole all-gathered matrix: a bad row of rank 1 fails on both ranks,
+    with rank 1's own message there and a peer message on rank 0."""
+    from sonicmoe.ep import check_count_matrix
+
+    ok = [[3, 4], [5, 6]]
+    assert check_count_matrix(ok, 12, 20, 0) == "" and check_count_matrix(ok, 12, 20, 1) == ""
+    bad = [[3, 4], [5, -1]]
+    assert "negative record count" in check_count_matrix(bad, 12, 20, 1)
+    m0 = check_count_matrix(bad, 12, 20, 0)
+    assert "peer rank (1)" in m0 and "negative" in m0
+    over = [[3, 9], [5, 9]]  # rank 1 receives 18 records, more than its output region of 12
+    assert "exceed the output region" in check_count_matrix(over, 20, 12, 1)
+    assert "peer rank (1)" in check_count_matrix(over, 20, 12, 0)
