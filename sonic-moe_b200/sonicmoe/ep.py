@@ -32,10 +32,16 @@ its blog).  One process per GPU; rank d of W owns the contiguous global experts
   exchange   NCCL all-to-all of the bf16 partial rows back to the token owners
   combine    sm_ep_combine: fp32 sum of each token's partial rows, rounded once to bf16
 
+The home transport instead runs: router top-k and this rank's routing plan over all E experts,
+records carrying each entry's row in that plan, the count all-gather, the up stage (records pulled
+from the peers' send buffers, rows stored into the tokens' home intermediates), one all-reduce,
+and the down projection with the top-k combine over the rank's own plan.
+
 The record counts are read on the host between the two exchanges (one small device-to-host copy
 per forward), and every rank checks them before any data moves; a bad count on any rank makes all
-ranks raise together (the check is itself a collective), so no rank is left waiting in a
-collective the others skipped.
+ranks raise together (the NCCL transport agrees on the verdict with a collective; the peer-memory
+transports all-gather the whole count matrix, so every rank checks every rank's counts and
+reaches the same verdict), so no rank is left waiting in a collective the others skipped.
 """
 import ctypes
 from dataclasses import dataclass
