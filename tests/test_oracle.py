@@ -230,3 +230,31 @@ def test_fp8_oracle_rows_matches_whole_layer_oracle():
         rows = np.array([0, 5, 17, 23])
         sub = layer.fp8_oracle_rows(x[rows], scores[rows], idx[rows], lambda e: (w1[e], w2[e]), concat)
         np.testing.assert_allclose(sub.numpy(), o.numpy()[rows], rtol=1e-12, atol=1e-12)
+
+
+def test_home_rows_layout_invariants():
+    """The home-down expert-parallel path writes entry (t, k) of a rank's tokens into row
+    s_rev - off[e] + off_pad[e] of that rank's padded layout, encoded as (source rank << 27) | row,
+    and its scale byte for k-group g into atom ((row/128)*KG + g/4)*512 + 16*(row%32) +
+    4*((row%128)/32) + g%4.  On random routing: the rows are a bijection onto each expert's valid
+    rows, stay below max_padded_blocks(T*K, E)*128, survive the encoding, and no two (row, k-group)
+    pairs share a scale byte inside the atom buffer."""
+    rs = np.random.RandomState(11)
+    T, E, K, I, W = 300, 24, 6, 384, 3
+    idx = np.stack([rs.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
+    freq, off, _, _, s_rev = metadata.tc_metadata(idx, E)
+    off_pad, _, nblk = metadata.padded_layout(freq)
+    rows = metadata.padded_rows(idx, s_rev, off, off_pad)
+    max_rows = ((T * K + 127) // 128 + min(T * K, E)) * 128  # sm_max_padded_blocks(T*K, E) * 128
+    assert nblk * 128 <= max_rows and rows.max() < max_rows
+    assert len(np.unique(rows)) == T * K
+    e = idx.reshape(-1)
+    assert np.all(rows >= off_pad[e]) and np.all(rows < off_pad[e] + freq[e])
+    for s in range(W):
+        code = (s << 27) | rows
+        assert np.all(code >> 27 == s) and np.all(code & ((1 << 27) - 1) == rows)
+    KG = -(-(I // 128) // 4)
+    g = np.arange(I // 128)
+    r = rows[:, None]
+    byte = ((r // 128) * KG + g // 4) * 512 + 16 * (r % 32) + 4 * ((r % 128) // 32) + g % 4
+    assert len(np.unique(byte)) == byte.size and byte.max() < (max_rows // 128) * KG * 512
