@@ -53,7 +53,7 @@ const char* sm_version(void);
 /*
  * Router top-k.  Replaces the custom op `sonicmoe::_softmax_topk_fwd`
  * (reference sonicmoe/functional/forward.py:107-141) and its CuTe kernel
- * (sonicmoe/functional/topk.py:241-419).
+ * (sonicmoe/functional/topk.py:143-260).
  *   logits [T, E] (dtype SM_DTYPE_*), scores [T, K] float32, indices [T, K] int32, both in
  *   descending score order; equal scores go to the lower expert index.
  *   softmax_over_topk = 1: softmax over the k selected logits; = 0: top-k of the full-row softmax,
@@ -100,9 +100,11 @@ int sm_general_route_metadata(const int32_t* sorted_token_idx, const int32_t* ex
  * counts and the padded layout) lives in a 1 MiB static device array that each GPU loading the
  * library keeps until the process exits; shapes needing more (E * ceil(T/128) + T*K/128 + 2E
  * int32 entries, roughly) return SM_EINVAL.  Same outputs as sm_route_metadata.  The first call
- * on a device looks up the array's address and should come before any stream capture.  All calls
- * share the array: calls that overlap on the GPU race, so the caller serialises them.
- * Allocates nothing (no cudaMalloc / cudaFree).
+ * on a device looks up the array's address and should come before any stream capture.  The
+ * address is kept per device with the id of the CUDA context it was taken in; after a device
+ * reset (a new primary context) the next call looks it up again, so that call too belongs before
+ * any capture.  All calls share the array: calls that overlap on the GPU race, so the caller
+ * serialises them.  Allocates nothing (no cudaMalloc / cudaFree).
  */
 int sm_route_metadata_noalloc(const int32_t* topk_indices, int T, int K, int E, int32_t* expert_frequency,
                               int32_t* expert_frequency_offset, int32_t* x_gather_idx, int32_t* s_scatter_idx,
@@ -207,6 +209,12 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
                         const int32_t* off_pad, const int32_t* expert_frequency_offset,
                         const int32_t* expert_frequency, const int32_t* s_scatter_idx, const int32_t* x_gather_idx,
                         const float* topk_scores, void* out, int32_t* err, void* stream);
+
+/* Number of output-column slices (1, 2 or 4) sm_moe_down_combine visits for T output rows of
+ * width H: the largest split whose bf16 slab T x (H / slices) exceeds no 80 MB share of L2.
+ * Introspection only (no counterpart in the reference): lets callers and tests know which tile
+ * order a shape runs. */
+int sm_moe_down_slices(int T, int H);
 
 /*
  * Expert parallelism (no counterpart in the reference, which is single-GPU: its blog lists EP as

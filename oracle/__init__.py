@@ -11,7 +11,7 @@ Modules and what pins them:
   Taylor polynomial; frexp + atanh series).  The CUDA router uses the same sequence of IEEE
   single operations, so routing scores are bit-exact between the two.
 * ``routing``  -- restatement of the reference top-k router
-  (``sonicmoe/functional/topk.py:241-419``): index bits written into the low mantissa bits,
+  (``sonicmoe/functional/topk.py:143-260``): index bits written into the low mantissa bits,
   descending order with ties to the lower expert, softmax over the top-k, or log-softmax ->
   top-k -> exp (+renorm).  PINNED: against the reference's own torch routing
   (``sonicmoe/functional/forward.py:128-141``) on the committed golden vectors

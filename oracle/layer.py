@@ -164,7 +164,8 @@ def fp8_oracle_rows(x_rows, scores_rows, idx_rows, expert_weights, concat_layout
     x_rows: [n, H] activations (bf16 values as float32); scores_rows / idx_rows: [n, K] routing of
     those tokens (K may be ragged by padding idx with -1); expert_weights(e) -> (w1_e [2I, H],
     w2_e [H, I]) float32 in the caller's layout.  Each touched expert is quantised once with the
-    same 128x128 blocks as the whole-layer oracle, so per row the result equals ``fp8_oracle``'s.
+    same 128x128 blocks as the whole-layer oracle (through ``quant.fake_quant_128x128_fast``, which
+    is pinned bit for bit to the spec path), so per row the result equals ``fp8_oracle``'s.
     """
     x_rows = np.asarray(x_rows, dtype=np.float32)
     idx_rows = np.asarray(idx_rows)
@@ -177,8 +178,8 @@ def fp8_oracle_rows(x_rows, scores_rows, idx_rows, expert_weights, concat_layout
         w1e, w2e = expert_weights(int(e))
         w1e = np.asarray(w1e, dtype=np.float32)[None]
         w2e = np.asarray(w2e, dtype=np.float32)[None]
-        w1t = torch.as_tensor(quant.dequant_128x128(*quant.quant_128x128(w1e))[0]).double()
-        w2t = torch.as_tensor(quant.dequant_128x128(*quant.quant_128x128(w2e))[0]).double()
+        w1t = torch.as_tensor(quant.fake_quant_128x128_fast(w1e)[0]).double()
+        w2t = torch.as_tensor(quant.fake_quant_128x128_fast(w2e)[0]).double()
         I = w1t.shape[0] // 2
         t_idx, k_idx = np.nonzero(idx_rows == e)
         t_idx = torch.as_tensor(t_idx).long()

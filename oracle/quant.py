@@ -159,3 +159,23 @@ def weight_sf_atoms(sf: np.ndarray) -> np.ndarray:
             for c in range(4):
                 out[:, :, g // 4, 16 * lane + 4 * c + (g % 4)] = sf[:, :, g]
     return out
+
+
+def fake_quant_128x128_fast(w: np.ndarray) -> np.ndarray:
+    """Dequantised 128x128-block e4m3 weights, ``dequant_128x128(*quant_128x128(w))``, computed
+    with torch's ``float8_e4m3fn`` conversion (IEEE round to nearest even) instead of the
+    element-by-element encoder above, for the full-size parity tests (tens of millions of values
+    per expert).  The scale step is the spec's own (``ceil_log2_f32`` of the float32 quotient
+    amax / 448), and every scaled value lies in [-448, 448], where torch's conversion needs no
+    saturation; ``tests/test_oracle.py`` pins the result bit for bit against the spec path."""
+    import torch
+
+    wt = torch.as_tensor(np.asarray(w, dtype=F32))
+    E, N, K = wt.shape
+    assert N % 128 == 0 and K % 128 == 0
+    blocks = wt.view(E, N // 128, 128, K // 128, 128)
+    amax = blocks.abs().amax(dim=(2, 4))  # [E, N/128, K/128], exact
+    e = torch.from_numpy(ceil_log2_f32((amax.numpy() / F32(E4M3_MAX)).astype(F32)).astype(np.float32))
+    inv = torch.exp2(-e)[:, :, None, :, None]  # exact powers of two
+    q = (blocks * inv).to(torch.float8_e4m3fn).to(torch.float32)
+    return (q * torch.exp2(e)[:, :, None, :, None]).reshape(E, N, K).numpy()

@@ -2,15 +2,15 @@
 
 Follows ``sonicmoe/functional/topk.py`` of the reference:
 
-* ``topk.py:281-339``  (TOPK_OVER_SOFTMAX) full-row log-softmax before selection:
+* ``topk.py:143-198``  (TOPK_OVER_SOFTMAX) full-row log-softmax before selection:
   ``logp = x - (max + log(sum_exp))``.
-* ``topk.py:341-356``  the column index is written into the low ``log2(next_pow2(E))`` mantissa
+* ``topk.py:200-215``  the column index is written into the low ``log2(next_pow2(E))`` mantissa
   bits of the float32 score, inverted (``~col``) when the score is ``>= 0`` so that on equal
   scores the LOWER column wins; the original low bits are discarded (for top-k-over-softmax
   this truncates the log-probabilities before ranking).
-* ``topk.py:362-375``  descending top-k, then the bits are cleared and the index decoded
+* ``topk.py:222-234``  descending top-k, then the bits are cleared and the index decoded
   (``~enc`` when the cleared score is ``>= 0``).
-* ``topk.py:377-401``  softmax over the k selected values (SOFTMAX_OVER_TOPK) or ``exp`` of the
+* ``topk.py:237-260``  softmax over the k selected values (SOFTMAX_OVER_TOPK) or ``exp`` of the
   log-probabilities, optionally renormalised to sum to one (``norm_topk_prob``).
 
 What this restatement fixes that the reference leaves to its GPU runtime: the exp/log
@@ -82,7 +82,7 @@ def topk_route(logits, K: int, softmax_over_topk: bool = True, norm_topk_probs: 
     x = np.ascontiguousarray(np.asarray(logits, dtype=F32))
     T, E = x.shape
     if norm_topk_probs and softmax_over_topk:
-        raise ValueError("norm_topk_probs only applies to top-k over softmax (topk.py:194-195)")
+        raise ValueError("norm_topk_probs only applies to top-k over softmax (topk.py:53-54)")
     if not (1 <= K <= E):
         raise ValueError(f"need 1 <= K <= E, got K={K}, E={E}")
     if T == 0:

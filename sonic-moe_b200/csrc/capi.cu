@@ -368,6 +368,11 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
   return cuda_status(launch_moe_down(g, static_cast<cudaStream_t>(stream)), "moe_down_combine");
 }
 
+int sm_moe_down_slices(int T, int H) {
+  if (T < 0 || H <= 0 || H % 256) return fail(SM_EINVAL, "need T >= 0 and H %% 256 == 0 (T=%d H=%d)", T, H);
+  return down_slices(T, H);
+}
+
 int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I, int E, int K,
                    int softmax_over_topk, int norm_topk_probs, int concat_layout, const uint8_t* w1q,
                    const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, void* out,

@@ -27,8 +27,6 @@
 // nothing and no host synchronisation is needed.
 // Every mbarrier wait is bounded (2 s); on a timeout the kernel records an error code, drains its
 // outstanding copies and MMAs with short bounded waits, frees tensor memory and returns.
-#include <cstdlib>
-
 #include "common.cuh"
 #include "sonic_internal.h"
 
@@ -450,17 +448,15 @@ static bool make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t 
 }
 
 // Column slices of the down projection: the largest slice whose bf16 output slab (tokens x slice
-// columns) fits the L2 budget, so the reductions of one slice land in L2.
-// Every slice re-reads all of A, so at most 4 slices: measured best both for the 268 MB token
-// output of config 2 (4 slices of 67 MB) and for the ~1 GB of partial rows an expert-parallel rank
-// reduces into at 4 GPUs (4 slices beat 16).
-static int down_slices(const GemmArgs& g) {
-  const int ntn = g.N / kBN;
-  long long budget = 80ll << 20;
-  if (const char* env = getenv("SONIC_B200_DOWN_SLAB_MB")) budget = atoll(env) << 20;
+// columns) fits an 80 MB share of the L2, so the reductions of one slice land in L2 (swept
+// 300/160/80/40/20 MB at config 2: 80 best).  Every slice re-reads all of A, so at most 4 slices:
+// measured best both for the 268 MB token output of config 2 (4 slices of 67 MB) and for the ~1 GB
+// of partial rows an expert-parallel rank reduces into at 4 GPUs (4 slices beat 16).
+int down_slices(long long tokens, int N) {
+  constexpr long long kSlabBudget = 80ll << 20;
+  const int ntn = N / kBN;
   int slices = 1;
-  while (slices < ntn && slices < 4 && static_cast<long long>(g.tokens) * (g.N / slices) * 2 > budget &&
-         ntn % (slices * 2) == 0)
+  while (slices < ntn && slices < 4 && tokens * (N / slices) * 2 > kSlabBudget && ntn % (slices * 2) == 0)
     slices *= 2;
   return slices;
 }
@@ -486,7 +482,7 @@ static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
   const int grid = static_cast<int>(max_tiles < g.num_sms ? max_tiles : g.num_sms);
   GemmArgs ga = g;
   ga.n_slices = 1;
-  if (!kUp) ga.n_slices = down_slices(g);
+  if (!kUp) ga.n_slices = down_slices(g.tokens, g.N);
   kern<<<grid, kGemmThreads, kSmemAlloc, st>>>(ta, tb, to, ga);
   return cudaGetLastError();
 }

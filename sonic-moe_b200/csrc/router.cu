@@ -1,7 +1,7 @@
 // Router top-k and routing metadata kernels.
 //
 // router_topk_kernel   -- warp-per-row top-k with the reference's index-in-mantissa tie rule
-//                         (sonicmoe/functional/topk.py:241-419) and its two softmax modes, plus a
+//                         (sonicmoe/functional/topk.py:143-260) and its two softmax modes, plus a
 //                         per-128-token tile histogram of the chosen experts for the metadata.
 // route_hist_kernel    -- the same tile histogram for externally supplied expert ids.
 // route_scan_kernel    -- per-expert exclusive scans over tiles, expert offsets and this build's
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
       load_row(row, v);
     }
     if (!softmax_over_topk) {
-      // log-softmax over the full row (topk.py:284-339): max, then sum of exp(x - max) in lane
+      // log-softmax over the full row (topk.py:143-198): max, then sum of exp(x - max) in lane
       // order followed by an xor butterfly (identical result on every lane), then x - log_norm.
       float mx = -__int_as_float(0x7f800000);
 #pragma unroll
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
 #pragma unroll
       for (int i = 0; i < PL; ++i) v[i] = __fsub_rn(v[i], log_norm);
     }
-    // index into the low mantissa bits (topk.py:341-356)
+    // index into the low mantissa bits (topk.py:200-215)
     uint32_t key[PL];
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
         if (lane == k) mysel = wmax;
       }
     }
-    // decode (topk.py:365-375) and score (topk.py:377-401) on lane k for selection k; the K-term
+    // decode (topk.py:222-234) and score (topk.py:237-260) on lane k for selection k; the K-term
     // sum is accumulated in selection order on every lane from the lanes' exps (same operations,
     // same order as a sequential loop over k)
     const bool act = lane < K;

@@ -98,6 +98,10 @@ struct GemmArgs {
 // sm_set_gemm_sm_reserve (left free for communication kernels that run at the same time).
 int gemm_grid_sms();
 
+// Column slices (1, 2 or 4) the down projection splits its output columns into for `tokens` output
+// rows of width N; all tiles of one slice run before the next slice.
+int down_slices(long long tokens, int N);
+
 cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st);
 cudaError_t launch_moe_down(const GemmArgs& g, cudaStream_t st);
 

@@ -53,6 +53,7 @@ SIGNATURES = {
         [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P],
     ),
     "sm_max_padded_blocks": (_I, [_LL, _I]),
+    "sm_moe_down_slices": (_I, [_I, _I]),
     "sm_ep_record_bytes": (_I, [_I, _I]),
     "sm_ep_dispatch_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "sm_ep_dispatch_prepare": (

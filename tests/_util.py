@@ -12,7 +12,7 @@ def seeded(seed: int) -> torch.Generator:
 
 
 def make_layer_inputs(T, H, I, E, seed=1111, x_std=1.0, w_std=0.02):
-    """bf16 x [T,H], router_w [E,H], w1 [E,2I,H], w2 [E,H,I] on the CPU (BASELINE distributions)."""
+    """bf16 x [T,H], router_w [E,H], w1 [E,2I,H], w2 [E,H,I] on the CPU (x ~ N(0, x_std), weights ~ N(0, w_std))."""
     g = seeded(seed)
     x = (torch.randn(T, H, generator=g) * x_std).to(torch.bfloat16)
     rw = (torch.randn(E, H, generator=g) * w_std).to(torch.bfloat16)

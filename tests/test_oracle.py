@@ -34,14 +34,14 @@ def test_routing_matches_reference(golden, case, mode):
     np.testing.assert_array_equal(i, d[f"idx_{mode}_{T}_{E}_{K}"])
     # Softmax over top-k: the bf16 logits lose nothing to the index bits -> fp32 rounding only.
     # Top-k over softmax: the reference kernel drops the low log2(next_pow2(E)) mantissa bits of
-    # the log-probabilities (topk.py:352-356) that its torch branch keeps, so the probability
+    # the log-probabilities (topk.py:213-215) that its torch branch keeps, so the probability
     # differs by up to |logp| * 2^(log2(E) - 23) relative (|logp| < 8 here).
     rtol = 2e-6 if mode == "sot" else 8.0 * 2.0 ** (int(np.ceil(np.log2(E))) - 23)
     np.testing.assert_allclose(s, d[f"scores_{mode}_{T}_{E}_{K}"], rtol=rtol, atol=1e-7)
 
 
 def test_routing_tie_semantics():
-    """Known answers from sonicmoe/functional/topk.py:341-375: equal scores -> lower expert first,
+    """Known answers from sonicmoe/functional/topk.py:200-234: equal scores -> lower expert first,
     for positive and for negative values; output is in descending order."""
     logits = np.array(
         [
@@ -62,7 +62,7 @@ def test_routing_tie_semantics():
 
 def test_routing_truncation_ties_topk_over_softmax():
     """Top-k over softmax ranks log-probs whose low log2(E) mantissa bits are dropped
-    (topk.py:336-356); two logits one float32 ulp apart become a tie won by the lower index."""
+    (topk.py:195-215); two logits one float32 ulp apart become a tie won by the lower index."""
     x = np.zeros((1, 8), dtype=np.float32)
     x[0, 5] = np.float32(1.0)
     x[0, 3] = np.nextafter(np.float32(1.0), np.float32(2.0))  # larger, but only in low bits
@@ -150,6 +150,21 @@ def test_quant_roundtrip_error():
     assert ws.shape == (2, 2, 3)
     wd = quant.dequant_128x128(wq, ws)
     assert layer.rel_fro(wd, w) < 0.05
+
+
+def test_fast_weight_fake_quant_matches_spec():
+    """The torch-conversion fake quantiser used at full sizes equals the spec path bit for bit,
+    including zero blocks, subnormal-scale blocks, round-half-even ties and the 448 edge."""
+    rs = np.random.RandomState(11)
+    w = (rs.randn(3, 256, 384) * 0.02).astype(np.float32)
+    w[0, :128, :128] = 0.0
+    w[1, 128:, 128:256] = rs.randn(128, 128).astype(np.float32) * 1e-39
+    w[2, 0, 0] = 448.0 * 7
+    w[2, 1, :8] = np.float32(448.0 * 7) * np.array([0.5, 0.53125, 0.5625, 1 / 64, 1 / 512, 3 / 1024, -1.0, -0.03125],
+                                                     dtype=np.float32)
+    ref = quant.dequant_128x128(*quant.quant_128x128(w))
+    fast = quant.fake_quant_128x128_fast(w)
+    assert np.array_equal(ref.view(np.uint32), fast.view(np.uint32))
 
 
 def test_sf_atoms_layout():
