@@ -252,20 +252,25 @@ def check_count_matrix(C, send_cap: int, out_cap: int, me: int) -> str:
 
 
 def default_transport(world: int, native: bool = True, chunks: int = None) -> str:
-    """Transport chosen when the caller names none.
+    """Transport chosen when the caller names none, from the measurements at config 2 per rank.
 
-    Measured at config 2 with 2 ranks: the home-down transport 4.08 ms per forward against 4.34 for
-    peer loads with the down projection at the owners (the bytes back per rank are 6x smaller for
-    e4m3 intermediate rows than for bf16 partial rows, and the home's down projection reduces into
-    its own T output rows instead of one partial row per received record).  A caller that asks
-    for chunks > 1 gets the chunked transports of the earlier measurements instead (peer loads up
-    to 4 ranks, copy-engine transfers from 8); device-stage stand-ins (tests) take NCCL.
+    * 2 ranks: the home-down transport (4.08 ms per forward against 4.34 for peer loads with the
+      down projection at the owners, in the same call: the bytes back per rank are 6x smaller for
+      e4m3 intermediate rows than for bf16 partial rows).
+    * 3-7 ranks: peer loads in one chunk (6.00-6.17 ms at 4 ranks; copy engines 6.25).
+    * 8 and more: copy-engine transfers pipelined over 6 chunks (7.01 ms at 8 ranks, against 9.54
+      for one-chunk peer loads).
+    The home-down transport has been measured at 2 ranks only, so it is the default there only.
+    A caller that asks for chunks > 1 gets the chunked transports; device-stage stand-ins (tests)
+    take NCCL.
     """
     if not native or world <= 1:
         return "nccl"
-    if chunks is None or chunks == 1:
+    if world >= 8:
+        return "copy"
+    if world == 2 and (chunks is None or chunks == 1):
         return "home"
-    return "copy" if world >= 8 else "p2p"
+    return "p2p"
 
 
 class ExpertParallelMoE:
@@ -321,6 +326,10 @@ class ExpertParallelMoE:
         self._streams = None
         self._copy_streams = None
         self._home_buf = None
+        # device error word of the last forward (already reduced over the ranks with MAX), read at
+        # the next forward's count exchange -- where the host waits for this stream anyway -- or
+        # by check_errors()
+        self._err_pending = None
         if transport in ("p2p", "copy", "home"):
             if max_tokens is None or hidden_size is None:
                 raise ValueError("the p2p transport needs max_tokens and hidden_size to size its shared buffers")
@@ -373,6 +382,29 @@ class ExpertParallelMoE:
         sf_bytes = self._home_sf_shape[0] * self._home_sf_shape[1] * 512
         self._home_buf = IpcBuffer(self._home_q_bytes + max(sf_bytes, 16), self.group)
 
+    # ---- device error word ----------------------------------------------------------------------
+    def _raise_pending(self):
+        """Raise if the previous forward's kernels recorded an error on any rank.  The word was
+        all-reduced with MAX, so every rank reads the same value and raises at the same point."""
+        pending, self._err_pending = self._err_pending, None
+        if pending is None:
+            return
+        code = int(pending.max().item())
+        if code:
+            raise RuntimeError(f"expert-parallel forward failed: device error {code} "
+                               f"({nat.ERR_NAMES.get(code, 'unknown code')}); its output is not valid")
+
+    def check_errors(self):
+        """Wait for the last forward and raise if any rank's kernels recorded an error.  Every
+        forward also checks the one before it, so only the last forward of a run needs this call."""
+        if self._err_pending is not None and self._err_pending.is_cuda:
+            torch.cuda.synchronize(self._err_pending.device)
+        self._raise_pending()
+
+    def _reduce_err(self, err):
+        if self.world > 1:
+            dist.all_reduce(err, op=dist.ReduceOp.MAX, group=self.group)
+
     # ---- collectives -------------------------------------------------------------------------
     def _a2a(self, out, inp, out_splits=None, in_splits=None):
         if self.world == 1:
@@ -424,6 +456,7 @@ class ExpertParallelMoE:
             allc = torch.empty(W * W, dtype=torch.int32, device=device)
             dist.all_gather_into_tensor(allc, st.send_counts, group=self.group)
             C = allc.view(W, W).cpu().tolist()  # C[s][d]: records of this chunk from s to d
+            self._raise_pending()  # the previous forward ran on this stream and has finished
             msg = check_count_matrix(C, self._send_cap, self._out_cap, self.rank)
             ev = torch.cuda.Event()
             ev.record(stream)
@@ -487,7 +520,8 @@ class ExpertParallelMoE:
             if c + 1 < Cn:  # the host waits for chunk c+1's dispatch while chunk c computes
                 counts[c + 1] = self._exchange_counts(states[c + 1], s_disp, dev)
             with torch.cuda.stream(s_main):
-                dist.all_reduce(errs[c:c + 1], group=self.group)  # every rank's chunk-c rows are complete
+                # every rank's chunk-c rows are complete; MAX keeps one rank's code intact
+                dist.all_reduce(errs[c:c + 1], op=dist.ReduceOp.MAX, group=self.group)
                 ev_rows = torch.cuda.Event()
                 ev_rows.record(s_main)
             with torch.cuda.stream(s_comb):
@@ -502,6 +536,7 @@ class ExpertParallelMoE:
         caller.wait_stream(s_main)
         for t in (logits, out, freq):
             t.record_stream(caller)
+        self._err_pending = errs
         self._note_exchange(sum(C_[q][me] for C_, _ in counts for q in range(W) if q != me),
                             sum(C_[me][d] for C_, _ in counts for d in range(W) if d != me), H, rb)
         return out, logits, freq
@@ -546,8 +581,8 @@ class ExpertParallelMoE:
             home_sf = [p + self._home_q_bytes for p in home_q]
             freq = self.stages.expert_up_p2p(self._send_buf.peers, seg_off, recv_counts, H, self.I, self.El, K,
                                              self.w1, home_q, home_sf, self._home_rows, errs, dev)
-            if W > 1:
-                dist.all_reduce(errs, group=self.group)  # every rank's rows have landed in every home
+            # every rank's rows have landed in every home; MAX keeps one rank's code intact
+            self._reduce_err(errs)
             out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
             aq = _RawRows(self._home_buf.ptr, self._home_rows, self.I)
             asf = _RawRows(self._home_buf.ptr + self._home_q_bytes, self._home_sf_shape[0], 1024)
@@ -556,6 +591,7 @@ class ExpertParallelMoE:
         caller.wait_stream(s_main)
         for t in (logits, out, freq, remote):
             t.record_stream(caller)
+        self._err_pending = errs
         self._note_exchange_home(sum(C[q][me] for q in range(W) if q != me), remote, rb)
         return out, logits, freq
 
@@ -603,6 +639,7 @@ class ExpertParallelMoE:
             allc = torch.empty(W * Cn * W, dtype=torch.int32, device=dev)
             dist.all_gather_into_tensor(allc, mine.view(-1), group=self.group)
             A = allc.view(W, Cn, W).cpu().tolist()  # A[s][c][d]: records of chunk c from s to d
+            self._raise_pending()  # the previous forward ran on this stream and has finished
             msg = ""
             for c in range(Cn):  # the whole matrix on every rank: the same verdict everywhere
                 msg = msg or check_count_matrix([[A[q][c][d] for d in range(W)] for q in range(W)],
@@ -649,7 +686,8 @@ class ExpertParallelMoE:
                 f = self.stages.expert_p2p(bases[c], seg_offs[c], recv_counts, H, self.I, self.El, K, self.w1,
                                            self.w2, self._out_buf.ptr + c * self._out_chunk_bytes, errs[c:c + 1], dev)
                 freq += f
-                dist.all_reduce(errs[c:c + 1], group=self.group)  # every rank's chunk-c rows are complete
+                # every rank's chunk-c rows are complete; MAX keeps one rank's code intact
+                dist.all_reduce(errs[c:c + 1], op=dist.ReduceOp.MAX, group=self.group)
                 ev_rows = torch.cuda.Event()
                 ev_rows.record(s_main)
             # partial rows out of every peer's output region for this rank's chunk-c records
@@ -686,6 +724,7 @@ class ExpertParallelMoE:
         caller.wait_stream(s_main)
         for t in (logits, out, freq):
             t.record_stream(caller)
+        self._err_pending = errs
         self._note_exchange(sum(A[q][c][me] for c in range(Cn) for q in range(W) if q != me),
                             sum(A[me][c][d] for c in range(Cn) for d in range(W) if d != me), H, rb)
         return out, logits, freq
@@ -722,6 +761,7 @@ class ExpertParallelMoE:
         recv = torch.empty_like(send)
         self._a2a(recv, send)
         counts = torch.stack([send, recv]).cpu()
+        self._raise_pending()  # the previous forward ran on this stream and has finished
         sc = [[int(counts[0, d, c]) for d in range(W)] for c in range(chunks)]
         rc = [[int(counts[1, s_, c]) for s_ in range(W)] for c in range(chunks)]
         msg = ""
@@ -756,6 +796,8 @@ class ExpertParallelMoE:
             self._wait(pending_ret[c])
             outs.append(self.stages.combine(ret[c][:sum(sc[c])], states[c].ret_row, bounds[c + 1] - bounds[c], K, H))
         out = torch.cat(outs) if chunks > 1 else outs[0]
+        self._reduce_err(err)
+        self._err_pending = err
         me = self.rank
         self._note_exchange(sum(rc[c][q] for c in range(chunks) for q in range(W) if q != me),
                             sum(sc[c][d] for c in range(chunks) for d in range(W) if d != me), H, rb)

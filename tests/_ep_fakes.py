@@ -22,13 +22,17 @@ def record_bytes(H, K):
 
 
 class FakeStages:
-    def __init__(self, bad_count_rank=None):
+    def __init__(self, bad_count_rank=None, err_code_rank=None, err_code=0):
         self.bad_count_rank = bad_count_rank
+        self.err_code_rank = err_code_rank  # this rank's expert stage reports err_code in its error word
+        self.err_code = err_code
+        self.rank = None
 
     def record_bytes(self, H, K):
         return record_bytes(H, K)
 
     def dispatch(self, x, logits, E, K, W, rank, sot, norm, err):
+        self.rank = rank
         T, H = x.shape
         El = E // W
         rb = record_bytes(H, K)
@@ -67,6 +71,8 @@ class FakeStages:
                              torch.from_numpy(ret_row), torch.from_numpy(send_counts))
 
     def expert(self, records, R, H, I, El, K, w1, w2, err):
+        if self.err_code_rank is not None and self.rank == self.err_code_rank:
+            err[0] = self.err_code  # a device stage that gave up, made on the host
         rec = records.numpy()
         w1q, w1s = oq.quant_128x128(w1.float().numpy())
         w1d = torch.as_tensor(oq.dequant_128x128(w1q, w1s)).double()

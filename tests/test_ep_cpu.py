@@ -33,7 +33,7 @@ def _inputs():
     return x, rw, w1, w2
 
 
-def _worker(rank, port, bad_rank, q):
+def _worker(rank, port, bad_rank, q, err_rank=None, err_code=0):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -53,8 +53,26 @@ def _worker(rank, port, bad_rank, q):
         x, rw, w1, w2 = _inputs()
         El = E // W
         moe = ExpertParallelMoE(rw, w1[rank * El:(rank + 1) * El], w2[rank * El:(rank + 1) * El], E, K,
-                                stages=FakeStages(bad_count_rank=bad_rank))
+                                stages=FakeStages(bad_count_rank=bad_rank, err_code_rank=err_rank, err_code=err_code))
         xs = x[rank * T_PER_RANK:(rank + 1) * T_PER_RANK].float()
+        if err_rank is not None:
+            # forward 1 records the error; it surfaces at forward 2's count exchange on every rank,
+            # and check_errors() reports it after a single forward
+            msgs = []
+            moe.forward(xs.to(torch.bfloat16))
+            try:
+                moe.forward(xs.to(torch.bfloat16))
+                msgs.append("no error")
+            except RuntimeError as e:
+                msgs.append(str(e))
+            moe.forward(xs.to(torch.bfloat16))
+            try:
+                moe.check_errors()
+                msgs.append("no error")
+            except RuntimeError as e:
+                msgs.append(str(e))
+            q.put((rank, "errors", msgs, None))
+            return
         try:
             out, logits, freq = moe.forward(xs.to(torch.bfloat16))
             # exchange accounting behind the multi-GPU roofline: bytes this rank received from the
@@ -70,11 +88,11 @@ def _worker(rank, port, bad_rank, q):
         dist.destroy_process_group()
 
 
-def _run(bad_rank):
+def _run(bad_rank, err_rank=None, err_code=0):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, bad_rank, q)) for r in range(W)]
+    procs = [ctx.Process(target=_worker, args=(r, port, bad_rank, q, err_rank, err_code)) for r in range(W)]
     for p in procs:
         p.start()
     res = {}
@@ -106,6 +124,17 @@ def test_ep_bad_count_aborts_every_rank():
     assert "peer rank" in res[0][1]
 
 
+def test_ep_device_error_raises_on_every_rank():
+    """A device error word set by one rank's expert stage (code 202, made on the host by the
+    stand-in) is all-reduced with MAX, so both ranks raise with that code: at the next forward's
+    count exchange, or from check_errors() after the last forward."""
+    res = _run(bad_rank=None, err_rank=1, err_code=202)
+    for r in range(W):
+        status, msgs, _ = res[r]
+        assert status == "errors", res[r]
+        assert all("device error 202" in m for m in msgs), (r, msgs)
+
+
 def test_check_counts():
     from sonicmoe.ep import check_counts
 
@@ -130,16 +159,16 @@ def test_home_transport_arguments():
 
 
 def test_default_transport():
-    """One process or device-stage stand-ins: NCCL; several GPUs: the home-down transport, unless
-    the caller asks for a chunked forward (peer loads, or copy engines from 8 ranks)."""
+    """One process or device-stage stand-ins: NCCL; the home-down transport only where it was
+    measured (2 ranks, one chunk); peer loads at 3-7 ranks; copy engines from 8 ranks."""
     from sonicmoe.ep import default_transport
 
     assert default_transport(1) == "nccl"
     assert default_transport(8, native=False) == "nccl"
-    assert default_transport(2) == "home" and default_transport(8) == "home"
-    assert default_transport(4, chunks=1) == "home"
-    assert default_transport(4, chunks=2) == "p2p"
-    assert default_transport(8, chunks=6) == "copy"
+    assert default_transport(2) == "home" and default_transport(2, chunks=1) == "home"
+    assert default_transport(2, chunks=2) == "p2p"
+    assert default_transport(4) == "p2p" and default_transport(4, chunks=2) == "p2p"
+    assert default_transport(8) == "copy" and default_transport(8, chunks=6) == "copy"
 
 
 def test_check_count_matrix_same_verdict_on_every_rank():

@@ -258,3 +258,76 @@ def test_ep_multi_gpu(transport, chunks):
     o_ref, _, idx = fp8_oracle(x.float().numpy(), logits, w1.float().numpy(), w2.float().numpy(), K)
     np.testing.assert_array_equal(np.concatenate([res[r][2] for r in range(W)]), np.bincount(idx.reshape(-1), minlength=E))
     assert rel_fro(out, o_ref.numpy()) <= TOL_FP8
+
+
+def _world1_worker(port, q, T, H, I, E, K, transport, chunks):
+    import datetime
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "sonic-moe_b200"), os.path.join(root, "tests")):
+        sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    from _util import make_layer_inputs as mk
+    from sonicmoe.ep import ExpertParallelMoE
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        x, rw, w1, w2 = mk(T, H, I, E, seed=91)
+        moe = ExpertParallelMoE(rw.to(dev), w1.to(dev), w2.to(dev), E, K, transport=transport, max_tokens=T,
+                                hidden_size=H, chunks=chunks)
+        for _ in range(2):
+            out, logits, freq = moe.forward(x.to(dev))
+        moe.check_errors()
+        res = [out.float().cpu().numpy(), logits.float().cpu().numpy(), freq.cpu().numpy()]
+        if transport == "home":
+            # plant an invalid home buffer size: every row past the first 128-row block has no home
+            # row, so the up epilogue's bounds check drops it and records error 202 (the down
+            # projection then reads only inside the real buffer); the forward must report it
+            full = moe._home_rows
+            moe._home_rows = 128
+            moe.forward(x.to(dev))
+            try:
+                moe.check_errors()
+                res.append("no error")
+            except RuntimeError as e:
+                res.append(str(e))
+            moe._home_rows = full
+            moe.forward(x.to(dev))
+            moe.check_errors()  # the next forward is clean again
+        q.put(("ok", res))
+        moe.close()
+    except Exception as e:  # report instead of hanging the parent
+        q.put(("exception", repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("transport,chunks", [("home", 1), ("p2p", 1), ("p2p", 2), ("copy", 2), ("nccl", 1)])
+def test_ep_world1_transports(transport, chunks):
+    """Every transport's host orchestration on a one-rank NCCL group (runs on a one-GPU box):
+    output within 1e-2 of the fake-quantised oracle, exact expert counts; for the home transport,
+    an up-projection row without a home row makes check_errors() raise with code 202."""
+    import torch.multiprocessing as mp
+
+    T, H, I, E, K = 384, 512, 256, 16, 4
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_world1_worker, args=(_free_port(), q, T, H, I, E, K, transport, chunks))
+    p.start()
+    status, res = q.get(timeout=300)
+    p.join(timeout=120)
+    assert status == "ok", res
+    assert p.exitcode == 0
+    out, logits, freq = res[:3]
+    x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=91)
+    o_ref, _, idx = fp8_oracle(x.float().numpy(), logits, w1.float().numpy(), w2.float().numpy(), K)
+    np.testing.assert_array_equal(freq, np.bincount(idx.reshape(-1), minlength=E))
+    assert rel_fro(out, o_ref.numpy()) <= TOL_FP8
+    if transport == "home":
+        assert "device error 202" in res[3], res[3]
