@@ -15,9 +15,19 @@ Weight-format contract (reference ``functional/__init__.py:560-566``): ``w1`` is
 quantised to e4m3 with 128x128 UE8M0 block scales on first use and cached per weight version;
 already prepared :class:`~sonicmoe.ops.Fp8ExpertWeights` may be passed instead.
 
+Op boundary: as in the reference, the router top-k (``sonicmoe::_topk_fwd``,
+``sonicmoe::_softmax_topk_fwd``, in ``forward.py``) and the routing metadata
+(``triton_kernels::TC_topk_router_metadata``, ``triton_kernels::general_routing_router_metadata``)
+are ``torch.library.custom_op``s writing into caller-allocated outputs; the engine's layer forward
+after the router GEMM is one more registered op per entry point (``sonicmoe::fp8_moe_tc_forward``,
+``sonicmoe::fp8_moe_general_forward``, with fake implementations for tracing), so ``torch.compile``
+traces a whole ``MoE`` forward without a graph break.
+
 Differences from the reference, all explicit errors: biases and activations other than SwiGLU
 raise ``NotImplementedError`` (the FP8 engine implements the bias-free SwiGLU layer); the forward
-is inference-only (no autograd graph is recorded).
+is inference-only: with ``is_inference_mode_enabled=False`` while autograd is recording and an
+input or weight requires grad, the layer raises ``NotImplementedError`` instead of returning an
+output whose expert weights would never receive a gradient.
 """
 import weakref
 
@@ -27,6 +37,7 @@ import torch.nn.functional as F
 from .. import ops
 from ..enums import ActivationType
 from ..ops import Fp8ExpertWeights
+from .forward import _topk_fwd, _topk_softmax_fwd  # noqa: F401  (registers the router ops)
 
 __all__ = [
     "moe_TC_softmax_topk_layer",
@@ -104,6 +115,61 @@ def _check_common(b1, b2, activation_type):
     return activation_type
 
 
+def _reject_training(is_inference_mode_enabled, *tensors):
+    if is_inference_mode_enabled or not torch.is_grad_enabled():
+        return
+    if any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors):
+        raise NotImplementedError(
+            "the FP8 B200 engine implements the inference forward only: call it with "
+            "is_inference_mode_enabled=True (MoE: eval() or is_inference_mode=True) or under torch.no_grad(); "
+            "no backward is provided, so training would leave the expert weights without gradients"
+        )
+
+
+@torch.library.custom_op("sonicmoe::fp8_moe_tc_forward", mutates_args=())
+def _fp8_moe_tc_forward(
+    x: torch.Tensor,
+    router_logits: torch.Tensor,
+    w1: torch.Tensor,
+    w2: torch.Tensor,
+    K: int,
+    is_softmax_over_topk: bool,
+    norm_topk_probs: bool,
+    concat_layout: bool,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Engine part of ``moe_TC_softmax_topk_layer`` after the router GEMM: (o [T, H] bf16,
+    expert_frequency [E] int32).  w1 / w2 are the reference's (2I, H, E) / (H, I, E) views."""
+    w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+    w2q = prepare_fp8_weights(w2, concat_glu=False)
+    return ops.moe_forward(x, router_logits, w1q, w2q, K, is_softmax_over_topk, norm_topk_probs)
+
+
+@_fp8_moe_tc_forward.register_fake
+def _(x, router_logits, w1, w2, K, is_softmax_over_topk, norm_topk_probs, concat_layout):
+    return x.new_empty(x.shape, dtype=torch.bfloat16), x.new_empty(router_logits.shape[1], dtype=torch.int32)
+
+
+@torch.library.custom_op("sonicmoe::fp8_moe_general_forward", mutates_args=())
+def _fp8_moe_general_forward(
+    x: torch.Tensor,
+    router_scores: torch.Tensor,
+    token_indices: torch.Tensor,
+    expert_indices: torch.Tensor,
+    w1: torch.Tensor,
+    w2: torch.Tensor,
+    concat_layout: bool,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Engine part of ``moe_general_routing_inputs``: (o [T, H] bf16, expert_frequency [E] int32)."""
+    w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+    w2q = prepare_fp8_weights(w2, concat_glu=False)
+    return ops.moe_general_forward(x, router_scores, token_indices, expert_indices, w1q, w2q)
+
+
+@_fp8_moe_general_forward.register_fake
+def _(x, router_scores, token_indices, expert_indices, w1, w2, concat_layout):
+    return x.new_empty(x.shape, dtype=torch.bfloat16), x.new_empty(w2.shape[-1], dtype=torch.int32)
+
+
 def moe_TC_softmax_topk_layer(
     x: torch.Tensor,
     router_w: torch.Tensor,
@@ -126,18 +192,24 @@ def moe_TC_softmax_topk_layer(
     _check_common(b1, b2, activation_type)
     if norm_topk_probs and is_softmax_over_topk:
         raise ValueError("`norm_topk_prob` only works with softmax-then-topk")
-    E = router_w.size(0)
+    _reject_training(is_inference_mode_enabled, x, router_w, w1, w2)
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
     x = x.contiguous()
     router_logits = F.linear(x, router_w.to(x.dtype))
-    w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
-    w2q = prepare_fp8_weights(w2, concat_glu=False)
-    if w1q.concat_glu != bool(concat_layout):
-        raise ValueError("prepared w1 layout does not match concat_layout")
-    o, expert_frequency = ops.moe_forward(
-        x, router_logits.contiguous(), w1q, w2q, K, is_softmax_over_topk, norm_topk_probs
-    )
+    if isinstance(w1, Fp8ExpertWeights) or isinstance(w2, Fp8ExpertWeights):
+        # already prepared e4m3 weights (a host-side object, not a tensor): eager call
+        w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+        w2q = prepare_fp8_weights(w2, concat_glu=False)
+        if w1q.concat_glu != bool(concat_layout):
+            raise ValueError("prepared w1 layout does not match concat_layout")
+        o, expert_frequency = ops.moe_forward(
+            x, router_logits.contiguous(), w1q, w2q, K, is_softmax_over_topk, norm_topk_probs
+        )
+    else:
+        o, expert_frequency = _fp8_moe_tc_forward(
+            x, router_logits.contiguous(), w1, w2, K, is_softmax_over_topk, norm_topk_probs, concat_layout
+        )
     return o, router_logits, expert_frequency
 
 
@@ -162,47 +234,70 @@ def moe_general_routing_inputs(
     (``functional/__init__.py:592``).
     """
     _check_common(b1, b2, activation_type)
+    _reject_training(is_inference_mode_enabled, x, router_scores, w1, w2)
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
     x = x.contiguous()
-    w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
-    w2q = prepare_fp8_weights(w2, concat_glu=False)
     if router_scores.dtype != torch.float32:
         router_scores = router_scores.float()
-    o, expert_frequency = ops.moe_general_forward(
-        x,
-        router_scores.contiguous(),
-        token_indices.to(torch.int32).contiguous(),
-        expert_indices.to(torch.int32).contiguous(),
-        w1q,
-        w2q,
-    )
-    return o, expert_frequency
+    args = (x, router_scores.contiguous(), token_indices.to(torch.int32).contiguous(),
+            expert_indices.to(torch.int32).contiguous())
+    if isinstance(w1, Fp8ExpertWeights) or isinstance(w2, Fp8ExpertWeights):
+        w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+        w2q = prepare_fp8_weights(w2, concat_glu=False)
+        return ops.moe_general_forward(*args, w1q, w2q)
+    return _fp8_moe_general_forward(*args, w1, w2, concat_layout)
 
 
+@torch.library.custom_op(
+    "triton_kernels::TC_topk_router_metadata",
+    mutates_args={"expert_frequency", "expert_frequency_offset", "x_gather_idx", "s_scatter_idx",
+                  "s_reverse_scatter_idx"},
+)
 def TC_topk_router_metadata_triton(
-    topk_router_indices, E, expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx,
-    s_reverse_scatter_idx,
+    topk_router_indices: torch.Tensor,
+    E: int,
+    expert_frequency: torch.Tensor,
+    expert_frequency_offset: torch.Tensor,
+    x_gather_idx: torch.Tensor,
+    s_scatter_idx: torch.Tensor,
+    s_reverse_scatter_idx: torch.Tensor,
 ) -> None:
-    """Reference signature (triton_kernels/__init__.py:78-86): fills the five output tensors in place."""
-    res = ops.route_metadata(topk_router_indices.to(torch.int32).contiguous(), E)
-    for dst, src in zip(
-        (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx), res
-    ):
+    """Reference op and signature (triton_kernels/__init__.py:68-86): fills the five int32 outputs in
+    place (directly when they are contiguous int32, else through a copy)."""
+    outs = (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx)
+    idx = topk_router_indices.to(torch.int32).contiguous()
+    if all(t.dtype == torch.int32 and t.is_contiguous() for t in outs):
+        ops.route_metadata(idx, E, outs=outs)
+        return
+    for dst, src in zip(outs, ops.route_metadata(idx, E)):
         dst.copy_(src)
 
 
+@torch.library.custom_op(
+    "triton_kernels::general_routing_router_metadata",
+    mutates_args={"expert_frequency", "expert_frequency_offset", "x_gather_idx", "s_scatter_idx",
+                  "s_reverse_scatter_idx", "num_activated_expert_per_token_offset"},
+)
 def general_routing_router_metadata_triton(
-    sorted_selected_T, selected_E, T, E, expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx,
-    s_reverse_scatter_idx, num_activated_expert_per_token_offset,
+    sorted_selected_T: torch.Tensor,
+    selected_E: torch.Tensor,
+    T: int,
+    E: int,
+    expert_frequency: torch.Tensor,
+    expert_frequency_offset: torch.Tensor,
+    x_gather_idx: torch.Tensor,
+    s_scatter_idx: torch.Tensor,
+    s_reverse_scatter_idx: torch.Tensor,
+    num_activated_expert_per_token_offset: torch.Tensor,
 ) -> None:
-    """Reference signature (triton_kernels/__init__.py:281-292): fills the six output tensors in place."""
-    res = ops.general_route_metadata(
-        sorted_selected_T.to(torch.int32).contiguous(), selected_E.to(torch.int32).contiguous(), T, E
-    )
-    for dst, src in zip(
-        (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx,
-         num_activated_expert_per_token_offset),
-        res,
-    ):
+    """Reference op and signature (triton_kernels/__init__.py:270-292): fills the six int32 outputs in place."""
+    outs = (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx,
+            num_activated_expert_per_token_offset)
+    tok = sorted_selected_T.to(torch.int32).contiguous()
+    ex = selected_E.to(torch.int32).contiguous()
+    if all(t.dtype == torch.int32 and t.is_contiguous() for t in outs):
+        ops.general_route_metadata(tok, ex, T, E, outs=outs)
+        return
+    for dst, src in zip(outs, ops.general_route_metadata(tok, ex, T, E)):
         dst.copy_(src)

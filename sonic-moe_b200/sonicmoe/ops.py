@@ -33,14 +33,23 @@ def _need(t: torch.Tensor, name: str, dtype=None):
 _LOGIT_DTYPES = {torch.bfloat16: nat.DTYPE_BF16, torch.float16: nat.DTYPE_F16, torch.float32: nat.DTYPE_F32}
 
 
-def router_topk(router_logits: torch.Tensor, K: int, softmax_over_topk: bool = True, norm_topk_probs: bool = False):
-    """(scores fp32 [T,K], indices int32 [T,K]) -- reference ``_topk_softmax_fwd`` (forward.py:107-141)."""
+def router_topk(router_logits: torch.Tensor, K: int, softmax_over_topk: bool = True, norm_topk_probs: bool = False,
+                scores: torch.Tensor = None, idx: torch.Tensor = None):
+    """(scores fp32 [T,K], indices int32 [T,K]) -- reference ``_topk_softmax_fwd`` (forward.py:107-141).
+
+    ``scores`` / ``idx``: optional contiguous fp32 / int32 [T, K] outputs to write into."""
     _need(router_logits, "router_logits")
     if router_logits.dtype not in _LOGIT_DTYPES:
         raise ValueError(f"unsupported logits dtype {router_logits.dtype}")
     T, E = router_logits.shape
-    scores = torch.empty(T, K, dtype=torch.float32, device=router_logits.device)
-    idx = torch.empty(T, K, dtype=torch.int32, device=router_logits.device)
+    if scores is None:
+        scores = torch.empty(T, K, dtype=torch.float32, device=router_logits.device)
+    if idx is None:
+        idx = torch.empty(T, K, dtype=torch.int32, device=router_logits.device)
+    _need(scores, "scores", torch.float32)
+    _need(idx, "idx", torch.int32)
+    if tuple(scores.shape) != (T, K) or tuple(idx.shape) != (T, K):
+        raise ValueError(f"outputs must be [{T}, {K}]")
     nat.call(
         "sm_router_topk",
         _ptr(router_logits),
@@ -61,20 +70,28 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
 
 
-def route_metadata(topk_indices: torch.Tensor, E: int, err: torch.Tensor = None):
+def _outs_or_new(outs, sizes, dev):
+    """The caller's contiguous int32 output tensors (checked), or new ones of the given sizes."""
+    if outs is None:
+        return [torch.empty(n, dtype=torch.int32, device=dev) for n in sizes]
+    for t, n in zip(outs, sizes):
+        _need(t, "metadata output", torch.int32)
+        if t.numel() != n:
+            raise ValueError(f"metadata output has {t.numel()} elements, expected {n}")
+    return list(outs)
+
+
+def route_metadata(topk_indices: torch.Tensor, E: int, err: torch.Tensor = None, outs=None):
     """Reference ``TC_topk_router_metadata_triton`` (triton_kernels/__init__.py:78-146).
 
-    Returns (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx).
+    Returns (expert_frequency, expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx),
+    written into ``outs`` (five contiguous int32 tensors) when given.
     """
     _need(topk_indices, "topk_indices", torch.int32)
     T, K = topk_indices.shape
     TK = T * K
     dev = topk_indices.device
-    freq = torch.empty(E, dtype=torch.int32, device=dev)
-    off = torch.empty(E + 1, dtype=torch.int32, device=dev)
-    xg = torch.empty(TK, dtype=torch.int32, device=dev)
-    ss = torch.empty(TK, dtype=torch.int32, device=dev)
-    sr = torch.empty(TK, dtype=torch.int32, device=dev)
+    freq, off, xg, ss, sr = _outs_or_new(outs, (E, E + 1, TK, TK, TK), dev)
     if err is None:
         err = torch.zeros(1, dtype=torch.int32, device=dev)
     ws = _workspace(nat.load().sm_route_metadata_workspace(T, TK, E), dev)
@@ -85,21 +102,18 @@ def route_metadata(topk_indices: torch.Tensor, E: int, err: torch.Tensor = None)
     return freq, off, xg, ss, sr
 
 
-def general_route_metadata(sorted_token_idx: torch.Tensor, expert_idx: torch.Tensor, T: int, E: int, err=None):
+def general_route_metadata(sorted_token_idx: torch.Tensor, expert_idx: torch.Tensor, T: int, E: int, err=None,
+                           outs=None):
     """Reference ``general_routing_router_metadata_triton`` (triton_kernels/__init__.py:281-353).
 
-    Returns (freq, offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx, token_offset[T+1]).
+    Returns (freq, offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx, token_offset[T+1]),
+    written into ``outs`` (six contiguous int32 tensors) when given.
     """
     _need(sorted_token_idx, "sorted_token_idx", torch.int32)
     _need(expert_idx, "expert_idx", torch.int32)
     TK = expert_idx.numel()
     dev = expert_idx.device
-    freq = torch.empty(E, dtype=torch.int32, device=dev)
-    off = torch.empty(E + 1, dtype=torch.int32, device=dev)
-    xg = torch.empty(TK, dtype=torch.int32, device=dev)
-    ss = torch.empty(TK, dtype=torch.int32, device=dev)
-    sr = torch.empty(TK, dtype=torch.int32, device=dev)
-    tok_off = torch.empty(T + 1, dtype=torch.int32, device=dev)
+    freq, off, xg, ss, sr, tok_off = _outs_or_new(outs, (E, E + 1, TK, TK, TK, T + 1), dev)
     if err is None:
         err = torch.zeros(1, dtype=torch.int32, device=dev)
     ws = _workspace(nat.load().sm_route_metadata_workspace(T, TK, E), dev)
@@ -234,9 +248,6 @@ def moe_down_combine(aq, asf, w2: Fp8ExpertWeights, plan: RoutePlan, scores: tor
     return out
 
 
-_WS_CACHE = {}
-
-
 def moe_forward(
     x: torch.Tensor,
     router_logits: torch.Tensor,
@@ -253,8 +264,9 @@ def moe_forward(
 ):
     """The whole FP8 layer forward after the router GEMM (one C-ABI call, 7 kernels).
 
-    The scratch workspace is cached per (device, size) and shared by every call of that shape, so
-    concurrent calls of the same shape on different streams must not overlap.
+    The scratch workspace is a fresh tensor of the caching allocator for every call, so calls on
+    different streams never share scratch (inside a captured CUDA graph it comes from the graph's
+    own memory pool).
     """
     _need(x, "x", torch.bfloat16)
     _need(router_logits, "router_logits", torch.bfloat16)
@@ -269,13 +281,7 @@ def moe_forward(
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     if expert_frequency is None:
         expert_frequency = torch.empty(E, dtype=torch.int32, device=dev)
-    nbytes = nat.load().sm_moe_workspace_bytes(T, H, I, E, K)
-    key = (dev.index, nbytes)
-    ws = _WS_CACHE.get(key)
-    if ws is None:
-        # kept for the life of the process: a captured CUDA graph may still point at it
-        ws = _workspace(nbytes, dev)
-        _WS_CACHE[key] = ws
+    ws = _workspace(nat.load().sm_moe_workspace_bytes(T, H, I, E, K), dev)
     nat.call(
         "sm_moe_forward", _ptr(x), _ptr(router_logits), T, H, I, E, K, int(softmax_over_topk), int(norm_topk_probs),
         int(w1.concat_glu), _ptr(w1.q), _ptr(w1.sf), _ptr(w2.q), _ptr(w2.sf), _ptr(out), _ptr(expert_frequency),

@@ -159,8 +159,12 @@ def test_moe_module_forward(sm):
     x = torch.randn(2, T // 2, H, dtype=torch.bfloat16, device="cuda")
     o, aux = m(x, is_inference_mode=True)
     assert o.shape == x.shape and aux is None
+    with pytest.raises(NotImplementedError, match="inference forward only"):
+        m(x)  # training mode, autograd recording, weights require grad: no silent graph-less output
+    m.eval()
     o2, aux2 = m(x)
     assert aux2 is not None and torch.isfinite(aux2)
+    assert torch.equal(o, o2)
     x2 = x.view(-1, H)
     with torch.no_grad():
         lg = torch.nn.functional.linear(x2, m.router.weight).float().cpu().numpy()  # same cuBLAS call as inside
@@ -170,6 +174,24 @@ def test_moe_module_forward(sm):
     assert rel_fro(o.view(-1, H).float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
     with pytest.raises(NotImplementedError):
         m(x, kernel_backend_moe=sonicmoe.KernelBackendMoE.torch)
+
+
+def test_moe_module_torch_compile_fullgraph(sm):
+    """torch.compile of a whole MoE forward with fullgraph=True: the engine's registered ops
+    (router logits stay a traced F.linear) leave no graph break, and the compiled output equals
+    the eager one."""
+    sonicmoe, _ = sm
+    torch.manual_seed(1)
+    T, H, I, E, K = 256, 512, 256, 8, 2
+    m = sonicmoe.MoE(E, K, H, I, sonicmoe.ActivationType.SWIGLU, False, 0.02).to(torch.bfloat16).cuda().eval()
+    x = torch.randn(T, H, dtype=torch.bfloat16, device="cuda")
+    with torch.no_grad():
+        o_eager, aux_eager = m(x)
+        cm = torch.compile(m, fullgraph=True)
+        o_c, aux_c = cm(x)
+    torch.cuda.synchronize()
+    assert torch.equal(o_eager, o_c)
+    assert torch.allclose(aux_eager, aux_c)
 
 
 def _general_inputs(T, E, avg_k, seed):
