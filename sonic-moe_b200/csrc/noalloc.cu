@@ -10,7 +10,11 @@
 //
 // The first call on each device looks up the array's device address (cudaGetSymbolAddress) with
 // that device current; make that first call before any stream capture.  Later calls only launch
-// kernels.  The array's size is fixed at kNoAllocScratchBytes (1 MiB).  Each call writes every scratch
+// kernels.  The address is remembered together with the unique id of the CUDA context it was taken
+// in (cuCtxGetId): after cudaDeviceReset, or any destruction and re-creation of the device's
+// primary context, the module is loaded again and the array may sit elsewhere, so a call in a
+// context with a different id looks the address up again instead of using a stale one (such a
+// call, like a first call, belongs before any stream capture).  The array's size is fixed at kNoAllocScratchBytes (1 MiB).  Each call writes every scratch
 // entry it later reads, so nothing has to start at zero, but all calls share the one array:
 // calls whose kernels overlap on the GPU (different streams, or host threads without stream
 // ordering between them) race and must be serialised by the caller.
@@ -29,25 +33,61 @@ static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocScratchBytes 
 
 namespace {
 
-std::mutex g_noalloc_mu;
-int32_t* g_noalloc_ptr[kMaxDevices] = {};
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
 
-// Device address of the static scratch on the current device.  In host code the array's name is
-// only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per device,
-// with that device current.
+std::mutex g_noalloc_mu;
+struct ScratchEntry {
+  int32_t* ptr = nullptr;
+  unsigned long long ctx_id = 0;  // 0: unknown (then the address is looked up on every call)
+};
+ScratchEntry g_noalloc[kMaxDevices];
+
+// Unique id of the calling thread's current context (ids are never reused within a process), or
+// false when there is no current context or the driver does not provide the query.
+bool current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool resolved = false;
+  if (!resolved) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    resolved = true;
+  }
+  if (!get_current || !get_id) return false;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS && *id != 0;
+}
+
+// Device address of the static scratch in the current device's current context.  In host code
+// the array's name is only a host-side stand-in, so the address comes from cudaGetSymbolAddress,
+// taken with the device current and kept per device for as long as the context stays the same.
 cudaError_t scratch_for_current_device(int32_t** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    g_noalloc_ptr[dev] = static_cast<int32_t*>(p);
+  ScratchEntry& en = g_noalloc[dev];
+  unsigned long long id = 0;
+  if (en.ptr && en.ctx_id != 0 && current_context_id(&id) && id == en.ctx_id) {
+    *out = en.ptr;
+    return cudaSuccess;
   }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // also creates the context if there is none yet
+  if (e != cudaSuccess) return e;
+  en.ptr = static_cast<int32_t*>(p);
+  en.ctx_id = current_context_id(&id) ? id : 0;
+  *out = en.ptr;
   return cudaSuccess;
 }
 

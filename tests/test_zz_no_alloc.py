@@ -5,8 +5,9 @@ step into a CUDA graph, where cudaMalloc is not allowed during capture, or a run
 all device memory up front).  Its scratch is a 1 MiB static device array shared by every call.
 
 The test calls it through the C ABI twice in a row and checks that both calls give exactly the
-outputs of the existing workspace-based entry point, sm_route_metadata (integer arrays: exact
-equality is the tolerance).  The two calls use different routings, so a stale leftover in the
+outputs of the existing workspace-based entry point, sm_route_metadata, and of the CPU oracle's
+restatement of the reference metadata (oracle.metadata.tc_metadata; integer arrays: exact equality
+is the tolerance).  The two calls use different routings, so a stale leftover in the
 shared array from the first call would show up in the second.  This file sorts last so that a run
 stopping at the first failure has already run every other test; it also passes alone.
 """
@@ -15,6 +16,8 @@ import ctypes
 import numpy as np
 import pytest
 import torch
+
+from oracle.metadata import tc_metadata
 
 pytestmark = pytest.mark.gpu
 
@@ -70,6 +73,9 @@ def test_noalloc_metadata_matches_workspace_entry_point_twice():
         assert err_a.item() == 0 and err_b.item() == 0
         for name, a, b in zip(("freq", "offset", "x_gather", "s_scatter", "s_reverse"), got, want):
             assert torch.equal(a, b), f"T={T} E={E} K={K}: {name} differs from sm_route_metadata"
+        ref = tc_metadata(idx.cpu().numpy(), E)
+        for name, a, r in zip(("freq", "offset", "x_gather", "s_scatter", "s_reverse"), got, ref):
+            np.testing.assert_array_equal(a.cpu().numpy(), r, err_msg=f"T={T} E={E} K={K}: {name} vs oracle")
 
 
 def test_noalloc_rejects_sizes_beyond_its_static_scratch():
