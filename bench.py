@@ -1,4 +1,4 @@
-"""Benchmark of the FP8 MoE-layer forward (T=32768, H=4096, I=1024, E=128, K=8).
+"""Benchmark of the FP8 MoE-layer forward (headline workload: T=32768, H=4096, I=1024, E=128, K=8).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -10,7 +10,7 @@ the timed region and larger than L2 (x 268 MB, e4m3 weights 1.6 GB), so no expli
 The timed steps replay a CUDA graph of the forward, as the reference benchmark does
 (benchmarks/moe-cute.py:308-331).
 
-Synthetic data: x ~ N(0,1) bf16, router/expert weights ~ N(0, 0.02) bf16,
+Synthetic data (the headline workload's shapes and distributions): x ~ N(0,1) bf16, router/expert weights ~ N(0, 0.02) bf16,
 expert weights quantised to e4m3 with 128x128 UE8M0 scales before timing (weight preparation is
 not part of the forward).  FLOPs per forward: 6*T*K*H*I (benchmarks/moe-cute.py:281-284).
 
@@ -283,8 +283,8 @@ def run_ours(args, rank, world, local_rank):
     assert err.item() == 0, f"kernel error word {err.item()}"
     ms_step = ms_total / args.steps
 
-    # per-kernel live timing of the two GEMMs (same stream, CUDA events around each launch)
-    stage = time_gemm_stages(x, rw, w1p, w2p, K, reps=max(3, min(args.steps, 10)))
+    # per-stage device times from events captured inside a graph of the staged pipeline
+    stage = time_stages(x, rw, w1p, w2p, K, reps=10)
 
     # end to end through the public API: pinned host input -> device, forward, result -> host
     e2e = time_e2e(x, rw, w1, w2, K, dev, steps=max(3, min(args.steps, 10)))
@@ -328,7 +328,13 @@ def run_profile(args, local_rank):
     assert err.item() == 0, f"kernel error word {err.item()}"
 
 
-def time_gemm_stages(x, rw, w1p, w2p, K, reps):
+def time_stages(x, rw, w1p, w2p, K, reps):
+    """Per-stage device times of the forward: `reps` copies of the staged pipeline (router logits
+    + top-k, routing plan, quantise + pack, output memset, up GEMM, down GEMM + combine) captured
+    back to back in one CUDA graph, with timing events between the stages.  One replay runs the
+    copies as consecutive forwards (the regime of the timed loop); the tensor maps are encoded at
+    capture, so no host work sits between the events.  Returns per-stage medians over the copies
+    (ms); they add up to the staged step."""
     import torch
     import torch.nn.functional as F
 
@@ -336,35 +342,47 @@ def time_gemm_stages(x, rw, w1p, w2p, K, reps):
 
     T, H = x.shape
     E = rw.shape[0]
-    logits = F.linear(x, rw)
-    scores, idx = ops.router_topk(logits, K)
     err = torch.zeros(1, dtype=torch.int32, device=x.device)
-    plan = ops.route_plan(idx, E, err)
-    xq, xsf = ops.quant_pack(x, idx, plan)
-    aq, asf = ops.moe_up(xq, xsf, w1p, plan, err)
-    out = torch.zeros(T, H, dtype=torch.bfloat16, device=x.device)
-    ops.moe_down_combine(aq, asf, w2p, plan, scores, T, err, out=out)
-    torch.cuda.synchronize()
-    ups, downs, packs = [], [], []
-    for _ in range(reps):
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
-        e[0].record()
-        ops.quant_pack(x, idx, plan)
-        e[1].record()
-        e[2].record()
-        ops.moe_up(xq, xsf, w1p, plan, err)
-        e[3].record()
-        out.zero_()
-        e[4].record()
+    names = ["route", "plan", "pack", "memset", "up", "down"]
+    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(names) + 1)] for _ in range(reps)]
+    last = {}
+
+    def staged(ev):
+        ev[0].record()
+        logits = F.linear(x, rw)
+        scores, idx = ops.router_topk(logits, K)
+        ev[1].record()
+        plan = ops.route_plan(idx, E, err)
+        ev[2].record()
+        xq, xsf = ops.quant_pack(x, idx, plan)
+        ev[3].record()
+        out = torch.zeros(T, H, dtype=torch.bfloat16, device=x.device)
+        ev[4].record()
+        aq, asf = ops.moe_up(xq, xsf, w1p, plan, err)
+        ev[5].record()
         ops.moe_down_combine(aq, asf, w2p, plan, scores, T, err, out=out)
-        e[5].record()
+        ev[6].record()
+        last["n_blocks"] = plan.n_blocks
+
+    stream = torch.cuda.Stream(device=x.device)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        staged(evs[0])
         torch.cuda.synchronize()
-        packs.append(e[0].elapsed_time(e[1]))
-        ups.append(e[2].elapsed_time(e[3]))
-        downs.append(e[4].elapsed_time(e[5]))
-    assert err.item() == 0
-    return {"pack_ms": statistics.median(packs), "up_ms": statistics.median(ups), "down_ms": statistics.median(downs),
-            "n_blocks": int(plan.n_blocks.item())}
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for ev in evs:  # each copy's buffers are freed before the next: the graph pool reuses them
+                staged(ev)
+        graph.replay()  # warm
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+    assert err.item() == 0, f"kernel error word {err.item()}"
+    res = {f"{n}_ms": statistics.median(ev[i].elapsed_time(ev[i + 1]) for ev in evs) for i, n in enumerate(names)}
+    res["staged_step_ms"] = statistics.median(ev[0].elapsed_time(ev[-1]) for ev in evs)
+    res["n_blocks"] = int(last["n_blocks"].item())
+    del graph
+    return res
 
 
 def time_e2e(x, rw, w1, w2, K, dev, steps):
@@ -505,7 +523,7 @@ def run_side_workload(args):
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / args.steps
     peaks, src = measured_peaks()
-    line = {"workload": desc, "T": T, "H": H, "I": I, "E": E, "K": K, "ms_step": ms, "tokens_per_s": T / (ms / 1e3),
+    line = {"workload": desc, "T": T, "H": H, "I": I, "E": E, "K": K, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
             "steps": args.steps, "clocks": clk.summary()}
     if args.workload == "c3":
         tf = flops_fwd(T, H, I, K) / (ms / 1e3) / 1e12
@@ -566,7 +584,7 @@ def main():
         cores = len(os.sched_getaffinity(0))
         tps, cores, sample, sec = cpu_reference(CPU_SAMPLE_TOKENS, reps=max(1, min(args.steps, 3)), threads=cores)
         line = {"metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": args.warmup, "ms_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
                 "config": dict(config, parallelism="cpu", sample_tokens=CPU_SAMPLE_TOKENS),
                 "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
@@ -598,7 +616,7 @@ def main():
         e2e = res["e2e"]
         line = {
             "metric": METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_step": res["ms_step"], "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
             "config": dict(config, parallelism=f"ep{world}", experts_per_rank=E // world,
                            timing="eager steps (host reads record counts), CUDA events, max over ranks"),
@@ -651,7 +669,7 @@ def main():
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_step": res["ms_step"],
+        "ms_per_step": res["ms_step"],
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -666,8 +684,10 @@ def main():
                      "achieved": up_tflops, "peak": fp8_peak, "unit": "TFLOP/s", "frac": up_tflops / fp8_peak,
                      "traffic": traffic,
                      "peak_source": f"2 x bf16_tflops of {peak_src} (tcgen05 e4m3 rate = 2 x bf16)",
-                     "down_kernel_tflops": down_tflops, "pack_ms": st["pack_ms"], "up_ms": st["up_ms"],
-                     "down_ms": st["down_ms"]},
+                     "down_kernel_tflops": down_tflops,
+                     "stages_ms": {k[:-3]: round(v, 4) for k, v in st.items() if k.endswith("_ms")},
+                     "stage_timing": "events between the stages of 10 back-to-back staged forwards captured "
+                                     "in one CUDA graph; medians over the copies"},
         "clocks": res["clocks"],
     }
     if cpu is not None:
