@@ -143,7 +143,7 @@ def build_ep_workload(dev, rank, world, T, H, I, E, K):
     return x, rw, ops.weight_prep(w1), ops.weight_prep(w2)
 
 
-def run_ep(args, rank, world, local_rank):
+def run_ep(args, rank, world, local_rank, cfg):
     import torch
     import torch.distributed as dist
 
@@ -151,7 +151,7 @@ def run_ep(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
+    T, H, I, E, K = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["K"]
     x, rw, w1p, w2p = build_ep_workload(dev, rank, world, T, H, I, E, K)
     moe = ExpertParallelMoE(rw, w1p, w2p, E, K, max_tokens=T, hidden_size=H, chunks=args.ep_chunks,
                             reserve_sms=args.ep_reserve_sms, transport=args.ep_transport)
@@ -460,6 +460,15 @@ SIDE_WORKLOADS = {
     "c3": (16384, 2048, 768, 128, 8, "config 3 (Qwen3-style): top-k over softmax + renorm, concatenated w1"),
     "c5_64": (64, 4096, 1536, 128, 8, "config 5 (decode, T=64): Zipf(1.2) routing via moe_general_routing_inputs"),
     "c5_512": (512, 4096, 1536, 128, 8, "config 5 (decode, T=512): Zipf(1.2) routing via moe_general_routing_inputs"),
+    "c4": (8192, 7168, 2048, 256, 8, "config 4 (DeepSeek-V3-style layer, one GPU's share of tokens): all 256 experts "
+                                     "on one GPU, softmax over top-k"),
+}
+
+# configurations the expert-parallel (N > 1) bench runs: tokens per GPU, all E experts sharded over the ranks
+EP_WORKLOADS = {
+    "c2": dict(CFG, desc="config 2: FP8 MoE forward T=32768 H=4096 I=1024 E=128 K=8 per GPU, SwiGLU, interleaved w1"),
+    "c4": dict(T=8192, H=7168, I=2048, E=256, K=8,
+               desc="config 4 (DeepSeek-V3-style): T=8192 per GPU, H=7168, I=2048, E=256 sharded over the ranks, K=8"),
 }
 
 
@@ -479,13 +488,18 @@ def run_side_workload(args):
     g = torch.Generator(device=dev).manual_seed(1111)
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
     rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    w1 = (torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    w2 = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w1 = torch.empty(E, 2 * I, H, dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty(E, H, I, dtype=torch.bfloat16, device=dev)
+    for e in range(E):  # expert by expert: no fp32 copy of all the weights at once
+        w1[e] = (torch.randn(2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w2[e] = (torch.randn(H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
     w1v, w2v = w1.permute(1, 2, 0), w2.permute(1, 2, 0)
-    if args.workload == "c3":
+    if args.workload in ("c3", "c4"):
+        c3 = args.workload == "c3"
+
         def forward():
             moe_TC_softmax_topk_layer(x, rw, w1v, None, w2v, None, K, None, is_inference_mode_enabled=True,
-                                      is_softmax_over_topk=False, norm_topk_probs=True, concat_layout=True)
+                                      is_softmax_over_topk=not c3, norm_topk_probs=c3, concat_layout=c3)
         active = E
     else:
         rs = np.random.RandomState(1111)
@@ -525,7 +539,7 @@ def run_side_workload(args):
     peaks, src = measured_peaks()
     line = {"workload": desc, "T": T, "H": H, "I": I, "E": E, "K": K, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
             "steps": args.steps, "clocks": clk.summary()}
-    if args.workload == "c3":
+    if args.workload in ("c3", "c4"):
         tf = flops_fwd(T, H, I, K) / (ms / 1e3) / 1e12
         line["roofline"] = {"bound": "tensor", "achieved": tf, "peak": 2 * peaks["bf16_tflops"], "unit": "TFLOP/s",
                             "frac": tf / (2 * peaks["bf16_tflops"]), "peak_source": src}
@@ -557,25 +571,27 @@ def main():
                     help="N>1: SMs the GEMMs leave to the overlapped dispatch/combine (default: the layer's)")
     ap.add_argument("--workload", choices=["c2"] + sorted(SIDE_WORKLOADS), default="c2",
                     help="c2 = the headline configuration (default, the contract line); the others time the "
-                         "benchmark's remaining configurations on one GPU")
+                         "benchmark's remaining configurations (c4 also expert parallel with --gpus N > 1)")
     ap.add_argument("--profile", action="store_true",
                     help="only run warmup + steps eager forwards (no graph, baselines or extra timing), "
                          "for ncu captures; prints nothing")
     args = ap.parse_args()
     CFG["T"] = args.tokens
+    EP_WORKLOADS["c2"]["T"] = args.tokens
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload != "c2":
-        run_side_workload(args)
-        return
-
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
-    config = {"workload": "config 2: FP8 MoE forward T=32768 H=4096 I=1024 E=128 K=8, SwiGLU, interleaved w1",
+    if args.workload != "c2" and (world == 1 or args.workload not in EP_WORKLOADS):
+        if rank == 0:
+            run_side_workload(args)
+        return
+    ep_cfg = EP_WORKLOADS[args.workload]
+    T, H, I, E, K = ep_cfg["T"], ep_cfg["H"], ep_cfg["I"], ep_cfg["E"], ep_cfg["K"]
+    config = {"workload": ep_cfg["desc"],
               "T_per_gpu": T, "H": H, "I": I, "E": E, "K": K, "routing": "softmax_over_topk",
-              "l2": "inputs larger than L2 (x 268 MB, e4m3 weights 1.6 GB); no flush",
+              "l2": "expert weights (e4m3) and activations larger than L2 per step; no flush",
               "timing": "CUDA graph replay of the forward, CUDA events, max over ranks"}
 
     if args.impl == "reference":
@@ -608,14 +624,16 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
-        res = run_ep(args, rank, world, local_rank)
+        res = run_ep(args, rank, world, local_rank, ep_cfg)
         dist.barrier()
         dist.destroy_process_group()
         if rank != 0:
             return
         e2e = res["e2e"]
+        metric = METRIC if args.workload == "c2" else \
+            f"FP8 MoE fwd TFLOPS/GPU & tokens/s (T{T // 1024}k/GPU,H{H},I{I},E{E},K{K}) expert parallel, B200"
         line = {
-            "metric": METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+            "metric": metric, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
             "config": dict(config, parallelism=f"ep{world}", experts_per_rank=E // world,

@@ -110,7 +110,22 @@ def test_ep_p2p_kernels_emulated_ranks(W, T, H, I, E, K):
     assert rel_fro(o_all.float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
 
 
-def _home_emulated(W, T, H, I, E, K, seed, corrupt=False):
+def _gpu_layer_inputs(T, H, I, E, seed):
+    """Same distributions as make_layer_inputs, drawn on the GPU expert by expert (config 4's bf16
+    weights are 22 GB; no host copy of all of them)."""
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w1 = torch.empty(E, 2 * I, H, dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty(E, H, I, dtype=torch.bfloat16, device=dev)
+    for e in range(E):
+        w1[e] = (torch.randn(2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w2[e] = (torch.randn(H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    return x, rw, w1, w2
+
+
+def _home_emulated(W, T, H, I, E, K, seed, corrupt=False, inputs=make_layer_inputs):
     """Home-down stages with W virtual ranks on one GPU: every owner's up GEMM stores its rows into
     the W separate home buffers (the peer-store address arithmetic), then every home runs the down
     projection over its own plan with all experts' w2."""
@@ -120,7 +135,7 @@ def _home_emulated(W, T, H, I, E, K, seed, corrupt=False):
     from sonicmoe.ep import NativeStages
     from sonicmoe.ops import weight_prep
 
-    x, rw, w1, w2 = make_layer_inputs(W * T, H, I, E, seed=seed)
+    x, rw, w1, w2 = inputs(W * T, H, I, E, seed=seed)
     dev = torch.device("cuda", 0)
     xg, rwg = x.to(dev), rw.to(dev)
     El = E // W
@@ -175,6 +190,26 @@ def test_ep_home_kernels_emulated_ranks(W, T, H, I, E, K):
                                w2.float().numpy(), K)
     np.testing.assert_array_equal(freq.cpu().numpy(), np.bincount(idx.reshape(-1), minlength=E))
     assert rel_fro(o_all.float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
+
+
+def test_ep_home_config4_shape_256_experts_8_ranks():
+    """Config 4's expert-parallel layout: E = 256 experts sharded 32 per rank over 8 emulated ranks,
+    H = 7168, I = 2048, top-8, at a reduced token count (64 tokens per rank).  Every owner's up GEMM
+    stores its rows into the 8 home buffers, every home runs the down projection over all 256
+    experts' w2.  Expert counts exact for all tokens; the full rows of 8 sampled tokens within 1e-2
+    of the per-token fake-quantised oracle."""
+    from oracle.layer import fp8_oracle_rows
+    from oracle.routing import topk_route
+
+    W, T, H, I, E, K = 8, 64, 7168, 2048, 256, 8
+    x, w1, w2, o_all, logits, freq, e = _home_emulated(W, T, H, I, E, K, seed=404, inputs=_gpu_layer_inputs)
+    assert e == 0
+    scores, idx = topk_route(logits.float().cpu().numpy(), K, True, False)
+    np.testing.assert_array_equal(freq.cpu().numpy(), np.bincount(idx.reshape(-1), minlength=E))
+    rows = np.sort(np.random.RandomState(4).choice(W * T, 8, replace=False))
+    o_ref = fp8_oracle_rows(x[torch.from_numpy(rows).cuda()].float().cpu().numpy(), scores[rows], idx[rows],
+                            lambda ex: (w1[ex].float().cpu().numpy(), w2[ex].float().cpu().numpy()))
+    assert rel_fro(o_all[torch.from_numpy(rows).cuda()].float().cpu().numpy(), o_ref.numpy()) <= TOL_FP8
 
 
 def test_ep_home_bad_return_row_is_reported():

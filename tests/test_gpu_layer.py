@@ -159,12 +159,15 @@ def test_moe_module_forward(sm):
     x = torch.randn(2, T // 2, H, dtype=torch.bfloat16, device="cuda")
     o, aux = m(x, is_inference_mode=True)
     assert o.shape == x.shape and aux is None
+    with pytest.raises(RuntimeError, match="no autograd formula"):
+        o.float().sum().backward()  # the output of an inference forward cannot be backpropagated
+    o = o.detach()
     with pytest.raises(NotImplementedError, match="inference forward only"):
         m(x)  # training mode, autograd recording, weights require grad: no silent graph-less output
     m.eval()
     o2, aux2 = m(x)
     assert aux2 is not None and torch.isfinite(aux2)
-    assert torch.equal(o, o2)
+    assert torch.equal(o, o2.detach())
     x2 = x.view(-1, H)
     with torch.no_grad():
         lg = torch.nn.functional.linear(x2, m.router.weight).float().cpu().numpy()  # same cuBLAS call as inside
