@@ -153,6 +153,36 @@ int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I
                    int32_t* expert_frequency, float* topk_scores, int32_t* topk_indices, void* workspace,
                    size_t workspace_bytes, int32_t* err, void* stream);
 
+/*
+ * Fused router, opt-in.  Replaces the router GEMM `F.linear(x, router_w)` of
+ * moe_TC_softmax_topk_layer (reference sonicmoe/functional/__init__.py:501) together with the
+ * top-k of sm_router_topk: one tcgen05 kernel per 128-token tile computes
+ * router_logits = x @ router_weight^T (bf16 operands, fp32 accumulation, rounded to bf16) and
+ * ranks those rows exactly as sm_router_topk ranks given logits.  The accumulation order is the
+ * tensor core's, not cuBLAS's, so a logit can differ from F.linear's in its last bf16 bit (and a
+ * near-tie then route differently); the reference has no such path.
+ *   x [T, H] bf16, router_weight [E, H] bf16 -> router_logits [T, E] bf16, scores / indices
+ *   [T, K] as for sm_router_topk.  E % 32 == 0 with 32 <= E <= 256, H % 64 == 0 (else
+ *   SM_ENOTSUP).  workspace: sm_router_fused_workspace(T, E) bytes (per-tile expert counts).
+ */
+size_t sm_router_fused_workspace(int T, int E);
+int sm_router_fused(const void* x, const void* router_weight, int T, int H, int E, int K, int softmax_over_topk,
+                    int norm_topk_probs, void* router_logits, float* scores, int32_t* indices, void* workspace,
+                    size_t workspace_bytes, int32_t* err, void* stream);
+
+/*
+ * sm_moe_forward with the fused router in place of the caller's router GEMM (same workspace
+ * size, sm_moe_workspace_bytes): router_weight [E, H] bf16 in, router_logits [T, E] bf16 out.
+ * Same limits as sm_router_fused.  Replaces moe_TC_softmax_topk_layer's forward including its
+ * F.linear (reference sonicmoe/functional/__init__.py:482-557).
+ */
+int sm_moe_forward_fused_router(const void* x, const void* router_weight, int T, int H, int I, int E, int K,
+                                int softmax_over_topk, int norm_topk_probs, int concat_layout, const uint8_t* w1q,
+                                const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, void* out,
+                                void* router_logits, int32_t* expert_frequency, float* topk_scores,
+                                int32_t* topk_indices, void* workspace, size_t workspace_bytes, int32_t* err,
+                                void* stream);
+
 /* Bytes of workspace sm_moe_general_forward needs for T tokens and TK routed (token, expert) entries. */
 size_t sm_moe_general_workspace_bytes(int T, int TK, int H, int I, int E);
 
@@ -199,6 +229,17 @@ int sm_moe_up(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1q, const u
               int concat_layout, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
               const int32_t* off_pad, const int32_t* expert_frequency, uint8_t* aq, uint8_t* asf, int32_t* err,
               void* stream);
+
+/* sm_moe_up for the training forward: also stores the pre-activation h = x W1^T that the
+ * reference keeps for its backward (sonicmoe/functional/__init__.py:253-258 allocates it, :266-268
+ * passes preact_out=h, store_preact=True).  preact [T*K, 2I] bf16, row = the entry's expert-sorted
+ * position (off[e] + rank within the expert, i.e. the row order of s_scatter_idx), columns in the
+ * caller's w1 order (interleaved gate/up, or [gate | up] with concat_layout = 1).  The values are
+ * the fp32 tensor-core sums of the e4m3 operands rounded to bf16. */
+int sm_moe_up_preact(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1q, const uint8_t* w1_sf, int H, int I,
+                     int E, int concat_layout, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+                     const int32_t* off_pad, const int32_t* expert_frequency_offset, const int32_t* expert_frequency,
+                     uint8_t* aq, uint8_t* asf, void* preact, int32_t* err, void* stream);
 
 /* Down projection with the top-k weighted combine fused (reference _DownProjection.forward and
  * _router_forward, sonicmoe/functional/__init__.py:365-420, forward.py:64-85).  Adds

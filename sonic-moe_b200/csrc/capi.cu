@@ -355,6 +355,21 @@ int sm_moe_up(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1q, const u
   return cuda_status(launch_moe_up(g, static_cast<cudaStream_t>(stream)), "moe_up");
 }
 
+int sm_moe_up_preact(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1q, const uint8_t* w1_sf, int H, int I,
+                     int E, int concat_layout, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+                     const int32_t* off_pad, const int32_t* expert_frequency_offset, const int32_t* expert_frequency,
+                     uint8_t* aq, uint8_t* asf, void* preact, int32_t* err, void* stream) {
+  if (H <= 0 || H % 128 || I <= 0 || I % 128 || E < 1 || max_blocks < 0)
+    return fail(SM_EINVAL, "bad shape H=%d I=%d E=%d", H, I, E);
+  if (!err || !preact || !expert_frequency_offset) return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(preact)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  GemmArgs g = up_args(xq, xsf, w1q, w1_sf, H, I, E, concat_layout, max_blocks, blk_expert, n_blocks, off_pad,
+                       expert_frequency, aq, asf, err);
+  g.off = expert_frequency_offset;
+  g.preact = static_cast<__nv_bfloat16*>(preact);
+  return cuda_status(launch_moe_up(g, static_cast<cudaStream_t>(stream)), "moe_up_preact");
+}
+
 int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2q, const uint8_t* w2_sf, int H, int I,
                         int E, int T, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
                         const int32_t* off_pad, const int32_t* expert_frequency_offset,
@@ -373,21 +388,38 @@ int sm_moe_down_slices(int T, int H) {
   return down_slices(T, H);
 }
 
-int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I, int E, int K,
-                   int softmax_over_topk, int norm_topk_probs, int concat_layout, const uint8_t* w1q,
-                   const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, void* out,
-                   int32_t* expert_frequency, float* topk_scores, int32_t* topk_indices, void* workspace,
-                   size_t workspace_bytes, int32_t* err, void* stream) {
+}  // extern "C"
+
+static int check_fused_router_args(int H, int E) {
+  if (E % 32 != 0 || E < 32 || E > 256)
+    return fail(SM_ENOTSUP, "the fused router needs E %% 32 == 0 and 32 <= E <= 256 (got E=%d)", E);
+  if (H <= 0 || H % 64) return fail(SM_ENOTSUP, "the fused router needs H %% 64 == 0 (got H=%d)", H);
+  return SM_OK;
+}
+
+// The layer forward; the router stage either ranks the given bf16 logits (router_weight null) or
+// computes them from x and router_weight with the fused router, writing them to router_logits.
+static int moe_forward_impl(const void* x, const void* router_logits, const void* router_weight, void* logits_out,
+                            int T, int H, int I, int E, int K, int softmax_over_topk, int norm_topk_probs,
+                            int concat_layout, const uint8_t* w1q, const uint8_t* w1_sf, const uint8_t* w2q,
+                            const uint8_t* w2_sf, void* out, int32_t* expert_frequency, float* topk_scores,
+                            int32_t* topk_indices, void* workspace, size_t workspace_bytes, int32_t* err,
+                            void* stream) {
   int rc = check_layer_args(T, H, I, E, K);
   if (rc) return rc;
   rc = check_router_args(T, E, K, softmax_over_topk, norm_topk_probs);
   if (rc) return rc;
+  if (router_weight) {
+    rc = check_fused_router_args(H, E);
+    if (rc) return rc;
+  }
   if (!expert_frequency) return fail(SM_EINVAL, "null pointer");
   if (T == 0) {  // nothing routed: zero expert counts, empty output
     return cuda_status(cudaMemsetAsync(expert_frequency, 0, sizeof(int32_t) * E, static_cast<cudaStream_t>(stream)),
                        "moe_forward");
   }
   if (!x || !router_logits || !w1q || !w1_sf || !w2q || !w2_sf || !out) return fail(SM_EINVAL, "null pointer");
+  if (router_weight && !aligned16(router_weight)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
   if (!aligned16(x) || !aligned16(out) || !aligned16(w1q) || !aligned16(w2q) || !aligned16(w1_sf) ||
       !aligned16(w2_sf) || !aligned16(workspace))
     return fail(SM_EINVAL, "pointers must be 16-byte aligned");
@@ -404,7 +436,10 @@ int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I
 
   cudaError_t e = cudaSuccess;
   if (!err) e = cudaMemsetAsync(w.err, 0, sizeof(int32_t), st);
-  if (e == cudaSuccess)
+  if (e == cudaSuccess && router_weight)
+    e = launch_router_fused(x, router_weight, T, H, E, K, softmax_over_topk, norm_topk_probs, logits_out, scores, idx,
+                            w.route.tile_counts, errw, st);
+  else if (e == cudaSuccess)
     e = launch_router_topk(router_logits, kDtypeBF16, T, E, K, softmax_over_topk, norm_topk_probs, scores, idx,
                            w.route.tile_counts, st);
   if (e == cudaSuccess)
@@ -427,6 +462,55 @@ int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I
     e = launch_moe_down(g, st);
   }
   return cuda_status(e, "moe_forward");
+}
+
+extern "C" {
+
+int sm_moe_forward(const void* x, const void* router_logits, int T, int H, int I, int E, int K,
+                   int softmax_over_topk, int norm_topk_probs, int concat_layout, const uint8_t* w1q,
+                   const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, void* out,
+                   int32_t* expert_frequency, float* topk_scores, int32_t* topk_indices, void* workspace,
+                   size_t workspace_bytes, int32_t* err, void* stream) {
+  return moe_forward_impl(x, router_logits, nullptr, nullptr, T, H, I, E, K, softmax_over_topk, norm_topk_probs,
+                          concat_layout, w1q, w1_sf, w2q, w2_sf, out, expert_frequency, topk_scores, topk_indices,
+                          workspace, workspace_bytes, err, stream);
+}
+
+int sm_moe_forward_fused_router(const void* x, const void* router_weight, int T, int H, int I, int E, int K,
+                                int softmax_over_topk, int norm_topk_probs, int concat_layout, const uint8_t* w1q,
+                                const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, void* out,
+                                void* router_logits, int32_t* expert_frequency, float* topk_scores,
+                                int32_t* topk_indices, void* workspace, size_t workspace_bytes, int32_t* err,
+                                void* stream) {
+  if (T > 0 && (!router_weight || !router_logits)) return fail(SM_EINVAL, "null pointer");
+  if (T > 0 && !aligned16(router_logits)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  return moe_forward_impl(x, router_logits, router_weight, router_logits, T, H, I, E, K, softmax_over_topk,
+                          norm_topk_probs, concat_layout, w1q, w1_sf, w2q, w2_sf, out, expert_frequency, topk_scores,
+                          topk_indices, workspace, workspace_bytes, err, stream);
+}
+
+int sm_router_fused(const void* x, const void* router_weight, int T, int H, int E, int K, int softmax_over_topk,
+                    int norm_topk_probs, void* router_logits, float* scores, int32_t* indices, void* workspace,
+                    size_t workspace_bytes, int32_t* err, void* stream) {
+  int rc = check_router_args(T, E, K, softmax_over_topk, norm_topk_probs);
+  if (rc) return rc;
+  rc = check_fused_router_args(H, E);
+  if (rc) return rc;
+  if (T == 0) return SM_OK;
+  if (!x || !router_weight || !router_logits || !scores || !indices || !err || !workspace)
+    return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(x) || !aligned16(router_weight) || !aligned16(router_logits))
+    return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  const size_t need = static_cast<size_t>(E) * route_tiles_tc(T) * sizeof(int32_t);
+  if (workspace_bytes < need) return fail(SM_EINVAL, "workspace too small (%zu < %zu)", workspace_bytes, need);
+  return cuda_status(launch_router_fused(x, router_weight, T, H, E, K, softmax_over_topk, norm_topk_probs,
+                                         router_logits, scores, indices, static_cast<int32_t*>(workspace), err,
+                                         static_cast<cudaStream_t>(stream)),
+                     "router_fused");
+}
+
+size_t sm_router_fused_workspace(int T, int E) {
+  return static_cast<size_t>(E > 0 ? E : 1) * (route_tiles_tc(T > 0 ? T : 1)) * sizeof(int32_t);
 }
 
 size_t sm_moe_general_workspace_bytes(int T, int TK, int H, int I, int E) {

@@ -233,6 +233,12 @@ __host__ __device__ constexpr uint32_t idesc_mxf8_e4m3(int M, int N, uint32_t sf
          (static_cast<uint32_t>(M >> 4) << 24) | (sfa_id << 29);
 }
 
+// two floats -> packed bf16x2 (round to nearest even), low half = a
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+
 // --------------------------------------------------------------------------------------------
 // named barrier among a subset of warps
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {

@@ -111,6 +111,7 @@ __device__ __forceinline__ RowMeta load_row_meta(const GemmArgs& g, int tile, in
   m.sc = 0.0f;
   if constexpr (kUp) {
     if (g.ret_dst != nullptr) m.tok = m.valid ? g.ret_dst[m.p] : -1;
+    if (g.preact != nullptr) m.tok = rel + g.off[m.e];  // expert-sorted entry row of the stored h
   } else {
     if (m.valid) {
       const int rs = rel + g.off[m.e];
@@ -136,6 +137,27 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const uint32_t 
   const bool valid = m.valid != 0;
   const int p = m.p, mb = m.mb, nt = m.nt;
   if constexpr (kUp) {
+    if (g.preact != nullptr && valid) {
+      // training forward: h as bf16 in the caller's w1 column order (interleaved: this thread's 64
+      // tile columns are consecutive; concatenated: 32 gate columns and the matching 32 up columns)
+      __nv_bfloat16* hrow = g.preact + static_cast<size_t>(m.tok) * g.N;
+      auto put32 = [&](__nv_bfloat16* dst, const uint32_t* src) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8)
+          *reinterpret_cast<uint4*>(dst + j) =
+              make_uint4(pack_bf16x2(__uint_as_float(src[j]), __uint_as_float(src[j + 1])),
+                         pack_bf16x2(__uint_as_float(src[j + 2]), __uint_as_float(src[j + 3])),
+                         pack_bf16x2(__uint_as_float(src[j + 4]), __uint_as_float(src[j + 5])),
+                         pack_bf16x2(__uint_as_float(src[j + 6]), __uint_as_float(src[j + 7])));
+      };
+      if (g.concat) {
+        put32(hrow + nt * 128 + 32 * cc, v);
+        put32(hrow + g.N / 2 + nt * 128 + 32 * cc, v + 32);
+      } else {
+        put32(hrow + nt * kBN + 64 * cc, v);
+        put32(hrow + nt * kBN + 64 * cc + 32, v + 32);
+      }
+    }
     float o[32];
     float am = 0.0f;
 #pragma unroll
@@ -444,6 +466,19 @@ static bool make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t 
   cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t inner,
+                    uint64_t outer, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * static_cast<uint64_t>(esize)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

@@ -101,21 +101,17 @@ struct RouterShape {
   static constexpr bool kPrefetch = PL <= 8;
 };
 
-template <typename InT, int PL, int KMAX>
-__global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
-    router_topk_kernel(const InT* __restrict__ logits, int T, int E, int K, int vec, int softmax_over_topk,
-                       int renorm, float* __restrict__ scores, int32_t* __restrict__ indices,
-                       int32_t* __restrict__ tile_counts, int n_tiles) {
-  constexpr int kWarps = RouterShape<PL>::kWarps;
-  extern __shared__ int32_t s_hist[];  // [E] when tile_counts != nullptr
+// Top-k (+ softmax) of the rows [row0, row0 + 128) of a [T, E] logits array, kWarps warps of the
+// calling CTA, warp w taking rows w, w + kWarps, ... ; the chosen experts are counted into the
+// CTA's shared histogram s_hist (when non-null).  Shared by the top-k kernel over given logits and
+// by the fused router, which runs it on the logits tile its GEMM has just written.
+template <typename InT, int PL, int KMAX, int kWarps, bool kPrefetch>
+__device__ __forceinline__ void route_tile_rows(const InT* __restrict__ logits, int row0, int T, int E, int K,
+                                                int vec, int softmax_over_topk, int renorm,
+                                                float* __restrict__ scores, int32_t* __restrict__ indices,
+                                                int32_t* s_hist) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
-  const int row0 = tile * kTileTokens;
-  if (tile_counts) {
-    for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
-    __syncthreads();
-  }
   int log_n = 0;
   while ((1 << log_n) < E) ++log_n;
   const uint32_t mask = (1u << log_n) - 1u;
@@ -135,13 +131,13 @@ __global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
     }
   };
   float vn[PL];
-  if (RouterShape<PL>::kPrefetch && warp < kTileTokens && row0 + warp < T) load_row(row0 + warp, vn);
+  if (kPrefetch && warp < kTileTokens && row0 + warp < T) load_row(row0 + warp, vn);
 
   for (int r = warp; r < kTileTokens; r += kWarps) {
     const int row = row0 + r;
     if (row >= T) break;
     float v[PL];
-    if (RouterShape<PL>::kPrefetch) {
+    if (kPrefetch) {
 #pragma unroll
       for (int i = 0; i < PL; ++i) v[i] = vn[i];
       const int rn = row + kWarps;
@@ -221,13 +217,179 @@ __global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
     if (act) {
       scores[static_cast<size_t>(row) * K + lane] = e;
       indices[static_cast<size_t>(row) * K + lane] = idx;
-      if (tile_counts) atomicAdd(&s_hist[idx], 1);
+      if (s_hist) atomicAdd(&s_hist[idx], 1);
     }
   }
+}
+
+template <typename InT, int PL, int KMAX>
+__global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
+    router_topk_kernel(const InT* __restrict__ logits, int T, int E, int K, int vec, int softmax_over_topk,
+                       int renorm, float* __restrict__ scores, int32_t* __restrict__ indices,
+                       int32_t* __restrict__ tile_counts, int n_tiles) {
+  extern __shared__ int32_t s_hist[];  // [E] when tile_counts != nullptr
+  const int tile = blockIdx.x;
+  if (tile_counts) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
+    __syncthreads();
+  }
+  route_tile_rows<InT, PL, KMAX, RouterShape<PL>::kWarps, RouterShape<PL>::kPrefetch>(
+      logits, tile * kTileTokens, T, E, K, vec, softmax_over_topk, renorm, scores, indices,
+      tile_counts ? s_hist : nullptr);
   if (tile_counts) {
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) tile_counts[static_cast<size_t>(e) * n_tiles + tile] = s_hist[e];
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Fused router: one CTA per 128-token tile computes the tile's logits x[tile] @ w^T with
+// tcgen05.mma.kind::f16 (bf16 operands by TMA with the 128-byte swizzle, 64 hidden columns per
+// stage, fp32 accumulator of E columns in tensor memory), rounds them to bf16 into the logits
+// output, and then all 16 warps run the same top-k (+ softmax) as router_topk_kernel on those
+// rows.  It replaces the separate logits GEMM (torch F.linear in the reference,
+// functional/__init__.py:501) plus the top-k launch; the tensor-core accumulation order differs
+// from cuBLAS's, so logits may differ in the last bf16 bit and the path is opt-in.
+// Roles: warp 0 TMA producer, warp 1 MMA issuer, warp 2 tensor-memory allocation, warps 4-7 read
+// the accumulator (warp w: rows 32 (w % 4) .. + 31).
+constexpr int kRfThreads = 512;
+constexpr int kRfKBlock = 64;  // bf16 values per 128-byte swizzled row: K extent of one stage
+constexpr int kRfStages = 4;
+constexpr int kRfABytes = kTileTokens * 128;  // 16 KB of x per stage
+
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+template <int PL, int KMAX>
+__global__ void __launch_bounds__(kRfThreads, 1)
+    router_fused_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                        int T, int H, int E, int K, int vec, int softmax_over_topk, int renorm, uint32_t tmem_cols,
+                        __nv_bfloat16* __restrict__ logits, float* __restrict__ scores,
+                        int32_t* __restrict__ indices, int32_t* __restrict__ tile_counts, int n_tiles, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  const int stage_bytes = kRfABytes + E * 128;  // multiple of 4 KB (E % 32 == 0)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRfStages * stage_bytes);
+  uint64_t* empty = full + kRfStages;
+  uint64_t* tmem_full = empty + kRfStages;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  int32_t* s_hist = reinterpret_cast<int32_t*>(tmem_holder + 4);  // [E]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int row0 = tile * kTileTokens;
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < kRfStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_w);
+  }
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
+  if (warp == 2) {
+    tmem_alloc(tmem_holder, tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int KB = H / kRfKBlock;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ TMA producer
+      const uint64_t pol_x = policy_evict_first();  // x streams through once
+      const uint64_t pol_w = policy_evict_last();   // the router weight is read by every tile
+      int kb = 0;
+      for (; kb < KB; ++kb) {
+        const int s = kb % kRfStages;
+        const uint32_t ph = (kb / kRfStages) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, err, kErrTimeoutProducer)) break;
+        uint8_t* st = smem + s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        tma_load_2d(st, &tmap_x, &full[s], kb * kRfKBlock, row0, pol_x);
+        tma_load_2d(st + kRfABytes, &tmap_w, &full[s], kb * kRfKBlock, 0, pol_w);
+      }
+      if (kb < KB) {
+        // an error elsewhere: let the loads already issued land before shared memory goes away
+        for (int j = (kb - kRfStages > 0 ? kb - kRfStages : 0); j < kb; ++j)
+          mbar_wait_ns(&full[j % kRfStages], (j / kRfStages) & 1, 50000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      const uint32_t idesc = idesc_bf16(kTileTokens, E);
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % kRfStages;
+        const uint32_t ph = (kb / kRfStages) & 1;
+        if (!mbar_wait(&full[s], ph, err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        uint8_t* st = smem + s * stage_bytes;
+        const uint64_t ad = sdesc_sw128(smem_u32(st));
+        const uint64_t bd = sdesc_sw128(smem_u32(st + kRfABytes));
+#pragma unroll
+        for (int kk = 0; kk < kRfKBlock / 16; ++kk)  // K = 16 per MMA: +32 bytes = +2 in the address field
+          tc_mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      // completes once every MMA issued above has finished (also after an early exit)
+      tc_commit(tmem_full);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // -------------------------------------------------------------------- logits out
+    const int q = warp & 3;
+    const int row = row0 + q * 32 + lane;
+    if (mbar_wait(tmem_full, 0, err, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+      for (int c = 0; c < E / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + 32 * c, v);
+        tmem_ld_wait();
+        if (row < T) {
+          uint4* dst = reinterpret_cast<uint4*>(logits + static_cast<size_t>(row) * E + 32 * c);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 w;
+            w.x = pack_bf16x2_rn(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1]));
+            w.y = pack_bf16x2_rn(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+            w.z = pack_bf16x2_rn(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+            w.w = pack_bf16x2_rn(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+            dst[j] = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();  // the tile's logits are written (visible to this CTA) and tensor memory is read
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tmem_cols);
+  }
+  // top-k of the tile's rows over the bf16 logits just written, by all 16 warps
+  route_tile_rows<__nv_bfloat16, PL, KMAX, kRfThreads / 32, true>(logits, row0, T, E, K, vec, softmax_over_topk,
+                                                                   renorm, scores, indices, s_hist);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) tile_counts[static_cast<size_t>(e) * n_tiles + tile] = s_hist[e];
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -446,6 +608,50 @@ cudaError_t launch_router_topk(const void* logits, int dtype, int T, int E, int 
     default:
       return launch_router_dtype<float>(logits, T, E, K, sot, renorm, scores, idx, tile_counts, st);
   }
+}
+
+template <int PL, int KMAX>
+static cudaError_t launch_router_fused_t(const void* x, const void* w, int T, int H, int E, int K, int vec, int sot,
+                                         int renorm, void* logits, float* scores, int32_t* idx,
+                                         int32_t* tile_counts, int* err, cudaStream_t st) {
+  const int n_tiles = (T + kTileTokens - 1) / kTileTokens;
+  CUtensorMap tx, tw;
+  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, static_cast<uint64_t>(H), static_cast<uint64_t>(T),
+                      kRfKBlock, kTileTokens, true) ||
+      !encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, static_cast<uint64_t>(H), static_cast<uint64_t>(E),
+                      kRfKBlock, static_cast<uint32_t>(E), true))
+    return cudaErrorInvalidValue;
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(E)) cols <<= 1;
+  const int smem = kRfStages * (kRfABytes + E * 128) + (2 * kRfStages + 1) * 8 + 16 + E * 4 + 1024;
+  auto kern = router_fused_kernel<PL, KMAX>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<n_tiles, kRfThreads, smem, st>>>(tx, tw, T, H, E, K, vec, sot, renorm, cols,
+                                          static_cast<__nv_bfloat16*>(logits), scores, idx, tile_counts, n_tiles, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_router_fused(const void* x, const void* w, int T, int H, int E, int K, int sot, int renorm,
+                                void* logits, float* scores, int32_t* idx, int32_t* tile_counts, int* err,
+                                cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (E % 32 != 0 || E < 32 || E > 256 || H % kRfKBlock != 0 || K < 1 || K > 32) return cudaErrorInvalidValue;
+  int vec = 1;
+  for (int v : {8, 4, 2})
+    if (E % (32 * v) == 0) {
+      vec = v;
+      break;
+    }
+  const int per_lane = ((E + 32 * vec - 1) / (32 * vec)) * vec;
+  if (K <= 16) {
+    if (per_lane <= 4)
+      return launch_router_fused_t<4, 16>(x, w, T, H, E, K, vec, sot, renorm, logits, scores, idx, tile_counts, err, st);
+    return launch_router_fused_t<8, 16>(x, w, T, H, E, K, vec, sot, renorm, logits, scores, idx, tile_counts, err, st);
+  }
+  if (per_lane <= 4)
+    return launch_router_fused_t<4, 32>(x, w, T, H, E, K, vec, sot, renorm, logits, scores, idx, tile_counts, err, st);
+  return launch_router_fused_t<8, 32>(x, w, T, H, E, K, vec, sot, renorm, logits, scores, idx, tile_counts, err, st);
 }
 
 static cudaError_t route_hist_impl(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,

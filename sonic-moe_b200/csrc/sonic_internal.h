@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -36,6 +37,15 @@ inline int max_padded_blocks(long long TK, int E) {
 
 cudaError_t launch_router_topk(const void* logits, int dtype, int T, int E, int K, int sot, int renorm,
                                float* scores, int32_t* idx, int32_t* tile_counts, cudaStream_t st);
+// Fused router (E % 32 == 0, 32 <= E <= 256, H % 64 == 0): logits = x @ w^T (bf16 [T, E], fp32
+// accumulation on tcgen05) and the top-k of each row, plus the per-tile expert histogram.
+cudaError_t launch_router_fused(const void* x, const void* w, int T, int H, int E, int K, int sot, int renorm,
+                                void* logits, float* scores, int32_t* idx, int32_t* tile_counts, int* err,
+                                cudaStream_t st);
+// 2-D row-major tensor map: `outer` rows of `inner` elements of `esize` bytes, box box_inner x
+// box_outer, 128-byte swizzle when swizzle128 (the host encoder of csrc/gemm.cu).
+bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t inner,
+                    uint64_t outer, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 cudaError_t launch_route_hist(const int32_t* experts, int TK, int entries_per_tile, int E, int n_tiles,
                               int32_t* tile_counts, int* err, cudaStream_t st);
 // Same, but negative expert ids are holes (no entry) instead of errors.
@@ -88,6 +98,10 @@ struct GemmArgs {
   uint8_t* home_sf[kMaxEpRanks];
   long long home_rows;
   int n_homes;
+  // up projection, training forward: the pre-activation h = x W1^T (bf16, [TK, N] in expert-sorted
+  // entry order: row off[e] + (p - off_pad[e]) for padded row p, columns in the caller's w1 order);
+  // null: not stored
+  __nv_bfloat16* preact;
   int* err;
   int num_sms;
   int tokens;    // T (rows of the token-major output), for the down projection's slice choice

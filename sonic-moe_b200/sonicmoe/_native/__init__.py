@@ -35,6 +35,12 @@ SIGNATURES = {
     "sm_last_error": (ctypes.c_char_p, []),
     "sm_version": (ctypes.c_char_p, []),
     "sm_router_topk": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "sm_router_fused_workspace": (_SZ, [_I, _I]),
+    "sm_router_fused": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P, _P]),
+    "sm_moe_forward_fused_router": (
+        _I,
+        [_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P],
+    ),
     "sm_route_metadata_workspace": (_SZ, [_I, _I, _I]),
     "sm_route_metadata": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "sm_general_route_metadata": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
@@ -89,6 +95,7 @@ SIGNATURES = {
     "sm_route_plan": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "sm_quant_pack": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "sm_moe_up_preact": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_moe_down_combine": (
         _I,
         [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],

@@ -149,6 +149,31 @@ def _(x, router_logits, w1, w2, K, is_softmax_over_topk, norm_topk_probs, concat
     return x.new_empty(x.shape, dtype=torch.bfloat16), x.new_empty(router_logits.shape[1], dtype=torch.int32)
 
 
+@torch.library.custom_op("sonicmoe::fp8_moe_tc_forward_fused_router", mutates_args=())
+def _fp8_moe_tc_forward_fused_router(
+    x: torch.Tensor,
+    router_w: torch.Tensor,
+    w1: torch.Tensor,
+    w2: torch.Tensor,
+    K: int,
+    is_softmax_over_topk: bool,
+    norm_topk_probs: bool,
+    concat_layout: bool,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``moe_TC_softmax_topk_layer`` with the fused router (router GEMM + top-k in one kernel):
+    (o [T, H] bf16, router_logits [T, E] bf16, expert_frequency [E] int32)."""
+    w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+    w2q = prepare_fp8_weights(w2, concat_glu=False)
+    return ops.moe_forward_fused_router(x, router_w, w1q, w2q, K, is_softmax_over_topk, norm_topk_probs)
+
+
+@_fp8_moe_tc_forward_fused_router.register_fake
+def _(x, router_w, w1, w2, K, is_softmax_over_topk, norm_topk_probs, concat_layout):
+    E = router_w.shape[0]
+    return (x.new_empty(x.shape, dtype=torch.bfloat16), x.new_empty((x.shape[0], E), dtype=torch.bfloat16),
+            x.new_empty(E, dtype=torch.int32))
+
+
 @torch.library.custom_op("sonicmoe::fp8_moe_general_forward", mutates_args=())
 def _fp8_moe_general_forward(
     x: torch.Tensor,
@@ -184,10 +209,17 @@ def moe_TC_softmax_topk_layer(
     is_softmax_over_topk: bool = True,
     norm_topk_probs: bool = False,
     concat_layout: bool = False,
+    *,
+    fused_router: bool = False,
 ):
     """Token-choice top-k MoE layer forward.  Returns (o [T, H], router_logits [T, E], expert_frequency [E]).
 
     ``stream_id`` is ignored, as in the reference (the current torch stream is used).
+
+    ``fused_router`` (keyword only; not in the reference): compute the router logits and their top-k
+    in one tcgen05 kernel instead of ``F.linear`` + the top-k kernel.  Its logits come from the
+    tensor core's fp32 accumulation, so they can differ from ``F.linear``'s in the last bf16 bit (and
+    a near-tie can then route to another expert); needs E % 32 == 0, 32 <= E <= 256, H % 64 == 0.
     """
     _check_common(b1, b2, activation_type)
     if norm_topk_probs and is_softmax_over_topk:
@@ -196,6 +228,19 @@ def moe_TC_softmax_topk_layer(
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
     x = x.contiguous()
+    if fused_router:
+        rw = router_w.to(x.dtype).contiguous()
+        if isinstance(w1, Fp8ExpertWeights) or isinstance(w2, Fp8ExpertWeights):
+            w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+            w2q = prepare_fp8_weights(w2, concat_glu=False)
+            if w1q.concat_glu != bool(concat_layout):
+                raise ValueError("prepared w1 layout does not match concat_layout")
+            o, router_logits, expert_frequency = ops.moe_forward_fused_router(
+                x, rw, w1q, w2q, K, is_softmax_over_topk, norm_topk_probs)
+        else:
+            o, router_logits, expert_frequency = _fp8_moe_tc_forward_fused_router(
+                x, rw, w1, w2, K, is_softmax_over_topk, norm_topk_probs, concat_layout)
+        return o, router_logits, expert_frequency
     router_logits = F.linear(x, router_w.to(x.dtype))
     if isinstance(w1, Fp8ExpertWeights) or isinstance(w2, Fp8ExpertWeights):
         # already prepared e4m3 weights (a host-side object, not a tensor): eager call

@@ -66,6 +66,31 @@ def router_topk(router_logits: torch.Tensor, K: int, softmax_over_topk: bool = T
     return scores, idx
 
 
+def router_fused(x: torch.Tensor, router_w: torch.Tensor, K: int, softmax_over_topk: bool = True,
+                 norm_topk_probs: bool = False, err: torch.Tensor = None):
+    """Fused router (opt-in): (router_logits bf16 [T, E], scores fp32 [T, K], indices int32 [T, K]) from
+    x [T, H] and router_w [E, H] in one tcgen05 kernel -- the reference's ``F.linear`` +
+    ``_topk_softmax_fwd`` (functional/__init__.py:501, forward.py:107-141).  The logits come from the
+    tensor core's fp32 accumulation, not cuBLAS's, so they can differ from ``F.linear`` in the last
+    bf16 bit; the ranking of the logits it returns is exactly ``router_topk``'s."""
+    _need(x, "x", torch.bfloat16)
+    _need(router_w, "router_w", torch.bfloat16)
+    T, H = x.shape
+    E = router_w.shape[0]
+    if router_w.shape[1] != H:
+        raise ValueError(f"router_w {tuple(router_w.shape)} does not match x {tuple(x.shape)}")
+    dev = x.device
+    logits = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
+    scores = torch.empty(T, K, dtype=torch.float32, device=dev)
+    idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+    if err is None:
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _workspace(nat.load().sm_router_fused_workspace(T, E), dev)
+    nat.call("sm_router_fused", _ptr(x), _ptr(router_w), T, H, E, K, int(softmax_over_topk), int(norm_topk_probs),
+             _ptr(logits), _ptr(scores), _ptr(idx), _ptr(ws), ws.numel(), _ptr(err), _stream())
+    return logits, scores, idx
+
+
 def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
 
@@ -223,11 +248,23 @@ def quant_pack(x: torch.Tensor, topk_indices: torch.Tensor, plan: RoutePlan):
     return xq, xsf
 
 
-def moe_up(xq, xsf, w1: Fp8ExpertWeights, plan: RoutePlan, err):
+def moe_up(xq, xsf, w1: Fp8ExpertWeights, plan: RoutePlan, err, preact_out: torch.Tensor = None):
+    """Up projection + SwiGLU + requantisation.  With ``preact_out`` (bf16 [T*K, 2I]) the training
+    forward's pre-activation h is stored too, in the reference's expert-sorted row order."""
     E, N2, H = w1.shape
     I = N2 // 2
     aq = torch.empty(plan.max_blocks * _BLOCK_M, I, dtype=torch.uint8, device=xq.device)
     asf = torch.zeros(plan.max_blocks, -(-I // 512), 512, dtype=torch.uint8, device=xq.device)
+    if preact_out is not None:
+        _need(preact_out, "preact_out", torch.bfloat16)
+        if preact_out.dim() != 2 or preact_out.shape[1] != N2 or preact_out.shape[0] != plan.s_scatter.numel():
+            raise ValueError(f"preact_out must be [T*K, {N2}] bf16")
+        nat.call(
+            "sm_moe_up_preact", _ptr(xq), _ptr(xsf), _ptr(w1.q), _ptr(w1.sf), H, I, E, int(w1.concat_glu),
+            plan.max_blocks, _ptr(plan.blk_expert), _ptr(plan.n_blocks), _ptr(plan.off_pad), _ptr(plan.off),
+            _ptr(plan.freq), _ptr(aq), _ptr(asf), _ptr(preact_out), _ptr(err), _stream(),
+        )
+        return aq, asf
     nat.call(
         "sm_moe_up", _ptr(xq), _ptr(xsf), _ptr(w1.q), _ptr(w1.sf), H, I, E, int(w1.concat_glu), plan.max_blocks,
         _ptr(plan.blk_expert), _ptr(plan.n_blocks), _ptr(plan.off_pad), _ptr(plan.freq), _ptr(aq), _ptr(asf),
@@ -288,6 +325,39 @@ def moe_forward(
         _ptr(topk_scores), _ptr(topk_indices), _ptr(ws), ws.numel(), _ptr(err), _stream(),
     )
     return out, expert_frequency
+
+
+def moe_forward_fused_router(
+    x: torch.Tensor,
+    router_w: torch.Tensor,
+    w1: Fp8ExpertWeights,
+    w2: Fp8ExpertWeights,
+    K: int,
+    softmax_over_topk: bool = True,
+    norm_topk_probs: bool = False,
+    err: torch.Tensor = None,
+):
+    """``moe_forward`` with the fused router in place of the caller's router GEMM (one C-ABI call):
+    returns (out [T, H] bf16, router_logits [T, E] bf16, expert_frequency [E] int32)."""
+    _need(x, "x", torch.bfloat16)
+    _need(router_w, "router_w", torch.bfloat16)
+    T, H = x.shape
+    E, N2, H1 = w1.shape
+    E2, H2, I = w2.shape
+    if H1 != H or H2 != H or N2 != 2 * I or E2 != E or tuple(router_w.shape) != (E, H):
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)}, router_w {tuple(router_w.shape)}, "
+                         f"w1 {w1.shape}, w2 {w2.shape}")
+    dev = x.device
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    logits = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
+    expert_frequency = torch.empty(E, dtype=torch.int32, device=dev)
+    ws = _workspace(nat.load().sm_moe_workspace_bytes(T, H, I, E, K), dev)
+    nat.call(
+        "sm_moe_forward_fused_router", _ptr(x), _ptr(router_w), T, H, I, E, K, int(softmax_over_topk),
+        int(norm_topk_probs), int(w1.concat_glu), _ptr(w1.q), _ptr(w1.sf), _ptr(w2.q), _ptr(w2.sf), _ptr(out),
+        _ptr(logits), _ptr(expert_frequency), None, None, _ptr(ws), ws.numel(), _ptr(err), _stream(),
+    )
+    return out, logits, expert_frequency
 
 
 def moe_general_forward(

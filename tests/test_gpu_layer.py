@@ -77,6 +77,41 @@ def test_moe_up_stage(sm, T, H, I, E, K, concat):
     assert (sf_gpu == sf_ref).mean() > 0.99
 
 
+@pytest.mark.parametrize("concat", [False, True])
+@pytest.mark.parametrize("T,H,I,E,K", [(256, 512, 256, 8, 2), (300, 768, 384, 16, 4)])
+def test_moe_up_stores_preact(sm, T, H, I, E, K, concat):
+    """Training forward (reference functional/__init__.py:253-268, store_preact): the up GEMM also
+    writes h = x W1^T as bf16 [T*K, 2I] in expert-sorted entry order and the caller's w1 column
+    order; within bf16 rounding (rel. Frobenius 1e-2) of the fake-quantised oracle's h, and the
+    intermediate `a` is bit for bit the one of the inference up GEMM."""
+    _, ops = sm
+    x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=3 * T + I)
+    logits = (x.float() @ rw.float().T).to(torch.bfloat16)
+    _, idx = oroute.topk_route(logits.float().numpy(), K)
+    w1p, _ = _prep(ops, w1, w2, concat)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    idx_t = torch.from_numpy(idx).cuda()
+    plan = ops.route_plan(idx_t, E, err)
+    xq, xsf = ops.quant_pack(x.cuda(), idx_t, plan)
+    h = torch.full((T * K, 2 * I), float("nan"), dtype=torch.bfloat16, device="cuda")
+    aq_h, asf_h = ops.moe_up(xq, xsf, w1p, plan, err, preact_out=h)
+    aq, asf = ops.moe_up(xq, xsf, w1p, plan, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0, f"kernel error word {err.item()}"
+    freq, off, _, s_scatter, s_rev = ometa.tc_metadata(idx, E)
+    off_pad, _, _ = ometa.padded_layout(freq)
+    rows = ometa.padded_rows(idx, s_rev, off, off_pad)
+    assert np.array_equal(aq_h.cpu().numpy()[rows], aq.cpu().numpy()[rows])
+    xd = oq.dequant_1x128(*oq.quant_1x128(x.float().numpy())).astype(np.float64)
+    w1d = oq.dequant_128x128(*oq.quant_128x128(w1.float().numpy())).astype(np.float64)
+    f = np.asarray(s_scatter).astype(np.int64)  # sorted position -> flat entry t*K + k
+    e = idx.reshape(-1)[f]
+    h_ref = np.einsum("rh,rnh->rn", xd[f // K], w1d[e])
+    h_gpu = h.float().cpu().numpy()
+    assert np.isfinite(h_gpu).all()  # every entry row written
+    assert rel_fro(h_gpu, h_ref) < 1e-2
+
+
 @pytest.mark.parametrize("T,H,I,E,K", [(256, 512, 256, 8, 2), (300, 768, 128, 16, 4)])
 def test_moe_down_stage(sm, T, H, I, E, K):
     _, ops = sm
