@@ -243,13 +243,64 @@ int sm_moe_up_preact(const uint8_t* xq, const uint8_t* xsf, const uint8_t* w1q, 
 
 /* Down projection with the top-k weighted combine fused (reference _DownProjection.forward and
  * _router_forward, sonicmoe/functional/__init__.py:365-420, forward.py:64-85).  Adds
- * score * y into out [T, H] bf16, which the caller zero-fills first.  Tiles are visited one
- * output-column slice at a time so that the slice being reduced into stays resident in L2. */
+ * score * y into out [T, H] bf16, which the caller zero-fills first (topk_scores = NULL: unit
+ * weights, the backward's dX).  Tiles are visited one output-column slice at a time so that the
+ * slice being reduced into stays resident in L2. */
 int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2q, const uint8_t* w2_sf, int H,
                         int I, int E, int T, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
                         const int32_t* off_pad, const int32_t* expert_frequency_offset,
                         const int32_t* expert_frequency, const int32_t* s_scatter_idx, const int32_t* x_gather_idx,
                         const float* topk_scores, void* out, int32_t* err, void* stream);
+
+/*
+ * Backward of the layer (reference sonicmoe/functional/backward.py and the autograd functions
+ * _UpProjection.backward / _DownProjection.backward, functional/__init__.py:303-362, 422-479), in
+ * FP8 with the forward's 1x128 / 128x128 UE8M0 scaling.  For dO [T, H] the stages are:
+ *   1. sm_quant_pack of dO (exactly as x in the forward) -> dO rows in the padded layout;
+ *   2. sm_moe_dact: dA' = dO W2 per entry (B = W2^T from sm_weight_prep_t of c_proj.weight), then
+ *      from the stored pre-activation h (sm_moe_up_preact): dS [T*K] (accumulated: zero it first),
+ *      a' = s * a and dH = SwiGLU backward of s * dA' -- dH as e4m3 + atoms for stage 3 and as bf16,
+ *      a' as bf16, both in padded rows (gemm_dact of functional/backward.py:211-278);
+ *   3. sm_moe_down_combine with topk_scores = NULL (unit weights) and B = W1^T (sm_weight_prep_t of
+ *      c_fc.weight, interleaved layout): dX [T, H] = sum over the token's entries of dH W1
+ *      (the reference's gemm + token_broadcast_backward, :173-206 and :281-305);
+ *   4. sm_tq_pack of dO (gathered) / x (gathered) / a' / dH (padded) -> transposed e4m3 operands
+ *      with one scale per 128 rows, then sm_moe_wgrad: dW2[e] = dO_e^T a'_e [H, I] and
+ *      dW1[e] = dH_e^T x_e [2I, H] (the reference's varlen-K gemms, :339-348, :465-473);
+ *   5. sm_router_bwd: dlogits [T, E] fp32 from dS (backward.py:308-430).
+ * Interleaved w1 layout only (concat_layout raises SM_ENOTSUP at the Python layer).
+ */
+/* W^T for a backward GEMM: w [E, N, K] bf16 -> wq_t [E, K, N] e4m3 with the 128x128 block scales of
+ * w, atoms [E][K/128][ceil(N/512)][512] (sm_weight_sf_bytes(E, K, N) bytes). */
+int sm_weight_prep_t(const void* w, int E, int N, int K, uint8_t* wq_t, uint8_t* sf_atoms, void* stream);
+/* Stage 2 above.  doq/dosf: dO packed like sm_quant_pack's xq/xsf; w2t: [E, I, H]; preact [T*K, 2I]
+ * bf16 (expert-sorted rows); dh_q [max_blocks*128, 2I] + dh_sf atoms, dh_bf16 [max_blocks*128, 2I],
+ * a_prime [max_blocks*128, I] (padded rows); dscores [T*K] fp32, flat entries, accumulated.
+ * I % 256 == 0. */
+int sm_moe_dact(const uint8_t* doq, const uint8_t* dosf, const uint8_t* w2t_q, const uint8_t* w2t_sf, int H, int I,
+                int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks, const int32_t* off_pad,
+                const int32_t* expert_frequency_offset, const int32_t* expert_frequency, const int32_t* s_scatter_idx,
+                const float* topk_scores, const void* preact, uint8_t* dh_q, uint8_t* dh_sf, void* dh_bf16,
+                void* a_prime, float* dscores, int32_t* err, void* stream);
+/* Transposed, column-quantised operand of a weight-gradient GEMM: out [C, max_blocks*128] e4m3,
+ * out[c][p] = q(src[row(p)][c]) with one UE8M0 scale per (c, 128-row block), atoms
+ * [C/128][ceil(max_blocks/4)][512]; row(p) = the token of padded row p (src_padded = 0: src is
+ * [T, C] token rows, gathered by x_gather_idx) or p itself (src_padded = 1: src [max_blocks*128, C]);
+ * padding rows are zero.  C % 128 == 0. */
+int sm_tq_pack(const void* src, int C, int src_padded, int max_blocks, const int32_t* blk_expert,
+               const int32_t* n_blocks, const int32_t* off_pad, const int32_t* expert_frequency_offset,
+               const int32_t* expert_frequency, const int32_t* x_gather_idx, uint8_t* out_q, uint8_t* out_sf,
+               void* stream);
+/* Weight gradient: out_w[e] [M, N] bf16 = A[:, rows_e] B[:, rows_e]^T over expert e's padded rows
+ * (off_pad), A [M, max_blocks*128] and B [N, max_blocks*128] from sm_tq_pack.  Experts without rows
+ * get zeros.  M % 128 == 0, N % 256 == 0. */
+int sm_moe_wgrad(const uint8_t* a_q, const uint8_t* a_sf, const uint8_t* b_q, const uint8_t* b_sf, int M, int N,
+                 int E, int max_blocks, const int32_t* off_pad, void* out_w, int32_t* err, void* stream);
+/* Router backward: dlogits [T, E] fp32 from dscores [T, K] (fp32), the forward's bf16 logits,
+ * scores and indices; same modes as sm_router_topk. */
+int sm_router_bwd(const void* router_logits, const float* topk_scores, const int32_t* topk_indices,
+                  const float* dscores, int T, int E, int K, int softmax_over_topk, int norm_topk_probs,
+                  float* dlogits, void* stream);
 
 /* Number of output-column slices (1, 2 or 4) sm_moe_down_combine visits for T output rows of
  * width H: the largest split whose bf16 slab T x (H / slices) exceeds no 80 MB share of L2.

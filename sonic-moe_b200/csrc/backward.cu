@@ -1,0 +1,223 @@
+// Backward of the FP8 MoE layer: the non-GEMM kernels.  The GEMMs are moe_gemm_kernel's
+// activation-gradient and weight-gradient kinds (csrc/gemm.cu) and its down kind with unit weights.
+//
+// weight_prep_t_kernel -- 128x128 block quantisation written transposed: w [E, N, K] -> wt [E, K, N]
+//                         e4m3 with the block's scale (the same block, read the other way), so that
+//                         a backward GEMM takes W^T as its K-major B operand.
+// tq_pack_kernel       -- the weight gradients' operands: rows of the padded expert layout (gathered
+//                         token rows, or rows of a padded array) transposed to [C, rows] and
+//                         quantised with one UE8M0 scale per 128 consecutive rows (the K groups of a
+//                         weight-gradient GEMM whose K is the expert's rows); padding rows are zero.
+// router_bwd_kernel    -- gradient of the router logits from the scores' gradient
+//                         (functional/backward.py:308-430: softmax over the top-k, or top-k of the
+//                         softmax with optional renormalisation).
+#include "common.cuh"
+#include "sonic_internal.h"
+
+namespace smb {
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+
+// One CTA of 256 threads per 128x128 block: blockIdx = (k block, n block, expert).
+__global__ void __launch_bounds__(256)
+    weight_prep_t_kernel(const __nv_bfloat16* __restrict__ w, int N, int Kd, uint8_t* __restrict__ wq,
+                         uint8_t* __restrict__ wsf) {
+  __shared__ uint16_t tile[kBlockM][kBlockK + 2];
+  __shared__ float s_red[8];
+  const int kb = blockIdx.x, nb = blockIdx.y, e = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int row = tid >> 1, half = tid & 1;
+  const uint16_t* src = reinterpret_cast<const uint16_t*>(w) +
+                        (static_cast<size_t>(e) * N + static_cast<size_t>(nb) * kBlockM + row) * Kd + kb * kBlockK +
+                        half * 64;
+  float am = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 raw = reinterpret_cast<const uint4*>(src)[i];
+    const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      tile[row][half * 64 + 8 * i + 2 * j] = static_cast<uint16_t>(wd[j] & 0xFFFFu);
+      tile[row][half * 64 + 8 * i + 2 * j + 1] = static_cast<uint16_t>(wd[j] >> 16);
+      am = fmaxf(am, fmaxf(fabsf(__uint_as_float(wd[j] << 16)), fabsf(__uint_as_float(wd[j] & 0xFFFF0000u))));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+  if ((tid & 31) == 0) s_red[tid >> 5] = am;
+  __syncthreads();
+  am = s_red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) am = fmaxf(am, s_red[i]);
+  const int e8 = scale_exp_of_amax(am);
+  const float inv = exp2_neg(e8);
+  // transposed: output row k (of this block) = column k of the input block, 64 n values per thread
+  const int k = tid >> 1;
+  uint8_t* dst = wq + (static_cast<size_t>(e) * Kd + static_cast<size_t>(kb) * kBlockK + k) * N +
+                 static_cast<size_t>(nb) * kBlockM + half * 64;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t wd[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = half * 64 + 16 * i + 4 * j;
+      wd[j] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(bf16_bits_to_f32(tile[n][k]), inv),
+                                               __fmul_rn(bf16_bits_to_f32(tile[n + 1][k]), inv))) |
+              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(bf16_bits_to_f32(tile[n + 2][k]), inv),
+                                                __fmul_rn(bf16_bits_to_f32(tile[n + 3][k]), inv)))
+               << 16);
+    }
+    reinterpret_cast<uint4*>(dst)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+  if (tid < 128) {
+    // atoms of the transposed weight: [E][Kd/128 row blocks][ceil(N/512)][512], K block nb
+    const int KGn = (N / kBlockK + 3) / 4;
+    const size_t atom = ((static_cast<size_t>(e) * (Kd / kBlockM) + kb) * KGn + nb / 4) * kSfAtomBytes;
+    wsf[atom + 16 * (tid >> 2) + 4 * (tid & 3) + (nb % 4)] = static_cast<uint8_t>(e8 + 127);
+  }
+}
+
+// One CTA of 256 threads per (block mb of the padded layout, 128-column block cb of the source).
+// Padded row p of block mb (expert e = blk_expert[mb], rel = p - off_pad[e]) is valid when
+// rel < freq[e]; its source row is x_gather[off[e] + rel] (token rows, gathered) or p itself
+// (src_padded).  out [C, rows_pad] e4m3: out[c][p] = q(src[row(p)][c]); atoms [C/128][KG][512] with
+// KG = ceil(rows_pad / 512), one scale per (c, 128-row block).
+__global__ void __launch_bounds__(256)
+    tq_pack_kernel(const __nv_bfloat16* __restrict__ src, int C, int src_padded, const int32_t* __restrict__ blk_expert,
+                   const int32_t* __restrict__ off_pad, const int32_t* __restrict__ off,
+                   const int32_t* __restrict__ freq, const int32_t* __restrict__ x_gather,
+                   const int32_t* __restrict__ n_blocks, long long rows_pad, uint8_t* __restrict__ outq,
+                   uint8_t* __restrict__ outsf) {
+  __shared__ uint16_t tile[kBlockM][kBlockK + 2];
+  const int mb = blockIdx.x, cb = blockIdx.y;
+  if (mb >= *n_blocks) return;  // blocks past the layout are never read
+  const int tid = threadIdx.x;
+  const int row = tid >> 1, half = tid & 1;
+  const int e = blk_expert[mb];
+  const int p = mb * kBlockM + row;
+  const int rel = p - off_pad[e];
+  const bool valid = rel < freq[e];
+  const long long srow = src_padded ? static_cast<long long>(p) : (valid ? x_gather[off[e] + rel] : 0);
+  const uint4* s4 =
+      reinterpret_cast<const uint4*>(src + srow * static_cast<long long>(C) + static_cast<long long>(cb) * kBlockK + half * 64);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 raw = valid ? s4[i] : make_uint4(0, 0, 0, 0);
+    const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      tile[row][half * 64 + 8 * i + 2 * j] = static_cast<uint16_t>(wd[j] & 0xFFFFu);
+      tile[row][half * 64 + 8 * i + 2 * j + 1] = static_cast<uint16_t>(wd[j] >> 16);
+    }
+  }
+  __syncthreads();
+  // output row c = source column cb*128 + c; this thread quantises its 64 of the block's 128 rows
+  const int c = tid >> 1;
+  float am = 0.0f;
+#pragma unroll 8
+  for (int r = 0; r < 64; ++r) am = fmaxf(am, fabsf(bf16_bits_to_f32(tile[half * 64 + r][c])));
+  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+  const int e8 = scale_exp_of_amax(am);
+  const float inv = exp2_neg(e8);
+  uint8_t* dst = outq + (static_cast<long long>(cb) * kBlockK + c) * rows_pad + static_cast<long long>(mb) * kBlockM +
+                 half * 64;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t wd[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = half * 64 + 16 * i + 4 * j;
+      wd[j] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(bf16_bits_to_f32(tile[r][c]), inv),
+                                               __fmul_rn(bf16_bits_to_f32(tile[r + 1][c]), inv))) |
+              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(bf16_bits_to_f32(tile[r + 2][c]), inv),
+                                                __fmul_rn(bf16_bits_to_f32(tile[r + 3][c]), inv)))
+               << 16);
+    }
+    reinterpret_cast<uint4*>(dst)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+  if (half == 0) {
+    const long long KG = (rows_pad / kBlockK + 3) / 4;
+    const long long atom = (static_cast<long long>(cb) * KG + mb / 4) * kSfAtomBytes;
+    outsf[atom + 16 * (c % 32) + 4 * (c / 32) + (mb % 4)] = static_cast<uint8_t>(e8 + 127);
+  }
+}
+
+// One warp per token row.  sot: dl[idx_k] = s_k (g_k - sum_j g_j s_j), zero elsewhere.  tos: p =
+// softmax(logits) over all E; dp_sel = g (or (g - sum_j g_j s_j) / sum_j p_sel_j when renormalised);
+// dl = p (dp - sum_k dp_sel_k p_sel_k) with dp zero outside the selection.
+__global__ void router_bwd_kernel(const __nv_bfloat16* __restrict__ logits, const float* __restrict__ scores,
+                                  const int32_t* __restrict__ idx, const float* __restrict__ ds, int T, int E, int K,
+                                  int softmax_over_topk, int renorm, float* __restrict__ dlogits) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const size_t row = static_cast<size_t>(warp);
+  float* out = dlogits + row * E;
+  const float g = lane < K ? ds[row * K + lane] : 0.0f;
+  const float s = lane < K ? scores[row * K + lane] : 0.0f;
+  const int ix = lane < K ? idx[row * K + lane] : 0;
+  if (softmax_over_topk) {
+    float dot = g * s;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    for (int e = lane; e < E; e += 32) out[e] = 0.0f;
+    __syncwarp();
+    if (lane < K) out[ix] = s * (g - dot);
+    return;
+  }
+  const __nv_bfloat16* lrow = logits + row * E;
+  float mx = -__int_as_float(0x7f800000);
+  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, __bfloat162float(lrow[e]));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.0f;
+  for (int e = lane; e < E; e += 32) sum += __expf(__bfloat162float(lrow[e]) - mx);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float p_sel = lane < K ? __expf(__bfloat162float(lrow[ix]) - mx) / sum : 0.0f;
+  float dp_sel = g;
+  if (renorm) {
+    float dot_s = g * s, S = p_sel;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      dot_s += __shfl_xor_sync(0xffffffffu, dot_s, o);
+      S += __shfl_xor_sync(0xffffffffu, S, o);
+    }
+    dp_sel = lane < K ? (g - dot_s) / S : 0.0f;
+  }
+  float dot = dp_sel * p_sel;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  for (int e = lane; e < E; e += 32) out[e] = -(__expf(__bfloat162float(lrow[e]) - mx) / sum) * dot;
+  __syncwarp();
+  if (lane < K) out[ix] = p_sel * (dp_sel - dot);
+}
+
+cudaError_t launch_weight_prep_t(const void* w, int E, int N, int Kd, uint8_t* wq, uint8_t* wsf, cudaStream_t st) {
+  if (E == 0) return cudaSuccess;
+  dim3 grid(Kd / kBlockK, N / kBlockM, E);
+  weight_prep_t_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), N, Kd, wq, wsf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tq_pack(const void* src, int C, int src_padded, const int32_t* blk_expert, const int32_t* off_pad,
+                           const int32_t* off, const int32_t* freq, const int32_t* x_gather, const int32_t* n_blocks,
+                           int max_blocks, uint8_t* outq, uint8_t* outsf, cudaStream_t st) {
+  if (max_blocks == 0) return cudaSuccess;
+  dim3 grid(max_blocks, C / kBlockK);
+  tq_pack_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), C, src_padded, blk_expert, off_pad, off,
+                                       freq, x_gather, n_blocks, static_cast<long long>(max_blocks) * kBlockM, outq,
+                                       outsf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_router_bwd(const void* logits, const float* scores, const int32_t* idx, const float* ds, int T,
+                              int E, int K, int sot, int renorm, float* dlogits, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  const int warps = 8;
+  router_bwd_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), scores,
+                                                                     idx, ds, T, E, K, sot, renorm, dlogits);
+  return cudaGetLastError();
+}
+
+}  // namespace smb

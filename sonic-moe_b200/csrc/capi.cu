@@ -383,6 +383,95 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
   return cuda_status(launch_moe_down(g, static_cast<cudaStream_t>(stream)), "moe_down_combine");
 }
 
+// ---------------------------------------------------------------------------------------------
+// backward
+int sm_weight_prep_t(const void* w, int E, int N, int K, uint8_t* wq_t, uint8_t* sf_atoms, void* stream) {
+  if (E < 1 || N <= 0 || K <= 0 || N % 128 || K % 128)
+    return fail(SM_EINVAL, "need E >= 1 and N, K multiples of 128 (E=%d N=%d K=%d)", E, N, K);
+  if (!w || !wq_t || !sf_atoms) return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(w) || !aligned16(wq_t)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  return cuda_status(launch_weight_prep_t(w, E, N, K, wq_t, sf_atoms, static_cast<cudaStream_t>(stream)),
+                     "weight_prep_t");
+}
+
+int sm_moe_dact(const uint8_t* doq, const uint8_t* dosf, const uint8_t* w2t_q, const uint8_t* w2t_sf, int H, int I,
+                int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks, const int32_t* off_pad,
+                const int32_t* expert_frequency_offset, const int32_t* expert_frequency, const int32_t* s_scatter_idx,
+                const float* topk_scores, const void* preact, uint8_t* dh_q, uint8_t* dh_sf, void* dh_bf16,
+                void* a_prime, float* dscores, int32_t* err, void* stream) {
+  if (H <= 0 || H % 128 || I <= 0 || I % 256 || E < 1 || max_blocks < 0)
+    return fail(SM_ENOTSUP, "bad shape H=%d I=%d E=%d (H %% 128 == 0, I %% 256 == 0)", H, I, E);
+  if (!err || !preact || !dh_q || !dh_sf || !dh_bf16 || !a_prime || !dscores || !topk_scores || !s_scatter_idx ||
+      !expert_frequency_offset)
+    return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(preact) || !aligned16(dh_q) || !aligned16(dh_bf16) || !aligned16(a_prime))
+    return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  GemmArgs g = up_args(doq, dosf, w2t_q, w2t_sf, H, I / 2, E, 0, max_blocks, blk_expert, n_blocks, off_pad,
+                       expert_frequency, dh_q, dh_sf, err);
+  g.N = I;  // output columns of this GEMM: the intermediate
+  g.off = expert_frequency_offset;
+  g.s_scatter = s_scatter_idx;
+  g.scores = topk_scores;
+  g.h_in = static_cast<const __nv_bfloat16*>(preact);
+  g.dh_bf16 = static_cast<__nv_bfloat16*>(dh_bf16);
+  g.a_prime = static_cast<__nv_bfloat16*>(a_prime);
+  g.ds = dscores;
+  return cuda_status(launch_moe_dact(g, static_cast<cudaStream_t>(stream)), "moe_dact");
+}
+
+int sm_tq_pack(const void* src, int C, int src_padded, int max_blocks, const int32_t* blk_expert,
+               const int32_t* n_blocks, const int32_t* off_pad, const int32_t* expert_frequency_offset,
+               const int32_t* expert_frequency, const int32_t* x_gather_idx, uint8_t* out_q, uint8_t* out_sf,
+               void* stream) {
+  if (C <= 0 || C % 128 || max_blocks < 0) return fail(SM_EINVAL, "need C %% 128 == 0 (C=%d)", C);
+  if (!src || !blk_expert || !n_blocks || !off_pad || !expert_frequency || !out_q || !out_sf ||
+      (!src_padded && (!x_gather_idx || !expert_frequency_offset)))
+    return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(src) || !aligned16(out_q)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  return cuda_status(launch_tq_pack(src, C, src_padded, blk_expert, off_pad, expert_frequency_offset, expert_frequency,
+                                    x_gather_idx, n_blocks, max_blocks, out_q, out_sf,
+                                    static_cast<cudaStream_t>(stream)),
+                     "tq_pack");
+}
+
+int sm_moe_wgrad(const uint8_t* a_q, const uint8_t* a_sf, const uint8_t* b_q, const uint8_t* b_sf, int M, int N,
+                 int E, int max_blocks, const int32_t* off_pad, void* out_w, int32_t* err, void* stream) {
+  if (M <= 0 || M % 128 || N <= 0 || N % 256 || E < 1 || max_blocks < 0)
+    return fail(SM_ENOTSUP, "bad shape M=%d N=%d E=%d (M %% 128 == 0, N %% 256 == 0)", M, N, E);
+  if (!a_q || !a_sf || !b_q || !b_sf || !off_pad || !out_w || !err) return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(out_w) || !aligned16(a_q) || !aligned16(b_q)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // experts without rows get no tile: their gradient is the zeros written here
+  cudaError_t e = cudaMemsetAsync(out_w, 0, static_cast<size_t>(E) * M * N * 2, st);
+  if (e != cudaSuccess || max_blocks == 0) return cuda_status(e, "moe_wgrad");
+  GemmArgs g{};
+  g.a = a_q;
+  g.a_sf = a_sf;
+  g.a_rows = M;
+  g.b = b_q;
+  g.b_sf = b_sf;
+  g.E = E;
+  g.N = N;
+  g.Kd = max_blocks * kBlockM;
+  g.off_pad = off_pad;
+  g.out_w = static_cast<__nv_bfloat16*>(out_w);
+  g.err = err;
+  g.num_sms = num_sms();
+  return cuda_status(launch_moe_wgrad(g, st), "moe_wgrad");
+}
+
+int sm_router_bwd(const void* router_logits, const float* topk_scores, const int32_t* topk_indices,
+                  const float* dscores, int T, int E, int K, int softmax_over_topk, int norm_topk_probs,
+                  float* dlogits, void* stream) {
+  int rc = check_router_args(T, E, K, softmax_over_topk, norm_topk_probs);
+  if (rc) return rc;
+  if (T > 0 && (!router_logits || !topk_scores || !topk_indices || !dscores || !dlogits))
+    return fail(SM_EINVAL, "null pointer");
+  return cuda_status(launch_router_bwd(router_logits, topk_scores, topk_indices, dscores, T, E, K, softmax_over_topk,
+                                       norm_topk_probs, dlogits, static_cast<cudaStream_t>(stream)),
+                     "router_bwd");
+}
+
 int sm_moe_down_slices(int T, int H) {
   if (T < 0 || H <= 0 || H % 256) return fail(SM_EINVAL, "need T >= 0 and H %% 256 == 0 (T=%d H=%d)", T, H);
   return down_slices(T, H);

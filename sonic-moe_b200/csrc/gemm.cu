@@ -47,19 +47,32 @@ constexpr int kRowChunkBytes = 128;  // down epilogue: one thread's 64 bf16 of o
 // groups, so its 16-byte stores are 4-way (the minimum for 512 bytes) instead of 32-way conflicted.
 constexpr int kSlotStride = 144;
 
+// Epilogue kinds of the one persistent kernel:
+//   kKindDown  down projection + top-k combine (bulk bf16 reductions into the token rows)
+//   kKindUp    up projection + SwiGLU + requantisation
+//   kKindDact  backward of the down projection and the activation: dA' = dO W2 per entry, then
+//              dS (row dot with a), dH (SwiGLU backward from the stored h, e4m3 + bf16) and
+//              a' = score * a (bf16)
+//   kKindWgrad weight gradient: tiles (expert, m, n) of D[e] = A[:, rows_e] B[:, rows_e]^T with K
+//              = the expert's padded rows, stored as bf16
+constexpr int kKindDown = 0, kKindUp = 1, kKindDact = 2, kKindWgrad = 3;
+
 // Shared-memory layout per epilogue kind.  The up projection keeps a 4-stage ring plus a 16 KB
 // output tile; the down projection gives one stage up for 72 KB of per-thread staging from which
-// its output rows are reduced into global memory by TMA bulk reductions.
-template <bool kUp>
+// its output rows are reduced into global memory by TMA bulk reductions; the backward kinds store
+// straight from registers.
+template <int kKind>
 struct GemmSmem {
-  static constexpr int kStages = kUp ? 4 : 3;
+  static constexpr bool kUp = kKind == kKindUp;
+  static constexpr int kStages = kKind == kKindDown ? 3 : 4;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kABytes;
   static constexpr int kOffSfa = kOffB + kStages * kBBytes;
   static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
   static constexpr int kOffStage = kOffSfb + kStages * kSfbBytes;
   // up: one 128 x 128-byte e4m3 output tile (128B-swizzled, TMA-stored); down: per-thread slots
-  static constexpr int kStageBytes = kUp ? kBlockM * 128 : kEpiWarps * 32 * kSlotStride;
+  static constexpr int kStageBytes =
+      kUp ? kBlockM * 128 : (kKind == kKindDown ? kEpiWarps * 32 * kSlotStride : 0);
   static constexpr int kOffBar = kOffStage + kStageBytes;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAmax = (kOffTmemHolder + 4 + 15) / 16 * 16;
@@ -99,8 +112,9 @@ struct RowMeta {
   float sc;   // down: its router score
 };
 
-template <bool kUp>
+template <int kKind>
 __device__ __forceinline__ RowMeta load_row_meta(const GemmArgs& g, int tile, int n_blocks, int ntn, int r) {
+  constexpr bool kUp = kKind == kKindUp;
   RowMeta m;
   tile_coords(tile, n_blocks, ntn, g.n_slices, m.mb, m.nt);
   m.e = g.blk_expert[m.mb];
@@ -112,14 +126,98 @@ __device__ __forceinline__ RowMeta load_row_meta(const GemmArgs& g, int tile, in
   if constexpr (kUp) {
     if (g.ret_dst != nullptr) m.tok = m.valid ? g.ret_dst[m.p] : -1;
     if (g.preact != nullptr) m.tok = rel + g.off[m.e];  // expert-sorted entry row of the stored h
+  } else if constexpr (kKind == kKindDact) {
+    if (m.valid) {
+      m.tok = rel + g.off[m.e];              // expert-sorted row of h
+      m.sc = g.scores[g.s_scatter[m.tok]];  // router score of the entry
+    }
   } else {
     if (m.valid) {
       const int rs = rel + g.off[m.e];
       m.tok = g.x_gather[rs];
-      m.sc = g.scores[g.s_scatter[rs]];
+      m.sc = g.scores ? g.scores[g.s_scatter[rs]] : 1.0f;
     }
   }
   return m;
+}
+
+// Activation-gradient epilogue (backward of functional/backward.py:211-278, `gemm_dact` with
+// colvec_scale = s and colvec_reduce): this thread holds dA'[entry, i] = (dO[token] W2[e])[i] for the
+// 64 intermediate columns i = 256 nt + 64 cc + j of its row.  With (g, u) the stored pre-activation
+// (interleaved columns 2i, 2i+1), sig = 1 / (1 + e^-g), a = g sig u:
+//   dS[entry] += sum_j dA'_j a_j            (fp32 atomics: four column warps x I/256 tiles)
+//   a'_j = s a_j                            (bf16, padded row; the dW2 operand)
+//   dg_j = s dA'_j u sig (1 + g (1 - sig)),  du_j = s dA'_j g sig
+// dH is written as bf16 (padded row; the dW1 operand) and as e4m3 with one UE8M0 scale for its
+// 128 values -- exactly one 1x128 group of the dX GEMM's K -- plus the scale byte in the atom.
+__device__ __forceinline__ void dact_grad(float dap, float gt, float up, float sc, float& a, float& dg, float& du) {
+  const float sig = __fdividef(1.0f, 1.0f + __expf(-gt));
+  const float silu = gt * sig;
+  a = silu * up;
+  const float da = sc * dap;
+  dg = da * up * sig * (1.0f + gt * (1.0f - sig));
+  du = da * silu;
+}
+
+__device__ __forceinline__ void dact_tile(const GemmArgs& g, const uint32_t (&v)[64], const RowMeta& m, int cc) {
+  if (!m.valid) return;
+  const int I = g.N;
+  const int i0 = m.nt * kBN + 64 * cc;
+  const uint4* hrow = reinterpret_cast<const uint4*>(g.h_in + static_cast<size_t>(m.tok) * (2 * I) + 2 * i0);
+  const float sc = m.sc;
+  const size_t p = static_cast<size_t>(m.p);
+  uint4* adst = reinterpret_cast<uint4*>(g.a_prime + p * I + i0);
+  uint4* hdst = reinterpret_cast<uint4*>(g.dh_bf16 + p * (2 * I) + 2 * i0);
+  float ds = 0.0f, am = 0.0f;
+  // pass 1, eight columns at a time: dS, a', bf16 dH and the amax of the row's 128 dH values
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 h0 = hrow[2 * c], h1 = hrow[2 * c + 1];
+    const uint32_t w[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    uint32_t ap[4], dh[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float dap = __uint_as_float(v[8 * c + k]);
+      float a, dg, du;
+      dact_grad(dap, __uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xFFFF0000u), sc, a, dg, du);
+      ds = fmaf(dap, a, ds);
+      am = fmaxf(am, fmaxf(fabsf(dg), fabsf(du)));
+      dh[k] = pack_bf16x2(dg, du);
+      if (k & 1) ap[k >> 1] = pack_bf16x2(__uint_as_float(ap[k >> 1]), sc * a);
+      else ap[k >> 1] = __float_as_uint(sc * a);
+    }
+    adst[c] = make_uint4(ap[0], ap[1], ap[2], ap[3]);
+    hdst[2 * c] = make_uint4(dh[0], dh[1], dh[2], dh[3]);
+    hdst[2 * c + 1] = make_uint4(dh[4], dh[5], dh[6], dh[7]);
+  }
+  atomicAdd(g.ds + g.s_scatter[m.tok], ds);
+  // pass 2: the same dH values (recomputed) as e4m3 under the row's UE8M0 scale
+  const int e8 = scale_exp_of_amax(am);
+  const float inv = exp2_neg(e8);
+  uint4* qdst = reinterpret_cast<uint4*>(g.out_q + p * (2 * I) + 2 * i0);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 h0 = hrow[2 * c], h1 = hrow[2 * c + 1];
+    const uint32_t w[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    uint32_t q[4];
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      float a0, dg0, du0, a1, dg1, du1;
+      dact_grad(__uint_as_float(v[8 * c + k]), __uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xFFFF0000u), sc,
+                a0, dg0, du0);
+      dact_grad(__uint_as_float(v[8 * c + k + 1]), __uint_as_float(w[k + 1] << 16),
+                __uint_as_float(w[k + 1] & 0xFFFF0000u), sc, a1, dg1, du1);
+      q[k >> 1] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(dg0, inv), __fmul_rn(du0, inv))) |
+                  (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(dg1, inv), __fmul_rn(du1, inv))) << 16);
+    }
+    qdst[c] = make_uint4(q[0], q[1], q[2], q[3]);
+  }
+  // K block (2 i0) / 128 = 4 nt + cc of the dX GEMM; atoms hold 4 consecutive K blocks
+  const int KG2 = (2 * I / kBlockK + 3) / 4;
+  const int kb2 = 4 * m.nt + cc;
+  const int rr = m.p % kBlockM;
+  g.out_sf[(static_cast<size_t>(m.mb) * KG2 + kb2 / 4) * kSfAtomBytes + 16 * (rr % 32) + 4 * (rr / 32) + (kb2 % 4)] =
+      static_cast<uint8_t>(e8 + 127);
 }
 
 // Epilogue of one accumulator tile: this thread holds row r (0..127) of the tile's 128-row block,
@@ -129,14 +227,17 @@ __device__ __forceinline__ RowMeta load_row_meta(const GemmArgs& g, int tile, in
 //          outputs of the tile (four threads, exchanged through shared memory), 1x128 requant.
 //   down : scale by the entry's router score, stage 128 bytes of bf16 in this thread's slot and
 //          bulk-reduce them into the token's output row.
-template <bool kUp>
+template <int kKind>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const uint32_t (&v)[64], const RowMeta& m, int r,
                                               int cc, int ew, int lane, int tcount, float* s_amax, uint64_t* amax_bar,
                                               uint64_t* store_bar, uint8_t* sStage, const CUtensorMap* tmap_out,
                                               uint64_t pol_out) {
+  constexpr bool kUp = kKind == kKindUp;
   const bool valid = m.valid != 0;
   const int p = m.p, mb = m.mb, nt = m.nt;
-  if constexpr (kUp) {
+  if constexpr (kKind == kKindDact) {
+    dact_tile(g, v, m, cc);
+  } else if constexpr (kUp) {
     if (g.preact != nullptr && valid) {
       // training forward: h as bf16 in the caller's w1 column order (interleaved: this thread's 64
       // tile columns are consecutive; concatenated: 32 gate columns and the matching 32 up columns)
@@ -251,11 +352,40 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const uint32_t 
   return true;
 }
 
-template <bool kUp>
+// Tile t of the schedule: A row block (m-block of the padded layout, or m-tile of the weight-gradient
+// output), n-tile, expert, first K block and number of K blocks.
+struct TileInfo {
+  int mb, nt, e, kb0, nkb;
+};
+template <int kKind>
+__device__ __forceinline__ TileInfo tile_info(const GemmArgs& g, int tile, int n_blocks, int ntn, int KB) {
+  TileInfo ti;
+  if constexpr (kKind == kKindWgrad) {
+    const int mt_n = g.a_rows / kBlockM;
+    const int per_e = mt_n * ntn;
+    ti.e = tile / per_e;
+    const int rem = tile - ti.e * per_e;
+    ti.mb = rem / ntn;
+    ti.nt = rem - ti.mb * ntn;
+    const int p0 = g.off_pad[ti.e];
+    ti.kb0 = p0 / kBlockK;
+    ti.nkb = (g.off_pad[ti.e + 1] - p0) / kBlockK;
+  } else {
+    tile_coords(tile, n_blocks, ntn, g.n_slices, ti.mb, ti.nt);
+    ti.e = g.blk_expert[ti.mb];
+    ti.kb0 = 0;
+    ti.nkb = KB;
+  }
+  return ti;
+}
+
+template <int kKind>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_out, const GemmArgs g) {
-  using L = GemmSmem<kUp>;
+  constexpr bool kUp = kKind == kKindUp;
+  constexpr bool kWgrad = kKind == kKindWgrad;
+  using L = GemmSmem<kKind>;
   constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -303,9 +433,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  const int n_blocks = *g.n_blocks;
+  const int n_blocks = kWgrad ? 0 : *g.n_blocks;
   const int ntn = g.N / kBN;
-  const int total = n_blocks * ntn;
+  const int total = kWgrad ? g.E * static_cast<int>(g.a_rows / kBlockM) * ntn : n_blocks * ntn;
   const int KB = g.Kd / kBlockK;
   const int KG = (KB + 3) / 4;
   const int nbk = g.N / kBlockM;
@@ -315,33 +445,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // ------------------------------------------------------------------ TMA producer
       // up: each A block is read by the 8 n-tiles running side by side, keep it; down: A streams
       // through once per column slice (evict_last measured ~1% faster for up, no gain for down)
-      const uint64_t pol_a = kUp ? policy_evict_last() : policy_evict_first();
+      const uint64_t pol_a = kKind == kKindDown ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_b = policy_evict_last();
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        int mb, nt;
-        tile_coords(tile, n_blocks, ntn, g.n_slices, mb, nt);
-        const int e = g.blk_expert[mb];
-        const int a_row = mb * kBlockM;
-        const int b_row = e * g.N + nt * kBN;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        const TileInfo ti = tile_info<kKind>(g, tile, n_blocks, ntn, KB);
+        if (ti.nkb == 0) continue;  // weight gradient of an expert without rows (output pre-zeroed)
+        const int a_row = ti.mb * kBlockM;
+        // B rows: expert e's N rows; the weight gradient's B has one set of rows for all experts
+        const int b_row = (kWgrad ? 0 : ti.e * g.N) + ti.nt * kBN;
+        for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, g.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
-          const bool sf = (kb & 3) == 0;
+          const int kg = ti.kb0 + kb;  // K block in the operands
+          // scale atoms cover 4 K blocks; a weight-gradient tile may start in the middle of one
+          const bool sf = (kg & 3) == 0 || kb == 0;
           mbar_arrive_expect_tx(&full[s], kABytes + kBBytes + (sf ? kSfaBytes + kSfbBytes : 0));
-          tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBlockK, a_row, pol_a);
-          tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBlockK, b_row, pol_b);
+          tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kg * kBlockK, a_row, pol_a);
+          tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kg * kBlockK, b_row, pol_b);
           if (sf) {
-            bulk_load(sSfa + s * kSfaBytes, g.a_sf + (static_cast<size_t>(mb) * KG + kb / 4) * kSfAtomBytes,
+            bulk_load(sSfa + s * kSfaBytes, g.a_sf + (static_cast<size_t>(ti.mb) * KG + kg / 4) * kSfAtomBytes,
                       kSfAtomBytes, &full[s]);
-            const size_t nb0 = static_cast<size_t>(e) * nbk + static_cast<size_t>(nt) * 2;
-            bulk_load(sSfb + s * kSfbBytes, g.b_sf + (nb0 * KG + kb / 4) * kSfAtomBytes, kSfAtomBytes, &full[s]);
-            bulk_load(sSfb + s * kSfbBytes + kSfAtomBytes, g.b_sf + ((nb0 + 1) * KG + kb / 4) * kSfAtomBytes,
+            const size_t nb0 = static_cast<size_t>(kWgrad ? 0 : ti.e) * nbk + static_cast<size_t>(ti.nt) * 2;
+            bulk_load(sSfb + s * kSfbBytes, g.b_sf + (nb0 * KG + kg / 4) * kSfAtomBytes, kSfAtomBytes, &full[s]);
+            bulk_load(sSfb + s * kSfbBytes + kSfAtomBytes, g.b_sf + ((nb0 + 1) * KG + kg / 4) * kSfAtomBytes,
                       kSfAtomBytes, &full[s]);
           }
         }
@@ -358,13 +490,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t idesc0 = idesc_mxf8_e4m3(kBlockM, kBN, 0, 0);
       int it = 0, tcount = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tcount) {
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const TileInfo ti = tile_info<kKind>(g, tile, n_blocks, ntn, KB);
+        if (ti.nkb == 0) continue;
         if (!mbar_wait(tmem_empty, (tcount & 1) ^ 1, g.err, kErrTimeoutMma)) {
           ok = false;
           break;
         }
+        ++tcount;
         tc_fence_after();
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&full[s], ph, g.err, kErrTimeoutMma)) {
@@ -372,8 +507,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t id = static_cast<uint32_t>(kb & 3);
-          if (id == 0) {
+          const int kg = ti.kb0 + kb;
+          const uint32_t id = static_cast<uint32_t>(kg & 3);
+          if (id == 0 || kb == 0) {
             tc_cp_sf(tmem + kTmemSfa, sdesc_sf(smem_u32(sSfa + s * kSfaBytes)));
             tc_cp_sf(tmem + kTmemSfb, sdesc_sf(smem_u32(sSfb + s * kSfbBytes)));
             tc_cp_sf(tmem + kTmemSfb + 4, sdesc_sf(smem_u32(sSfb + s * kSfbBytes + kSfAtomBytes)));
@@ -405,7 +541,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     int tcount = 0;
     const uint64_t pol_out = policy_evict_last();
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tcount) {
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      TileInfo ti{};
+      if constexpr (kWgrad) {
+        ti = tile_info<kKind>(g, tile, n_blocks, ntn, KB);
+        if (ti.nkb == 0) continue;
+      }
       if (!mbar_wait(tmem_full, tcount & 1, g.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       uint32_t v[64];
@@ -421,11 +562,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tmem_empty);
 
-      // the accumulator is released: the row's metadata loads overlap the next tile's main loop
-      const RowMeta meta = load_row_meta<kUp>(g, tile, n_blocks, ntn, r);
-      if (!epilogue_tile<kUp>(g, v, meta, r, cc, ew, lane, tcount, s_amax, amax_bar, store_bar, sStage, &tmap_out,
-                              pol_out))
-        break;
+      if constexpr (kWgrad) {
+        // D[e] rows 128 mt + r, columns 256 nt + 64 cc .. + 63, as bf16
+        __nv_bfloat16* dst = g.out_w + (static_cast<size_t>(ti.e) * g.a_rows + ti.mb * kBlockM + r) * g.N +
+                             ti.nt * kBN + 64 * cc;
+#pragma unroll
+        for (int j = 0; j < 64; j += 8)
+          *reinterpret_cast<uint4*>(dst + j) =
+              make_uint4(pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
+                         pack_bf16x2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])),
+                         pack_bf16x2(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5])),
+                         pack_bf16x2(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7])));
+        ++tcount;
+        continue;
+      } else {
+        // the accumulator is released: the row's metadata loads overlap the next tile's main loop
+        const RowMeta meta = load_row_meta<kKind>(g, tile, n_blocks, ntn, r);
+        const bool ok_tile = epilogue_tile<kKind>(g, v, meta, r, cc, ew, lane, tcount, s_amax, amax_bar, store_bar,
+                                                  sStage, &tmap_out, pol_out);
+        ++tcount;
+        if (!ok_tile) break;
+      }
     }
     // rows stored into other GPUs' memory are performed system-wide before the kernel completes
     if (kUp && g.ret_dst != nullptr) __threadfence_system();
@@ -496,28 +653,30 @@ int down_slices(long long tokens, int N) {
   return slices;
 }
 
-template <bool kUp>
+template <int kKind>
 static cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t st) {
+  constexpr bool kUp = kKind == kKindUp;
   const long long max_blocks = g.a_rows / kBlockM;
-  const long long max_tiles = max_blocks * (g.N / kBN);
+  const long long max_tiles = max_blocks * (g.N / kBN) * (kKind == kKindWgrad ? g.E : 1);
   if (max_tiles == 0) return cudaSuccess;
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, g.a, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.Kd), kBlockM)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tb, g.b, static_cast<uint64_t>(g.E) * g.N, static_cast<uint64_t>(g.Kd), kBN)) return cudaErrorInvalidValue;
+  const uint64_t b_rows = static_cast<uint64_t>(kKind == kKindWgrad ? 1 : g.E) * g.N;
+  if (!make_tmap(&tb, g.b, b_rows, static_cast<uint64_t>(g.Kd), kBN)) return cudaErrorInvalidValue;
   CUtensorMap to = ta;  // the down projection and the expert-parallel up projection have no tiled output
   if (kUp && g.ret_dst == nullptr &&
       !make_tmap(&to, g.out_q, static_cast<uint64_t>(g.a_rows), static_cast<uint64_t>(g.N / 2), kBlockM))
     return cudaErrorInvalidValue;
   if (kUp && g.ret_dst != nullptr && (g.n_homes < 1 || g.n_homes > kMaxEpRanks || g.home_rows < 0))
     return cudaErrorInvalidValue;
-  auto kern = moe_gemm_kernel<kUp>;
-  constexpr int kSmemAlloc = GemmSmem<kUp>::kAlloc;
+  auto kern = moe_gemm_kernel<kKind>;
+  constexpr int kSmemAlloc = GemmSmem<kKind>::kAlloc;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
   if (e != cudaSuccess) return e;
   const int grid = static_cast<int>(max_tiles < g.num_sms ? max_tiles : g.num_sms);
   GemmArgs ga = g;
   ga.n_slices = 1;
-  if (!kUp) ga.n_slices = down_slices(g.tokens, g.N);
+  if (kKind == kKindDown) ga.n_slices = down_slices(g.tokens, g.N);
   kern<<<grid, kGemmThreads, kSmemAlloc, st>>>(ta, tb, to, ga);
   return cudaGetLastError();
 }
@@ -533,8 +692,10 @@ int gemm_grid_sms() {
   return n - (r > 0 ? r : 0);
 }
 
-cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st) { return launch_gemm<true>(g, st); }
-cudaError_t launch_moe_down(const GemmArgs& g, cudaStream_t st) { return launch_gemm<false>(g, st); }
+cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st) { return launch_gemm<kKindUp>(g, st); }
+cudaError_t launch_moe_down(const GemmArgs& g, cudaStream_t st) { return launch_gemm<kKindDown>(g, st); }
+cudaError_t launch_moe_dact(const GemmArgs& g, cudaStream_t st) { return launch_gemm<kKindDact>(g, st); }
+cudaError_t launch_moe_wgrad(const GemmArgs& g, cudaStream_t st) { return launch_gemm<kKindWgrad>(g, st); }
 
 }  // namespace smb
 

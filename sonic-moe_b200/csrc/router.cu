@@ -254,7 +254,10 @@ __global__ void __launch_bounds__(RouterShape<PL>::kWarps * 32)
 // the accumulator (warp w: rows 32 (w % 4) .. + 31).
 constexpr int kRfThreads = 512;
 constexpr int kRfKBlock = 64;  // bf16 values per 128-byte swizzled row: K extent of one stage
-constexpr int kRfStages = 4;
+// Ring depth: 3 stages when a stage is at most 32 KB (E <= 128), so that two CTAs share an SM and
+// one tile's top-k and ring refill overlap the other's MMAs; 4 stages (one CTA per SM) above.
+constexpr int kRfMaxStages = 4;
+__host__ __device__ constexpr int rf_stages(int E) { return E <= 128 ? 3 : 4; }
 constexpr int kRfABytes = kTileTokens * 128;  // 16 KB of x per stage
 
 __device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -273,7 +276,7 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
 }
 
 template <int PL, int KMAX>
-__global__ void __launch_bounds__(kRfThreads, 1)
+__global__ void __launch_bounds__(kRfThreads, 2)
     router_fused_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         int T, int H, int E, int K, int vec, int softmax_over_topk, int renorm, uint32_t tmem_cols,
                         __nv_bfloat16* __restrict__ logits, float* __restrict__ scores,
@@ -282,8 +285,9 @@ __global__ void __launch_bounds__(kRfThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   const int stage_bytes = kRfABytes + E * 128;  // multiple of 4 KB (E % 32 == 0)
+  const int kRfStages = rf_stages(E);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRfStages * stage_bytes);
-  uint64_t* empty = full + kRfStages;
+  uint64_t* empty = full + kRfMaxStages;
   uint64_t* tmem_full = empty + kRfStages;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_full + 1);
   int32_t* s_hist = reinterpret_cast<int32_t*>(tmem_holder + 4);  // [E]
@@ -623,7 +627,7 @@ static cudaError_t launch_router_fused_t(const void* x, const void* w, int T, in
     return cudaErrorInvalidValue;
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(E)) cols <<= 1;
-  const int smem = kRfStages * (kRfABytes + E * 128) + (2 * kRfStages + 1) * 8 + 16 + E * 4 + 1024;
+  const int smem = rf_stages(E) * (kRfABytes + E * 128) + (2 * kRfMaxStages + 1) * 8 + 16 + E * 4 + 1024;
   auto kern = router_fused_kernel<PL, KMAX>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

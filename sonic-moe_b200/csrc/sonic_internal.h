@@ -64,6 +64,13 @@ cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* expert
                               uint8_t* xsf, cudaStream_t st);
 cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_glu, uint8_t* wq, uint8_t* wsf,
                                cudaStream_t st);
+// backward (csrc/backward.cu)
+cudaError_t launch_weight_prep_t(const void* w, int E, int N, int Kd, uint8_t* wq, uint8_t* wsf, cudaStream_t st);
+cudaError_t launch_tq_pack(const void* src, int C, int src_padded, const int32_t* blk_expert, const int32_t* off_pad,
+                           const int32_t* off, const int32_t* freq, const int32_t* x_gather, const int32_t* n_blocks,
+                           int max_blocks, uint8_t* outq, uint8_t* outsf, cudaStream_t st);
+cudaError_t launch_router_bwd(const void* logits, const float* scores, const int32_t* idx, const float* ds, int T,
+                              int E, int K, int sot, int renorm, float* dlogits, cudaStream_t st);
 
 struct GemmArgs {
   // A: padded expert-major activations [rows, Kd] e4m3 + SF atoms [rows/128][ceil(Kd/512)][512]
@@ -102,6 +109,17 @@ struct GemmArgs {
   // entry order: row off[e] + (p - off_pad[e]) for padded row p, columns in the caller's w1 order);
   // null: not stored
   __nv_bfloat16* preact;
+  // activation-gradient GEMM (A = dO rows packed like the forward's x, B = W2 transposed [E, I, H],
+  // N = I): h_in [T*K, 2I] the forward's pre-activation (expert-sorted rows); outputs out_q / out_sf
+  // = dH e4m3 + atoms (padded rows, K = 2I), dh_bf16 [rows, 2I] and a_prime [rows, I] (padded
+  // rows), ds [T*K] fp32 accumulated by flat entry (zeroed by the caller)
+  const __nv_bfloat16* h_in;
+  __nv_bfloat16* dh_bf16;
+  __nv_bfloat16* a_prime;
+  float* ds;
+  // weight-gradient GEMM: A [a_rows, Kd] and B [N, Kd] e4m3 with K = padded entry rows (1x128 scale
+  // groups along K), expert e owning K rows [off_pad[e], off_pad[e+1]); out_w [E, a_rows, N] bf16
+  __nv_bfloat16* out_w;
   int* err;
   int num_sms;
   int tokens;    // T (rows of the token-major output), for the down projection's slice choice
@@ -118,5 +136,7 @@ int down_slices(long long tokens, int N);
 
 cudaError_t launch_moe_up(const GemmArgs& g, cudaStream_t st);
 cudaError_t launch_moe_down(const GemmArgs& g, cudaStream_t st);
+cudaError_t launch_moe_dact(const GemmArgs& g, cudaStream_t st);
+cudaError_t launch_moe_wgrad(const GemmArgs& g, cudaStream_t st);
 
 }  // namespace smb

@@ -254,13 +254,13 @@ def check_count_matrix(C, send_cap: int, out_cap: int, me: int) -> str:
 def default_transport(world: int, native: bool = True, chunks: int = None) -> str:
     """Transport chosen when the caller names none, from the measurements at config 2 per rank.
 
-    * 2 ranks: the home-down transport (4.08 ms per forward against 4.34 for peer loads with the
-      down projection at the owners, in the same call: the bytes back per rank are 6x smaller for
-      e4m3 intermediate rows than for bf16 partial rows).
-    * 3-7 ranks: peer loads in one chunk (6.00-6.17 ms at 4 ranks; copy engines 6.25).
+    * 2-4 ranks: the home-down transport (2 ranks: 4.08-4.13 ms per forward against 4.33 for peer
+      loads with the down projection at the owners; 4 ranks: 5.11 against 6.24 ms, in the same
+      call: the bytes back per rank are 6x smaller for e4m3 intermediate rows than for bf16
+      partial rows).  At config 4 (E=256, H=7168) the two are within 2% at 2 and 4 ranks.
+    * 5-7 ranks: peer loads in one chunk (not measured at these sizes).
     * 8 and more: copy-engine transfers pipelined over 6 chunks (7.01 ms at 8 ranks, against 9.54
-      for one-chunk peer loads).
-    The home-down transport has been measured at 2 ranks only, so it is the default there only.
+      for one-chunk peer loads); the home-down transport is not measured at 8.
     A caller that asks for chunks > 1 gets the chunked transports; device-stage stand-ins (tests)
     take NCCL.
     """
@@ -268,7 +268,7 @@ def default_transport(world: int, native: bool = True, chunks: int = None) -> st
         return "nccl"
     if world >= 8:
         return "copy"
-    if world == 2 and (chunks is None or chunks == 1):
+    if world <= 4 and (chunks is None or chunks == 1):
         return "home"
     return "p2p"
 

@@ -23,11 +23,17 @@ after the router GEMM is one more registered op per entry point (``sonicmoe::fp8
 ``sonicmoe::fp8_moe_general_forward``, with fake implementations for tracing), so ``torch.compile``
 traces a whole ``MoE`` forward without a graph break.
 
+Training: with ``is_inference_mode_enabled=False`` while autograd is recording and an input or
+weight requires grad, ``moe_TC_softmax_topk_layer`` runs the training forward (the up GEMM also
+stores the pre-activation h) inside an autograd function whose backward is the engine's FP8
+backward (``ops.moe_backward``: dx, the router logits' gradient, dw1, dw2), as the reference's
+``_UpProjection`` / ``_DownProjection`` / router functions do.
+
 Differences from the reference, all explicit errors: biases and activations other than SwiGLU
-raise ``NotImplementedError`` (the FP8 engine implements the bias-free SwiGLU layer); the forward
-is inference-only: with ``is_inference_mode_enabled=False`` while autograd is recording and an
-input or weight requires grad, the layer raises ``NotImplementedError`` instead of returning an
-output whose expert weights would never receive a gradient.
+raise ``NotImplementedError`` (the FP8 engine implements the bias-free SwiGLU layer); the backward
+covers the interleaved w1 layout of ``moe_TC_softmax_topk_layer`` with I % 256 == 0 --
+``concat_layout=True`` and ``moe_general_routing_inputs`` raise ``NotImplementedError`` when a
+gradient is requested, instead of returning an output whose expert weights would never receive one.
 """
 import weakref
 
@@ -115,15 +121,68 @@ def _check_common(b1, b2, activation_type):
     return activation_type
 
 
-def _reject_training(is_inference_mode_enabled, *tensors):
+def _wants_training(is_inference_mode_enabled, *tensors) -> bool:
+    """True when autograd must see the layer: a training-mode call while grad is recorded and an input
+    or weight requires grad."""
     if is_inference_mode_enabled or not torch.is_grad_enabled():
-        return
-    if any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors):
+        return False
+    return any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors)
+
+
+def _reject_training(is_inference_mode_enabled, *tensors, what="this layer"):
+    if _wants_training(is_inference_mode_enabled, *tensors):
         raise NotImplementedError(
-            "the FP8 B200 engine implements the inference forward only: call it with "
-            "is_inference_mode_enabled=True (MoE: eval() or is_inference_mode=True) or under torch.no_grad(); "
-            "no backward is provided, so training would leave the expert weights without gradients"
+            f"the FP8 B200 engine has no backward for {what}: call it with is_inference_mode_enabled=True "
+            "or under torch.no_grad(); training would leave the expert weights without gradients"
         )
+
+
+class _FP8MoEFunction(torch.autograd.Function):
+    """Training forward + FP8 backward of the token-choice layer after the router GEMM (the reference's
+    router function, _UpProjection and _DownProjection autograd functions,
+    functional/__init__.py:174-202, 227-479).  Inputs: x [T, H] bf16, router_logits [T, E], w1 / w2 in
+    the reference's (2I, H, E) / (H, I, E) views (interleaved gate/up rows); outputs (o, expert_frequency)."""
+
+    @staticmethod
+    def forward(ctx, x, router_logits, w1, w2, K, softmax_over_topk, norm_topk_probs):
+        w1q = prepare_fp8_weights(w1, concat_glu=False)
+        w2q = prepare_fp8_weights(w2, concat_glu=False)
+        T, H = x.shape
+        E = router_logits.shape[1]
+        I = w1q.shape[1] // 2
+        dev = x.device
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        scores, idx = ops.router_topk(router_logits, K, softmax_over_topk, norm_topk_probs)
+        plan = ops.route_plan(idx, E, err)
+        xq, xsf = ops.quant_pack(x, idx, plan)
+        h = torch.empty(T * K, 2 * I, dtype=torch.bfloat16, device=dev)
+        aq, asf = ops.moe_up(xq, xsf, w1q, plan, err, preact_out=h)
+        del xq, xsf
+        out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+        ops.moe_down_combine(aq, asf, w2q, plan, scores, T, err, out=out)
+        ctx.save_for_backward(x, router_logits, w1, w2, scores, idx, h, err, plan.freq, plan.off, plan.x_gather,
+                              plan.s_scatter, plan.s_rev, plan.off_pad, plan.blk_expert, plan.n_blocks)
+        ctx.max_blocks = plan.max_blocks
+        ctx.modes = (bool(softmax_over_topk), bool(norm_topk_probs))
+        freq = plan.freq.clone()
+        ctx.mark_non_differentiable(freq)
+        return out, freq
+
+    @staticmethod
+    def backward(ctx, dout, _dfreq):
+        (x, router_logits, w1, w2, scores, idx, h, err, freq, off, x_gather, s_scatter, s_rev, off_pad, blk_expert,
+         n_blocks) = ctx.saved_tensors
+        plan = ops.RoutePlan(freq, off, x_gather, s_scatter, s_rev, off_pad, blk_expert, n_blocks, ctx.max_blocks)
+        sot, norm = ctx.modes
+        w1e = _as_expert_major(w1.detach()).contiguous()
+        w2e = _as_expert_major(w2.detach()).contiguous()
+        dx, dlogits, dw1, dw2, _ = ops.moe_backward(dout.to(torch.bfloat16), x, router_logits, w1e, w2e, scores, idx,
+                                                    plan, h, sot, norm, err)
+        code = int(err.item())
+        if code:
+            raise RuntimeError(f"FP8 MoE backward: device error {code}")
+        return (dx, dlogits.to(router_logits.dtype), dw1.permute(1, 2, 0).to(w1.dtype), dw2.permute(1, 2, 0).to(w2.dtype),
+                None, None, None)
 
 
 @torch.library.custom_op("sonicmoe::fp8_moe_tc_forward", mutates_args=())
@@ -224,10 +283,19 @@ def moe_TC_softmax_topk_layer(
     _check_common(b1, b2, activation_type)
     if norm_topk_probs and is_softmax_over_topk:
         raise ValueError("`norm_topk_prob` only works with softmax-then-topk")
-    _reject_training(is_inference_mode_enabled, x, router_w, w1, w2)
+    training = _wants_training(is_inference_mode_enabled, x, router_w, w1, w2)
+    if training and (concat_layout or fused_router or isinstance(w1, Fp8ExpertWeights)
+                     or isinstance(w2, Fp8ExpertWeights)):
+        raise NotImplementedError("the FP8 backward covers bf16 weights in the interleaved layout with the "
+                                  "F.linear router (no concat_layout, fused_router or prepared weights)")
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
     x = x.contiguous()
+    if training:
+        router_logits = F.linear(x, router_w.to(x.dtype))
+        o, expert_frequency = _FP8MoEFunction.apply(x, router_logits, w1, w2, K, is_softmax_over_topk,
+                                                    norm_topk_probs)
+        return o, router_logits, expert_frequency
     if fused_router:
         rw = router_w.to(x.dtype).contiguous()
         if isinstance(w1, Fp8ExpertWeights) or isinstance(w2, Fp8ExpertWeights):
@@ -279,7 +347,7 @@ def moe_general_routing_inputs(
     (``functional/__init__.py:592``).
     """
     _check_common(b1, b2, activation_type)
-    _reject_training(is_inference_mode_enabled, x, router_scores, w1, w2)
+    _reject_training(is_inference_mode_enabled, x, router_scores, w1, w2, what="moe_general_routing_inputs")
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
     x = x.contiguous()

@@ -395,3 +395,112 @@ def moe_general_forward(
         _ptr(expert_frequency), _ptr(ws), ws.numel(), _ptr(err), _stream(),
     )
     return out, expert_frequency
+
+
+# ---------------------------------------------------------------------------------------------
+# backward stages (FP8, interleaved SwiGLU); see include/sonic_b200.h for the data layouts
+
+
+def weight_prep_t(w: torch.Tensor) -> Fp8ExpertWeights:
+    """W^T as a backward GEMM's K-major operand: w [E, N, K] bf16 -> e4m3 [E, K, N] with the 128x128
+    block scales of w (the same blocks, read transposed)."""
+    if w.dtype != torch.bfloat16:
+        w = w.to(torch.bfloat16)
+    w = w.contiguous()
+    E, N, K = w.shape
+    q = torch.empty(E, K, N, dtype=torch.uint8, device=w.device)
+    sf = torch.zeros(E, K // _BLOCK_M, -(-(N // 128) // 4), 512, dtype=torch.uint8, device=w.device)
+    nat.call("sm_weight_prep_t", _ptr(w), E, N, K, _ptr(q), _ptr(sf), _stream())
+    return Fp8ExpertWeights(q, sf, False)
+
+
+def moe_dact(doq, dosf, w2t: Fp8ExpertWeights, plan: RoutePlan, scores_flat: torch.Tensor, preact: torch.Tensor, err,
+             dscores: torch.Tensor = None):
+    """dA' = dO W2 per entry fused with the SwiGLU backward: (dh_q, dh_sf, dh_bf16, a_prime, dscores)."""
+    E, I, H = w2t.shape
+    rows = plan.max_blocks * _BLOCK_M
+    dev = doq.device
+    dh_q = torch.empty(rows, 2 * I, dtype=torch.uint8, device=dev)
+    dh_sf = torch.zeros(plan.max_blocks, -(-(2 * I) // 512), 512, dtype=torch.uint8, device=dev)
+    dh = torch.empty(rows, 2 * I, dtype=torch.bfloat16, device=dev)
+    a_prime = torch.empty(rows, I, dtype=torch.bfloat16, device=dev)
+    if dscores is None:
+        dscores = torch.zeros(preact.shape[0], dtype=torch.float32, device=dev)
+    _need(preact, "preact", torch.bfloat16)
+    nat.call(
+        "sm_moe_dact", _ptr(doq), _ptr(dosf), _ptr(w2t.q), _ptr(w2t.sf), H, I, E, plan.max_blocks,
+        _ptr(plan.blk_expert), _ptr(plan.n_blocks), _ptr(plan.off_pad), _ptr(plan.off), _ptr(plan.freq),
+        _ptr(plan.s_scatter), _ptr(scores_flat), _ptr(preact), _ptr(dh_q), _ptr(dh_sf), _ptr(dh), _ptr(a_prime),
+        _ptr(dscores), _ptr(err), _stream(),
+    )
+    return dh_q, dh_sf, dh, a_prime, dscores
+
+
+def tq_pack(src: torch.Tensor, plan: RoutePlan, padded: bool):
+    """Transposed, column-quantised weight-gradient operand [C, rows] of padded rows (gathered token
+    rows of src [T, C] when not ``padded``)."""
+    _need(src, "src", torch.bfloat16)
+    C = src.shape[1]
+    rows = plan.max_blocks * _BLOCK_M
+    q = torch.empty(C, rows, dtype=torch.uint8, device=src.device)
+    sf = torch.zeros(C // _BLOCK_M, -(-plan.max_blocks // 4), 512, dtype=torch.uint8, device=src.device)
+    nat.call(
+        "sm_tq_pack", _ptr(src), C, int(padded), plan.max_blocks, _ptr(plan.blk_expert), _ptr(plan.n_blocks),
+        _ptr(plan.off_pad), _ptr(plan.off), _ptr(plan.freq), _ptr(plan.x_gather), _ptr(q), _ptr(sf), _stream(),
+    )
+    return q, sf
+
+
+def moe_wgrad(aq, asf, bq, bsf, E: int, plan: RoutePlan, err):
+    """Per-expert weight gradient [E, M, N] bf16 = A[:, rows_e] B[:, rows_e]^T."""
+    M, N = aq.shape[0], bq.shape[0]
+    out = torch.empty(E, M, N, dtype=torch.bfloat16, device=aq.device)
+    nat.call("sm_moe_wgrad", _ptr(aq), _ptr(asf), _ptr(bq), _ptr(bsf), M, N, E, plan.max_blocks, _ptr(plan.off_pad),
+             _ptr(out), _ptr(err), _stream())
+    return out
+
+
+def router_bwd(router_logits: torch.Tensor, scores: torch.Tensor, idx: torch.Tensor, dscores: torch.Tensor,
+               softmax_over_topk: bool = True, norm_topk_probs: bool = False):
+    """Gradient of the router logits [T, E] (fp32) from the scores' gradient [T, K]."""
+    T, E = router_logits.shape
+    K = idx.shape[1]
+    dl = torch.empty(T, E, dtype=torch.float32, device=router_logits.device)
+    nat.call("sm_router_bwd", _ptr(router_logits), _ptr(scores), _ptr(idx), _ptr(dscores.contiguous()), T, E, K,
+             int(softmax_over_topk), int(norm_topk_probs), _ptr(dl), _stream())
+    return dl
+
+
+def moe_backward(dout: torch.Tensor, x: torch.Tensor, router_logits: torch.Tensor, w1: torch.Tensor,
+                 w2: torch.Tensor, scores: torch.Tensor, idx: torch.Tensor, plan: RoutePlan, preact: torch.Tensor,
+                 softmax_over_topk: bool, norm_topk_probs: bool, err):
+    """The layer backward from dO [T, H]: (dx [T, H] bf16, dlogits [T, E] fp32, dw1 [E, 2I, H] bf16,
+    dw2 [E, H, I] bf16, dscores [T, K] fp32).  w1 / w2: the bf16 expert weights [E, 2I, H] / [E, H, I]
+    (interleaved gate/up rows)."""
+    T, H = dout.shape
+    E = w1.shape[0]
+    K = idx.shape[1]
+    dout = dout.contiguous()
+    doq, dosf = quant_pack(dout, idx, plan)
+    w2t = weight_prep_t(w2)
+    dh_q, dh_sf, dh, a_prime, ds = moe_dact(doq, dosf, w2t, plan, scores.view(-1), preact, err)
+    del doq, dosf, w2t
+    w1t = weight_prep_t(w1)
+    dx = torch.zeros(T, H, dtype=torch.bfloat16, device=dout.device)
+    E1, H1, N2 = w1t.shape
+    nat.call(
+        "sm_moe_down_combine", _ptr(dh_q), _ptr(dh_sf), _ptr(w1t.q), _ptr(w1t.sf), H, N2, E, T, plan.max_blocks,
+        _ptr(plan.blk_expert), _ptr(plan.n_blocks), _ptr(plan.off_pad), _ptr(plan.off), _ptr(plan.freq),
+        _ptr(plan.s_scatter), _ptr(plan.x_gather), None, _ptr(dx), _ptr(err), _stream(),
+    )
+    del dh_q, dh_sf, w1t
+    dot_q, dot_sf = tq_pack(dout, plan, padded=False)
+    apt_q, apt_sf = tq_pack(a_prime, plan, padded=True)
+    dw2 = moe_wgrad(dot_q, dot_sf, apt_q, apt_sf, E, plan, err)  # [E, H, I]
+    del dot_q, dot_sf, apt_q, apt_sf, a_prime
+    dht_q, dht_sf = tq_pack(dh, plan, padded=True)
+    xt_q, xt_sf = tq_pack(x.contiguous(), plan, padded=False)
+    dw1 = moe_wgrad(dht_q, dht_sf, xt_q, xt_sf, E, plan, err)  # [E, 2I, H]
+    ds = ds.view(T, K)
+    dlogits = router_bwd(router_logits, scores, idx, ds, softmax_over_topk, norm_topk_probs)
+    return dx, dlogits, dw1, dw2, ds

@@ -159,15 +159,16 @@ def test_home_transport_arguments():
 
 
 def test_default_transport():
-    """One process or device-stage stand-ins: NCCL; the home-down transport only where it was
-    measured (2 ranks, one chunk); peer loads at 3-7 ranks; copy engines from 8 ranks."""
+    """One process or device-stage stand-ins: NCCL; the home-down transport where it was measured
+    (2 and 4 ranks, one chunk); peer loads at 5-7 ranks or with chunks; copy engines from 8 ranks."""
     from sonicmoe.ep import default_transport
 
     assert default_transport(1) == "nccl"
     assert default_transport(8, native=False) == "nccl"
     assert default_transport(2) == "home" and default_transport(2, chunks=1) == "home"
     assert default_transport(2, chunks=2) == "p2p"
-    assert default_transport(4) == "p2p" and default_transport(4, chunks=2) == "p2p"
+    assert default_transport(4) == "home" and default_transport(4, chunks=2) == "p2p"
+    assert default_transport(6) == "p2p"
     assert default_transport(8) == "copy" and default_transport(8, chunks=6) == "copy"
 
 

@@ -1,0 +1,137 @@
+"""GPU parity of the FP8 backward (stages of ``sonicmoe.ops.moe_backward`` and the autograd path of
+``moe_TC_softmax_topk_layer`` / ``MoE``) against the CPU restatement in ``oracle/backward.py``.
+
+Tolerance: relative Frobenius error <= 1e-2 for every gradient against the float64 oracle that
+fake-quantises the same operands (1x128 / 128x128 / column-wise e4m3, bf16 intermediates) -- the
+bound the forward uses.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import backward as obwd
+from oracle import routing as oroute
+from _util import make_layer_inputs, rel_fro
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+CASES = [
+    # T, H, I, E, K, softmax_over_topk, norm
+    (256, 512, 256, 8, 2, True, False),
+    (384, 1024, 512, 16, 4, False, True),
+    (64, 512, 256, 64, 8, False, False),  # most experts empty
+]
+
+
+@pytest.fixture(scope="module")
+def ops():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from sonicmoe import ops as _ops
+
+    return _ops
+
+
+def _forward_state(ops, x, rw, w1, w2, K, sot, norm):
+    """Routing, plan and stored pre-activation of the training forward (as the autograd function runs it)."""
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    logits = torch.nn.functional.linear(x, rw)
+    scores, idx = ops.router_topk(logits, K, sot, norm)
+    plan = ops.route_plan(idx, w1.shape[0], err)
+    xq, xsf = ops.quant_pack(x, idx, plan)
+    h = torch.empty(x.shape[0] * K, w1.shape[1], dtype=torch.bfloat16, device="cuda")
+    ops.moe_up(xq, xsf, ops.weight_prep(w1), plan, err, preact_out=h)
+    return logits, scores, idx, plan, h, err
+
+
+@pytest.mark.parametrize("T,H,I,E,K,sot,norm", CASES)
+def test_moe_backward_stages_vs_oracle(ops, T, H, I, E, K, sot, norm):
+    x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=11 * T + E)
+    xc, rwc, w1c, w2c = x.cuda(), rw.cuda(), w1.cuda(), w2.cuda()
+    logits, scores, idx, plan, h, err = _forward_state(ops, xc, rwc, w1c, w2c, K, sot, norm)
+    g = torch.Generator().manual_seed(T + 1)
+    dout = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
+    dx, dl, dw1, dw2, ds = ops.moe_backward(dout.cuda(), xc, logits, w1c, w2c, scores, idx, plan, h, sot, norm, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0, f"kernel error word {err.item()}"
+    s_np, i_np = scores.cpu().numpy(), idx.cpu().numpy()
+    s_ref, i_ref = oroute.topk_route(logits.float().cpu().numpy(), K, sot, norm)
+    np.testing.assert_array_equal(i_np, i_ref)
+    rdx, rdw1, rdw2, rds, rdl = obwd.fp8_backward(
+        x.float().numpy(), dout.float().numpy(), w1.float().numpy(), w2.float().numpy(), s_np, i_np,
+        h.float().cpu().numpy(), sot, norm, logits=logits.float().cpu().numpy())
+    for name, got, ref in (("ds", ds, rds), ("dlogits", dl, rdl), ("dx", dx, rdx), ("dw2", dw2, rdw2),
+                           ("dw1", dw1, rdw1)):
+        err_rel = rel_fro(got.float().cpu().numpy(), ref)
+        assert err_rel <= TOL, f"{name}: rel. Frobenius {err_rel:.3g}"
+
+
+def test_router_bwd_matches_oracle(ops):
+    T, E, K = 300, 64, 6
+    g = torch.Generator().manual_seed(3)
+    lg = torch.randn(T, E, generator=g).to(torch.bfloat16)
+    ds = torch.randn(T, K, generator=g)
+    for sot, norm in ((True, False), (False, False), (False, True)):
+        s, i = ops.router_topk(lg.cuda(), K, sot, norm)
+        dl = ops.router_bwd(lg.cuda(), s, i, ds.cuda(), sot, norm)
+        ref = obwd.router_backward(lg.float().numpy(), s.cpu().numpy(), i.cpu().numpy(), ds.numpy(), sot, norm)
+        assert rel_fro(dl.cpu().numpy(), ref) < 1e-5
+
+
+def test_weight_prep_t_is_the_transpose(ops):
+    from oracle import quant as oq
+
+    g = torch.Generator().manual_seed(4)
+    w = (torch.randn(3, 256, 384, generator=g) * 0.05).to(torch.bfloat16)
+    wt = ops.weight_prep_t(w.cuda())
+    w_f = ops.weight_prep(w.cuda())
+    # same e4m3 values, read transposed, and the transposed block scales
+    assert torch.equal(wt.q.cpu(), w_f.q.cpu().transpose(1, 2))
+    q, sf = oq.quant_128x128(w.float().numpy())
+    np.testing.assert_array_equal(wt.q.cpu().numpy(), q.transpose(0, 2, 1))
+
+
+@pytest.mark.parametrize("T,H,I,E,K,sot,norm", CASES[:2])
+def test_layer_autograd_vs_oracle(T, H, I, E, K, sot, norm):
+    """moe_TC_softmax_topk_layer in training mode: gradients of x (expert path + router F.linear),
+    router_w, w1, w2 through the autograd function, against the oracle plus the router GEMM's
+    float64 backward."""
+    from sonicmoe.functional import moe_TC_softmax_topk_layer
+
+    x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=13 * T + E)
+    xc = x.cuda().requires_grad_()
+    rwc = rw.cuda().requires_grad_()
+    w1c = w1.cuda().requires_grad_()
+    w2c = w2.cuda().requires_grad_()
+    o, logits, freq = moe_TC_softmax_topk_layer(xc, rwc, w1c.permute(1, 2, 0), None, w2c.permute(1, 2, 0), None, K,
+                                                None, is_inference_mode_enabled=False, is_softmax_over_topk=sot,
+                                                norm_topk_probs=norm)
+    g = torch.Generator().manual_seed(T + 2)
+    dout = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
+    (o.float() * dout.cuda().float()).sum().backward()
+    torch.cuda.synchronize()
+    from sonicmoe import ops
+
+    _, scores, idx, plan, h, _ = _forward_state(ops, x.cuda(), rw.cuda(), w1.cuda(), w2.cuda(), K, sot, norm)
+    lg = logits.detach().float().cpu().numpy()
+    rdx, rdw1, rdw2, _, rdl = obwd.fp8_backward(
+        x.float().numpy(), dout.float().numpy(), w1.float().numpy(), w2.float().numpy(), scores.cpu().numpy(),
+        idx.cpu().numpy(), h.float().cpu().numpy(), sot, norm, logits=lg)
+    rdx_total = rdx + rdl @ rw.double().numpy()
+    rdrw = rdl.T @ x.double().numpy()
+    for name, got, ref in (("dx", xc.grad, rdx_total), ("drouter_w", rwc.grad, rdrw), ("dw1", w1c.grad, rdw1),
+                           ("dw2", w2c.grad, rdw2)):
+        assert got is not None, name
+        err_rel = rel_fro(got.float().cpu().numpy(), ref)
+        assert err_rel <= TOL, f"{name}: rel. Frobenius {err_rel:.3g}"
+
+
+def test_training_refusals():
+    from sonicmoe.functional import moe_TC_softmax_topk_layer
+
+    x, rw, w1, w2 = make_layer_inputs(64, 512, 256, 8, seed=1)
+    w1c = w1.cuda().requires_grad_()
+    with pytest.raises(NotImplementedError, match="interleaved"):
+        moe_TC_softmax_topk_layer(x.cuda(), rw.cuda(), w1c.permute(1, 2, 0), None, w2.cuda().permute(1, 2, 0), None,
+                                  2, None, is_inference_mode_enabled=False, concat_layout=True)

@@ -197,8 +197,13 @@ def test_moe_module_forward(sm):
     with pytest.raises(RuntimeError, match="no autograd formula"):
         o.float().sum().backward()  # the output of an inference forward cannot be backpropagated
     o = o.detach()
-    with pytest.raises(NotImplementedError, match="inference forward only"):
-        m(x)  # training mode, autograd recording, weights require grad: no silent graph-less output
+    # training mode, autograd recording: the training forward (same output) with the FP8 backward
+    o_t, aux_t = m(x)
+    assert torch.equal(o, o_t.detach()) and aux_t is not None
+    (o_t.float().square().mean() + aux_t).backward()
+    for p in (m.router.weight, m.c_fc.weight, m.c_proj.weight):
+        assert p.grad is not None and torch.isfinite(p.grad).all() and p.grad.abs().sum() > 0
+    m.zero_grad()
     m.eval()
     o2, aux2 = m(x)
     assert aux2 is not None and torch.isfinite(aux2)

@@ -30,15 +30,23 @@ def test_moe_forward_exports_as_one_graph():
     assert tuple(o_meta.shape) == (T, H) and o_meta.dtype == torch.bfloat16
 
 
-def test_training_mode_is_refused():
+def test_training_without_a_backward_is_refused():
+    """Gradient requests the FP8 backward does not cover raise before any device work: the
+    concatenated w1 layout, the fused router, and the general-routing layer."""
     import sonicmoe
-    from sonicmoe.functional import moe_TC_softmax_topk_layer
+    from sonicmoe.functional import moe_TC_softmax_topk_layer, moe_general_routing_inputs
 
     T, H, I, E, K = 16, 256, 128, 4, 2
     m = sonicmoe.MoE(E, K, H, I, sonicmoe.ActivationType.SWIGLU, False, 0.02)
     x = torch.randn(T, H)
-    with pytest.raises(NotImplementedError, match="inference forward only"):
-        m(x)  # training mode with autograd recording
-    with pytest.raises(NotImplementedError, match="inference forward only"):
-        moe_TC_softmax_topk_layer(x, m.router.weight, m.c_fc.weight.permute(1, 2, 0), None,
-                                  m.c_proj.weight.permute(1, 2, 0), None, K, None, is_inference_mode_enabled=False)
+    w1, w2 = m.c_fc.weight.permute(1, 2, 0), m.c_proj.weight.permute(1, 2, 0)
+    with pytest.raises(NotImplementedError, match="interleaved layout"):
+        moe_TC_softmax_topk_layer(x, m.router.weight, w1, None, w2, None, K, None, is_inference_mode_enabled=False,
+                                  concat_layout=True)
+    with pytest.raises(NotImplementedError, match="interleaved layout"):
+        moe_TC_softmax_topk_layer(x, m.router.weight, w1, None, w2, None, K, None, is_inference_mode_enabled=False,
+                                  fused_router=True)
+    tok = torch.arange(T, dtype=torch.int32)
+    with pytest.raises(NotImplementedError, match="no backward for moe_general_routing_inputs"):
+        moe_general_routing_inputs(x, torch.ones(T), tok, tok % E, w1, None, w2, None, E, None,
+                                   is_inference_mode_enabled=False)
