@@ -257,12 +257,12 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
  * _UpProjection.backward / _DownProjection.backward, functional/__init__.py:303-362, 422-479), in
  * FP8 with the forward's 1x128 / 128x128 UE8M0 scaling.  For dO [T, H] the stages are:
  *   1. sm_quant_pack of dO (exactly as x in the forward) -> dO rows in the padded layout;
- *   2. sm_moe_dact: dA' = dO W2 per entry (B = W2^T from sm_weight_prep_t of c_proj.weight), then
+ *   2. sm_moe_dact: dA' = dO W2 per entry (B = W2^T, sm_weight_prep_t of the prepared c_proj.weight), then
  *      from the stored pre-activation h (sm_moe_up_preact): dS [T*K] (accumulated: zero it first),
  *      a' = s * a and dH = SwiGLU backward of s * dA' -- dH as e4m3 + atoms for stage 3 and as bf16,
  *      a' as bf16, both in padded rows (gemm_dact of functional/backward.py:211-278);
  *   3. sm_moe_down_combine with topk_scores = NULL (unit weights) and B = W1^T (sm_weight_prep_t of
- *      c_fc.weight, interleaved layout): dX [T, H] = sum over the token's entries of dH W1
+ *      the prepared c_fc.weight, interleaved layout): dX [T, H] = sum over the token's entries of dH W1
  *      (the reference's gemm + token_broadcast_backward, :173-206 and :281-305);
  *   4. sm_tq_pack of dO (gathered) / x (gathered) / a' / dH (padded) -> transposed e4m3 operands
  *      with one scale per 128 rows, then sm_moe_wgrad: dW2[e] = dO_e^T a'_e [H, I] and
@@ -270,9 +270,11 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
  *   5. sm_router_bwd: dlogits [T, E] fp32 from dS (backward.py:308-430).
  * Interleaved w1 layout only (concat_layout raises SM_ENOTSUP at the Python layer).
  */
-/* W^T for a backward GEMM: w [E, N, K] bf16 -> wq_t [E, K, N] e4m3 with the 128x128 block scales of
- * w, atoms [E][K/128][ceil(N/512)][512] (sm_weight_sf_bytes(E, K, N) bytes). */
-int sm_weight_prep_t(const void* w, int E, int N, int K, uint8_t* wq_t, uint8_t* sf_atoms, void* stream);
+/* W^T for a backward GEMM from the forward's prepared weight (sm_weight_prep, interleaved):
+ * wq [E, N, K] e4m3 + atoms -> wq_t [E, K, N] e4m3, the same values and 128x128 block scales read
+ * transposed, atoms_t [E][K/128][ceil(N/512)][512] (sm_weight_sf_bytes(E, K, N) bytes). */
+int sm_weight_prep_t(const uint8_t* wq, const uint8_t* sf_atoms, int E, int N, int K, uint8_t* wq_t,
+                     uint8_t* sf_atoms_t, void* stream);
 /* Stage 2 above.  doq/dosf: dO packed like sm_quant_pack's xq/xsf; w2t: [E, I, H]; preact [T*K, 2I]
  * bf16 (expert-sorted rows); dh_q [max_blocks*128, 2I] + dh_sf atoms, dh_bf16 [max_blocks*128, 2I],
  * a_prime [max_blocks*128, I] (padded rows); dscores [T*K] fp32, flat entries, accumulated.

@@ -1,9 +1,9 @@
 // Backward of the FP8 MoE layer: the non-GEMM kernels.  The GEMMs are moe_gemm_kernel's
 // activation-gradient and weight-gradient kinds (csrc/gemm.cu) and its down kind with unit weights.
 //
-// weight_prep_t_kernel -- 128x128 block quantisation written transposed: w [E, N, K] -> wt [E, K, N]
-//                         e4m3 with the block's scale (the same block, read the other way), so that
-//                         a backward GEMM takes W^T as its K-major B operand.
+// weight_t_kernel      -- the forward's prepared e4m3 weight [E, N, K] transposed to [E, K, N] with
+//                         its 128x128 block scales moved along (the same blocks, read the other way),
+//                         so that a backward GEMM takes W^T as its K-major B operand.
 // tq_pack_kernel       -- the weight gradients' operands: rows of the padded expert layout (gathered
 //                         token rows, or rows of a padded array) transposed to [C, rows] and
 //                         quantised with one UE8M0 scale per 128 consecutive rows (the K groups of a
@@ -18,62 +18,46 @@ namespace smb {
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
 
-// One CTA of 256 threads per 128x128 block: blockIdx = (k block, n block, expert).
+// One CTA of 256 threads per 128x128 block of the prepared weight: blockIdx = (k block, n block,
+// expert).  The e4m3 bytes are transposed through shared memory (rows 144 bytes apart: the 16-byte
+// stores of a warp's rows fall into distinct bank groups), and the block's scale byte moves from
+// atom (n block, k block) of wq to atom (k block, n block) of wq_t -- the same 128x128 block, so the
+// values are those of the forward's weight, read transposed.
 __global__ void __launch_bounds__(256)
-    weight_prep_t_kernel(const __nv_bfloat16* __restrict__ w, int N, int Kd, uint8_t* __restrict__ wq,
-                         uint8_t* __restrict__ wsf) {
-  __shared__ uint16_t tile[kBlockM][kBlockK + 2];
-  __shared__ float s_red[8];
+    weight_t_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wsf, int N, int Kd,
+                    uint8_t* __restrict__ wqt, uint8_t* __restrict__ wsft) {
+  constexpr int kStride = 144;
+  __shared__ __align__(16) uint8_t tile[kBlockM * kStride];
   const int kb = blockIdx.x, nb = blockIdx.y, e = blockIdx.z;
   const int tid = threadIdx.x;
   const int row = tid >> 1, half = tid & 1;
-  const uint16_t* src = reinterpret_cast<const uint16_t*>(w) +
-                        (static_cast<size_t>(e) * N + static_cast<size_t>(nb) * kBlockM + row) * Kd + kb * kBlockK +
-                        half * 64;
-  float am = 0.0f;
+  const uint4* src = reinterpret_cast<const uint4*>(
+      wq + (static_cast<size_t>(e) * N + static_cast<size_t>(nb) * kBlockM + row) * Kd + kb * kBlockK + half * 64);
+  uint4* srow = reinterpret_cast<uint4*>(tile + row * kStride + half * 64);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint4 raw = reinterpret_cast<const uint4*>(src)[i];
-    const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      tile[row][half * 64 + 8 * i + 2 * j] = static_cast<uint16_t>(wd[j] & 0xFFFFu);
-      tile[row][half * 64 + 8 * i + 2 * j + 1] = static_cast<uint16_t>(wd[j] >> 16);
-      am = fmaxf(am, fmaxf(fabsf(__uint_as_float(wd[j] << 16)), fabsf(__uint_as_float(wd[j] & 0xFFFF0000u))));
-    }
-  }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-  if ((tid & 31) == 0) s_red[tid >> 5] = am;
+  for (int i = 0; i < 4; ++i) srow[i] = src[i];
   __syncthreads();
-  am = s_red[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) am = fmaxf(am, s_red[i]);
-  const int e8 = scale_exp_of_amax(am);
-  const float inv = exp2_neg(e8);
-  // transposed: output row k (of this block) = column k of the input block, 64 n values per thread
+  // output row k = column k of the block; this thread gathers 64 of its 128 n values, 4 at a time
   const int k = tid >> 1;
-  uint8_t* dst = wq + (static_cast<size_t>(e) * Kd + static_cast<size_t>(kb) * kBlockK + k) * N +
-                 static_cast<size_t>(nb) * kBlockM + half * 64;
+  uint32_t w[16];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t wd[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = half * 64 + 16 * i + 4 * j;
-      wd[j] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(bf16_bits_to_f32(tile[n][k]), inv),
-                                               __fmul_rn(bf16_bits_to_f32(tile[n + 1][k]), inv))) |
-              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(bf16_bits_to_f32(tile[n + 2][k]), inv),
-                                                __fmul_rn(bf16_bits_to_f32(tile[n + 3][k]), inv)))
-               << 16);
-    }
-    reinterpret_cast<uint4*>(dst)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  for (int j = 0; j < 16; ++j) {
+    const int n = half * 64 + 4 * j;
+    w[j] = static_cast<uint32_t>(tile[n * kStride + k]) | (static_cast<uint32_t>(tile[(n + 1) * kStride + k]) << 8) |
+           (static_cast<uint32_t>(tile[(n + 2) * kStride + k]) << 16) |
+           (static_cast<uint32_t>(tile[(n + 3) * kStride + k]) << 24);
   }
+  uint4* dst = reinterpret_cast<uint4*>(wqt + (static_cast<size_t>(e) * Kd + static_cast<size_t>(kb) * kBlockK + k) * N +
+                                        static_cast<size_t>(nb) * kBlockM + half * 64);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
   if (tid < 128) {
-    // atoms of the transposed weight: [E][Kd/128 row blocks][ceil(N/512)][512], K block nb
+    // the block's scale: byte (kb % 4) of any row slot of atom (e, nb, kb / 4) of wq
+    const int KG = (Kd / kBlockK + 3) / 4;
+    const uint8_t sc = wsf[((static_cast<size_t>(e) * (N / kBlockM) + nb) * KG + kb / 4) * kSfAtomBytes + (kb % 4)];
     const int KGn = (N / kBlockK + 3) / 4;
     const size_t atom = ((static_cast<size_t>(e) * (Kd / kBlockM) + kb) * KGn + nb / 4) * kSfAtomBytes;
-    wsf[atom + 16 * (tid >> 2) + 4 * (tid & 3) + (nb % 4)] = static_cast<uint8_t>(e8 + 127);
+    wsft[atom + 16 * (tid >> 2) + 4 * (tid & 3) + (nb % 4)] = sc;
   }
 }
 
@@ -88,7 +72,9 @@ __global__ void __launch_bounds__(256)
                    const int32_t* __restrict__ freq, const int32_t* __restrict__ x_gather,
                    const int32_t* __restrict__ n_blocks, long long rows_pad, uint8_t* __restrict__ outq,
                    uint8_t* __restrict__ outsf) {
-  __shared__ uint16_t tile[kBlockM][kBlockK + 2];
+  // rows 272 bytes apart: 16-byte aligned for the vector stores, four banks apart from row to row
+  constexpr int kStride = kBlockK + 8;
+  __shared__ __align__(16) uint16_t tile[kBlockM][kStride];
   const int mb = blockIdx.x, cb = blockIdx.y;
   if (mb >= *n_blocks) return;  // blocks past the layout are never read
   const int tid = threadIdx.x;
@@ -100,22 +86,20 @@ __global__ void __launch_bounds__(256)
   const long long srow = src_padded ? static_cast<long long>(p) : (valid ? x_gather[off[e] + rel] : 0);
   const uint4* s4 =
       reinterpret_cast<const uint4*>(src + srow * static_cast<long long>(C) + static_cast<long long>(cb) * kBlockK + half * 64);
+  uint4* t4 = reinterpret_cast<uint4*>(&tile[row][half * 64]);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint4 raw = valid ? s4[i] : make_uint4(0, 0, 0, 0);
-    const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      tile[row][half * 64 + 8 * i + 2 * j] = static_cast<uint16_t>(wd[j] & 0xFFFFu);
-      tile[row][half * 64 + 8 * i + 2 * j + 1] = static_cast<uint16_t>(wd[j] >> 16);
-    }
-  }
+  for (int i = 0; i < 8; ++i) t4[i] = valid ? s4[i] : make_uint4(0, 0, 0, 0);
   __syncthreads();
-  // output row c = source column cb*128 + c; this thread quantises its 64 of the block's 128 rows
+  // output row c = source column cb*128 + c; this thread quantises its 64 of the block's 128 rows,
+  // held in registers between the amax and the conversion
   const int c = tid >> 1;
+  float v[64];
   float am = 0.0f;
-#pragma unroll 8
-  for (int r = 0; r < 64; ++r) am = fmaxf(am, fabsf(bf16_bits_to_f32(tile[half * 64 + r][c])));
+#pragma unroll
+  for (int r = 0; r < 64; ++r) {
+    v[r] = bf16_bits_to_f32(tile[half * 64 + r][c]);
+    am = fmaxf(am, fabsf(v[r]));
+  }
   am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
   const int e8 = scale_exp_of_amax(am);
   const float inv = exp2_neg(e8);
@@ -126,12 +110,9 @@ __global__ void __launch_bounds__(256)
     uint32_t wd[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int r = half * 64 + 16 * i + 4 * j;
-      wd[j] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(bf16_bits_to_f32(tile[r][c]), inv),
-                                               __fmul_rn(bf16_bits_to_f32(tile[r + 1][c]), inv))) |
-              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(bf16_bits_to_f32(tile[r + 2][c]), inv),
-                                                __fmul_rn(bf16_bits_to_f32(tile[r + 3][c]), inv)))
-               << 16);
+      const float* q = v + 16 * i + 4 * j;
+      wd[j] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[0], inv), __fmul_rn(q[1], inv))) |
+              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[2], inv), __fmul_rn(q[3], inv))) << 16);
     }
     reinterpret_cast<uint4*>(dst)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
@@ -193,10 +174,11 @@ __global__ void router_bwd_kernel(const __nv_bfloat16* __restrict__ logits, cons
   if (lane < K) out[ix] = p_sel * (dp_sel - dot);
 }
 
-cudaError_t launch_weight_prep_t(const void* w, int E, int N, int Kd, uint8_t* wq, uint8_t* wsf, cudaStream_t st) {
+cudaError_t launch_weight_t(const uint8_t* wq, const uint8_t* wsf, int E, int N, int Kd, uint8_t* wqt, uint8_t* wsft,
+                            cudaStream_t st) {
   if (E == 0) return cudaSuccess;
   dim3 grid(Kd / kBlockK, N / kBlockM, E);
-  weight_prep_t_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), N, Kd, wq, wsf);
+  weight_t_kernel<<<grid, 256, 0, st>>>(wq, wsf, N, Kd, wqt, wsft);
   return cudaGetLastError();
 }
 

@@ -385,12 +385,13 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
 
 // ---------------------------------------------------------------------------------------------
 // backward
-int sm_weight_prep_t(const void* w, int E, int N, int K, uint8_t* wq_t, uint8_t* sf_atoms, void* stream) {
+int sm_weight_prep_t(const uint8_t* wq, const uint8_t* sf_atoms, int E, int N, int K, uint8_t* wq_t,
+                     uint8_t* sf_atoms_t, void* stream) {
   if (E < 1 || N <= 0 || K <= 0 || N % 128 || K % 128)
     return fail(SM_EINVAL, "need E >= 1 and N, K multiples of 128 (E=%d N=%d K=%d)", E, N, K);
-  if (!w || !wq_t || !sf_atoms) return fail(SM_EINVAL, "null pointer");
-  if (!aligned16(w) || !aligned16(wq_t)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
-  return cuda_status(launch_weight_prep_t(w, E, N, K, wq_t, sf_atoms, static_cast<cudaStream_t>(stream)),
+  if (!wq || !sf_atoms || !wq_t || !sf_atoms_t) return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(wq) || !aligned16(wq_t)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  return cuda_status(launch_weight_t(wq, sf_atoms, E, N, K, wq_t, sf_atoms_t, static_cast<cudaStream_t>(stream)),
                      "weight_prep_t");
 }
 

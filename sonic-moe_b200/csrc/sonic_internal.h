@@ -65,7 +65,8 @@ cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* expert
 cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_glu, uint8_t* wq, uint8_t* wsf,
                                cudaStream_t st);
 // backward (csrc/backward.cu)
-cudaError_t launch_weight_prep_t(const void* w, int E, int N, int Kd, uint8_t* wq, uint8_t* wsf, cudaStream_t st);
+cudaError_t launch_weight_t(const uint8_t* wq, const uint8_t* wsf, int E, int N, int Kd, uint8_t* wqt, uint8_t* wsft,
+                            cudaStream_t st);
 cudaError_t launch_tq_pack(const void* src, int C, int src_padded, const int32_t* blk_expert, const int32_t* off_pad,
                            const int32_t* off, const int32_t* freq, const int32_t* x_gather, const int32_t* n_blocks,
                            int max_blocks, uint8_t* outq, uint8_t* outsf, cudaStream_t st);

@@ -96,7 +96,7 @@ SIGNATURES = {
     "sm_quant_pack": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up_preact": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
-    "sm_weight_prep_t": (_I, [_P, _I, _I, _I, _P, _P, _P]),
+    "sm_weight_prep_t": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "sm_moe_dact": (
         _I,
         [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],

@@ -174,10 +174,11 @@ class _FP8MoEFunction(torch.autograd.Function):
          n_blocks) = ctx.saved_tensors
         plan = ops.RoutePlan(freq, off, x_gather, s_scatter, s_rev, off_pad, blk_expert, n_blocks, ctx.max_blocks)
         sot, norm = ctx.modes
-        w1e = _as_expert_major(w1.detach()).contiguous()
-        w2e = _as_expert_major(w2.detach()).contiguous()
-        dx, dlogits, dw1, dw2, _ = ops.moe_backward(dout.to(torch.bfloat16), x, router_logits, w1e, w2e, scores, idx,
-                                                    plan, h, sot, norm, err)
+        # the e4m3 weights the forward ran with (cached per weight version), read transposed
+        w1q = prepare_fp8_weights(w1, concat_glu=False)
+        w2q = prepare_fp8_weights(w2, concat_glu=False)
+        dx, dlogits, dw1, dw2, _ = ops.moe_backward(dout.to(torch.bfloat16).contiguous(), x, router_logits, w1q, w2q,
+                                                    scores, idx, plan, h, sot, norm, err)
         code = int(err.item())
         if code:
             raise RuntimeError(f"FP8 MoE backward: device error {code}")

@@ -401,16 +401,15 @@ def moe_general_forward(
 # backward stages (FP8, interleaved SwiGLU); see include/sonic_b200.h for the data layouts
 
 
-def weight_prep_t(w: torch.Tensor) -> Fp8ExpertWeights:
-    """W^T as a backward GEMM's K-major operand: w [E, N, K] bf16 -> e4m3 [E, K, N] with the 128x128
-    block scales of w (the same blocks, read transposed)."""
-    if w.dtype != torch.bfloat16:
-        w = w.to(torch.bfloat16)
-    w = w.contiguous()
+def weight_prep_t(w: Fp8ExpertWeights) -> Fp8ExpertWeights:
+    """W^T as a backward GEMM's K-major operand, from the forward's prepared weight: e4m3 [E, N, K] ->
+    [E, K, N], the same values and 128x128 block scales read transposed."""
+    if w.concat_glu:
+        raise NotImplementedError("the FP8 backward takes the interleaved w1 layout")
     E, N, K = w.shape
-    q = torch.empty(E, K, N, dtype=torch.uint8, device=w.device)
-    sf = torch.zeros(E, K // _BLOCK_M, -(-(N // 128) // 4), 512, dtype=torch.uint8, device=w.device)
-    nat.call("sm_weight_prep_t", _ptr(w), E, N, K, _ptr(q), _ptr(sf), _stream())
+    q = torch.empty(E, K, N, dtype=torch.uint8, device=w.q.device)
+    sf = torch.zeros(E, K // _BLOCK_M, -(-(N // 128) // 4), 512, dtype=torch.uint8, device=w.q.device)
+    nat.call("sm_weight_prep_t", _ptr(w.q), _ptr(w.sf), E, N, K, _ptr(q), _ptr(sf), _stream())
     return Fp8ExpertWeights(q, sf, False)
 
 
@@ -471,12 +470,12 @@ def router_bwd(router_logits: torch.Tensor, scores: torch.Tensor, idx: torch.Ten
     return dl
 
 
-def moe_backward(dout: torch.Tensor, x: torch.Tensor, router_logits: torch.Tensor, w1: torch.Tensor,
-                 w2: torch.Tensor, scores: torch.Tensor, idx: torch.Tensor, plan: RoutePlan, preact: torch.Tensor,
+def moe_backward(dout: torch.Tensor, x: torch.Tensor, router_logits: torch.Tensor, w1: Fp8ExpertWeights,
+                 w2: Fp8ExpertWeights, scores: torch.Tensor, idx: torch.Tensor, plan: RoutePlan, preact: torch.Tensor,
                  softmax_over_topk: bool, norm_topk_probs: bool, err):
     """The layer backward from dO [T, H]: (dx [T, H] bf16, dlogits [T, E] fp32, dw1 [E, 2I, H] bf16,
-    dw2 [E, H, I] bf16, dscores [T, K] fp32).  w1 / w2: the bf16 expert weights [E, 2I, H] / [E, H, I]
-    (interleaved gate/up rows)."""
+    dw2 [E, H, I] bf16, dscores [T, K] fp32).  w1 / w2: the forward's prepared e4m3 expert weights
+    ([E, 2I, H] interleaved gate/up rows / [E, H, I]); the backward GEMMs use them transposed."""
     T, H = dout.shape
     E = w1.shape[0]
     K = idx.shape[1]

@@ -52,7 +52,8 @@ def test_moe_backward_stages_vs_oracle(ops, T, H, I, E, K, sot, norm):
     logits, scores, idx, plan, h, err = _forward_state(ops, xc, rwc, w1c, w2c, K, sot, norm)
     g = torch.Generator().manual_seed(T + 1)
     dout = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
-    dx, dl, dw1, dw2, ds = ops.moe_backward(dout.cuda(), xc, logits, w1c, w2c, scores, idx, plan, h, sot, norm, err)
+    dx, dl, dw1, dw2, ds = ops.moe_backward(dout.cuda(), xc, logits, ops.weight_prep(w1c), ops.weight_prep(w2c),
+                                            scores, idx, plan, h, sot, norm, err)
     torch.cuda.synchronize()
     assert err.item() == 0, f"kernel error word {err.item()}"
     s_np, i_np = scores.cpu().numpy(), idx.cpu().numpy()
@@ -80,16 +81,23 @@ def test_router_bwd_matches_oracle(ops):
 
 
 def test_weight_prep_t_is_the_transpose(ops):
+    """The transposed weight holds the forward's e4m3 values read transposed, and its scale atoms the
+    same 128x128 block scales: both dequantise to the transposed fake-quantised weight."""
     from oracle import quant as oq
 
     g = torch.Generator().manual_seed(4)
     w = (torch.randn(3, 256, 384, generator=g) * 0.05).to(torch.bfloat16)
-    wt = ops.weight_prep_t(w.cuda())
     w_f = ops.weight_prep(w.cuda())
-    # same e4m3 values, read transposed, and the transposed block scales
+    wt = ops.weight_prep_t(w_f)
     assert torch.equal(wt.q.cpu(), w_f.q.cpu().transpose(1, 2))
     q, sf = oq.quant_128x128(w.float().numpy())
     np.testing.assert_array_equal(wt.q.cpu().numpy(), q.transpose(0, 2, 1))
+    # scale of block (k, n) of the transpose = scale of block (n, k): byte (n % 4) of atom (e, k, n / 4)
+    atoms = wt.sf.cpu().numpy()  # [E, K/128, ceil(N/512), 512]
+    for e in range(3):
+        for kb in range(384 // 128):
+            for nb in range(256 // 128):
+                assert atoms[e, kb, nb // 4, nb % 4] == sf[e, nb, kb]
 
 
 @pytest.mark.parametrize("T,H,I,E,K,sot,norm", CASES[:2])
