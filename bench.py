@@ -306,6 +306,58 @@ def run_ours(args, rank, world, local_rank):
     return res
 
 
+def run_train(args):
+    """One training step of the layer through the public API on one GPU: the training forward of
+    ``moe_TC_softmax_topk_layer`` (is_inference_mode_enabled=False, weights requiring grad; the up GEMM
+    also stores h) and ``backward`` of a fixed output gradient through the FP8 backward.  The
+    expert weights are bumped in place before every step, as an optimiser step would, so their
+    e4m3 preparation is part of every step.  Eager steps (autograd), CUDA events around the loop.
+    FLOPs per step: 18*T*K*H*I (forward 6, backward 12: dA', dX, dW1, dW2)."""
+    import torch
+
+    from sonicmoe.functional import moe_TC_softmax_topk_layer
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
+    g = torch.Generator(device=dev).manual_seed(1111)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16).requires_grad_()
+    rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16).requires_grad_()
+    w1 = (torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16).requires_grad_()
+    w2 = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16).requires_grad_()
+    dout = (torch.randn(T, H, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+
+    def step():
+        # a new weight version, as after an optimiser step (no data pass: only the version counter)
+        torch.autograd.graph.increment_version(w1)
+        torch.autograd.graph.increment_version(w2)
+        o, _, _ = moe_TC_softmax_topk_layer(x, rw, w1.permute(1, 2, 0), None, w2.permute(1, 2, 0), None, K, None,
+                                            is_inference_mode_enabled=False)
+        o.backward(dout)
+        x.grad = rw.grad = w1.grad = w2.grad = None
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if args.profile:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        return
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"workload": "config 2 training step (forward + FP8 backward), one GPU", "T": T, "H": H, "I": I,
+                      "E": E, "K": K, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+                      "tflops": 18.0 * T * K * H * I / (ms / 1e3) / 1e12, "steps": args.steps,
+                      "clocks": clk.summary()}))
+
+
 def run_profile(args, local_rank):
     """Eager forwards only, with the bf16 expert weights freed after preparation (smaller footprint)."""
     import torch
@@ -572,6 +624,8 @@ def main():
     ap.add_argument("--workload", choices=["c2"] + sorted(SIDE_WORKLOADS), default="c2",
                     help="c2 = the headline configuration (default, the contract line); the others time the "
                          "benchmark's remaining configurations (c4 also expert parallel with --gpus N > 1)")
+    ap.add_argument("--train", action="store_true",
+                    help="time one GPU's training step (forward + FP8 backward) of config 2 instead of the forward")
     ap.add_argument("--profile", action="store_true",
                     help="only run warmup + steps eager forwards (no graph, baselines or extra timing), "
                          "for ncu captures; prints nothing")
@@ -612,6 +666,10 @@ def main():
 
     import torch
 
+    if args.train:
+        if rank == 0:
+            run_train(args)
+        return
     if args.profile:
         run_profile(args, local_rank)
         return
