@@ -268,22 +268,25 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
  *      with one scale per 128 rows, then sm_moe_wgrad: dW2[e] = dO_e^T a'_e [H, I] and
  *      dW1[e] = dH_e^T x_e [2I, H] (the reference's varlen-K gemms, :339-348, :465-473);
  *   5. sm_router_bwd: dlogits [T, E] fp32 from dS (backward.py:308-430).
- * Interleaved w1 layout only (concat_layout raises SM_ENOTSUP at the Python layer).
+ * Both w1 layouts (interleaved, or concatenated with concat_layout = 1 in stage 2).
  */
-/* W^T for a backward GEMM from the forward's prepared weight (sm_weight_prep, interleaved):
+/* W^T for a backward GEMM from the forward's prepared weight (sm_weight_prep; for a concatenated
+ * w1 the K order of the result is the prepared weight's re-blocked row order):
  * wq [E, N, K] e4m3 + atoms -> wq_t [E, K, N] e4m3, the same values and 128x128 block scales read
  * transposed, atoms_t [E][K/128][ceil(N/512)][512] (sm_weight_sf_bytes(E, K, N) bytes). */
 int sm_weight_prep_t(const uint8_t* wq, const uint8_t* sf_atoms, int E, int N, int K, uint8_t* wq_t,
                      uint8_t* sf_atoms_t, void* stream);
 /* Stage 2 above.  doq/dosf: dO packed like sm_quant_pack's xq/xsf; w2t: [E, I, H]; preact [T*K, 2I]
- * bf16 (expert-sorted rows); dh_q [max_blocks*128, 2I] + dh_sf atoms, dh_bf16 [max_blocks*128, 2I],
- * a_prime [max_blocks*128, I] (padded rows); dscores [T*K] fp32, flat entries, accumulated.
- * I % 256 == 0. */
+ * bf16 (expert-sorted rows, the caller's w1 column order); dh_q [max_blocks*128, 2I] + dh_sf atoms,
+ * dh_bf16 [max_blocks*128, 2I], a_prime [max_blocks*128, I] (padded rows); dscores [T*K] fp32, flat
+ * entries, accumulated.  concat_layout = 1: h and dh_bf16 in [gate | up] order and dh_q in the
+ * re-blocked order of the prepared concatenated w1 (gate block j, up block j, ...), matching
+ * sm_weight_prep_t of that weight.  I % 256 == 0. */
 int sm_moe_dact(const uint8_t* doq, const uint8_t* dosf, const uint8_t* w2t_q, const uint8_t* w2t_sf, int H, int I,
                 int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks, const int32_t* off_pad,
                 const int32_t* expert_frequency_offset, const int32_t* expert_frequency, const int32_t* s_scatter_idx,
-                const float* topk_scores, const void* preact, uint8_t* dh_q, uint8_t* dh_sf, void* dh_bf16,
-                void* a_prime, float* dscores, int32_t* err, void* stream);
+                const float* topk_scores, const void* preact, int concat_layout, uint8_t* dh_q, uint8_t* dh_sf,
+                void* dh_bf16, void* a_prime, float* dscores, int32_t* err, void* stream);
 /* Transposed, column-quantised operand of a weight-gradient GEMM: out [C, max_blocks*128] e4m3,
  * out[c][p] = q(src[row(p)][c]) with one UE8M0 scale per (c, 128-row block), atoms
  * [C/128][ceil(max_blocks/4)][512]; row(p) = the token of padded row p (src_padded = 0: src is

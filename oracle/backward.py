@@ -55,11 +55,14 @@ def router_backward(logits, scores, idx, ds, softmax_over_topk=True, norm_topk_p
     return p * (dp - dot)
 
 
-def fp8_backward(x, dout, w1, w2, scores, idx, h, softmax_over_topk=True, norm_topk_probs=False, logits=None):
+def fp8_backward(x, dout, w1, w2, scores, idx, h, softmax_over_topk=True, norm_topk_probs=False, logits=None,
+                 concat_layout=False):
     """(dx [T, H], dw1 [E, 2I, H], dw2 [E, H, I], ds [T, K], dlogits [T, E] or None), float64.
 
     x, dout [T, H]; w1 [E, 2I, H], w2 [E, H, I] (bf16 values as float); scores / idx [T, K] the
-    forward's routing; h [T*K, 2I] the stored pre-activation in expert-sorted entry order."""
+    forward's routing; h [T*K, 2I] the stored pre-activation in expert-sorted entry order.  With
+    concat_layout the gate / up halves of w1, h and dH are [gate | up] instead of interleaved; dH's 1x128
+    groups along 2I are then gate-only and up-only groups, as in the engine."""
     x = np.asarray(x, dtype=np.float32)
     dout = np.asarray(dout, dtype=np.float32)
     idx = np.asarray(idx)
@@ -78,7 +81,7 @@ def fp8_backward(x, dout, w1, w2, scores, idx, h, softmax_over_topk=True, norm_t
     s = np.asarray(scores, dtype=np.float64).reshape(-1)
     # h rows are in expert-sorted order: entry f sits at row s_rev[f]
     hf = np.asarray(h, dtype=np.float64)[s_rev]
-    g, u = hf[:, 0::2], hf[:, 1::2]
+    g, u = (hf[:, :I], hf[:, I:]) if concat_layout else (hf[:, 0::2], hf[:, 1::2])
     sig = 1.0 / (1.0 + np.exp(-g))
     a = g * sig * u
     dod = _q1x128(dout)
@@ -88,9 +91,12 @@ def fp8_backward(x, dout, w1, w2, scores, idx, h, softmax_over_topk=True, norm_t
         dap[r] = dod[tok[r]] @ w2d[ex]
     ds = (dap * a).sum(1)
     da = s[:, None] * dap
+    dg, du = da * u * sig * (1.0 + g * (1.0 - sig)), da * g * sig
     dh = np.empty((T * K, 2 * I))
-    dh[:, 0::2] = da * u * sig * (1.0 + g * (1.0 - sig))
-    dh[:, 1::2] = da * g * sig
+    if concat_layout:
+        dh[:, :I], dh[:, I:] = dg, du
+    else:
+        dh[:, 0::2], dh[:, 1::2] = dg, du
     a_prime = s[:, None] * a
     dhq = _q1x128(dh)
     dx = np.zeros((T, H))

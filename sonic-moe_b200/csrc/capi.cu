@@ -398,8 +398,8 @@ int sm_weight_prep_t(const uint8_t* wq, const uint8_t* sf_atoms, int E, int N, i
 int sm_moe_dact(const uint8_t* doq, const uint8_t* dosf, const uint8_t* w2t_q, const uint8_t* w2t_sf, int H, int I,
                 int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks, const int32_t* off_pad,
                 const int32_t* expert_frequency_offset, const int32_t* expert_frequency, const int32_t* s_scatter_idx,
-                const float* topk_scores, const void* preact, uint8_t* dh_q, uint8_t* dh_sf, void* dh_bf16,
-                void* a_prime, float* dscores, int32_t* err, void* stream) {
+                const float* topk_scores, const void* preact, int concat_layout, uint8_t* dh_q, uint8_t* dh_sf,
+                void* dh_bf16, void* a_prime, float* dscores, int32_t* err, void* stream) {
   if (H <= 0 || H % 128 || I <= 0 || I % 256 || E < 1 || max_blocks < 0)
     return fail(SM_ENOTSUP, "bad shape H=%d I=%d E=%d (H %% 128 == 0, I %% 256 == 0)", H, I, E);
   if (!err || !preact || !dh_q || !dh_sf || !dh_bf16 || !a_prime || !dscores || !topk_scores || !s_scatter_idx ||
@@ -407,8 +407,8 @@ int sm_moe_dact(const uint8_t* doq, const uint8_t* dosf, const uint8_t* w2t_q, c
     return fail(SM_EINVAL, "null pointer");
   if (!aligned16(preact) || !aligned16(dh_q) || !aligned16(dh_bf16) || !aligned16(a_prime))
     return fail(SM_EINVAL, "pointers must be 16-byte aligned");
-  GemmArgs g = up_args(doq, dosf, w2t_q, w2t_sf, H, I / 2, E, 0, max_blocks, blk_expert, n_blocks, off_pad,
-                       expert_frequency, dh_q, dh_sf, err);
+  GemmArgs g = up_args(doq, dosf, w2t_q, w2t_sf, H, I / 2, E, concat_layout ? 1 : 0, max_blocks, blk_expert,
+                       n_blocks, off_pad, expert_frequency, dh_q, dh_sf, err);
   g.N = I;  // output columns of this GEMM: the intermediate
   g.off = expert_frequency_offset;
   g.s_scatter = s_scatter_idx;

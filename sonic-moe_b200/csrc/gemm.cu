@@ -76,7 +76,8 @@ struct GemmSmem {
   static constexpr int kOffBar = kOffStage + kStageBytes;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAmax = (kOffTmemHolder + 4 + 15) / 16 * 16;
-  static constexpr int kAmaxFloats = kUp ? 2 * 4 * kBlockM : 0;
+  // up: [tile parity][column warp][row] row maxima; activation gradient: [parity][gate/up][column warp][row]
+  static constexpr int kAmaxFloats = kUp ? 2 * 4 * kBlockM : (kKind == kKindDact ? 2 * 2 * 4 * kBlockM : 0);
   static constexpr int kBytes = kOffAmax + kAmaxFloats * 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
   static_assert(kAlloc <= 232448, "shared memory budget");
@@ -220,6 +221,106 @@ __device__ __forceinline__ void dact_tile(const GemmArgs& g, const uint32_t (&v)
       static_cast<uint8_t>(e8 + 127);
 }
 
+// Concatenated w1 ([gate | up] rows): h holds g at column i and u at I + i.  dH goes out as bf16 in
+// that order (the dW1 operand, so dW1 keeps the caller's layout) and as e4m3 in the forward
+// weight's re-blocked order -- column 256 j + c holds gate 128 j + c for c < 128, up 128 j + c - 128
+// -- the K order of W1^T transposed from the prepared (re-blocked) W1.  The thread's 64 gate values
+// are half of one 1x128 group and its 64 up values half of the next; the other halves belong to
+// column warp cc ^ 1 of the same rows, so the group maxima are exchanged through shared memory
+// (every epilogue warp arrives once per tile; rows without an entry contribute zeros).
+__device__ __forceinline__ bool dact_tile_concat(const GemmArgs& g, const uint32_t (&v)[64], const RowMeta& m, int cc,
+                                                 int lane, int tcount, float* s_amax, uint64_t* amax_bar) {
+  const int I = g.N;
+  const int i0 = m.nt * kBN + 64 * cc;
+  const int r = m.p % kBlockM;
+  const bool valid = m.valid != 0;
+  const float sc = m.sc;
+  const size_t p = static_cast<size_t>(m.p);
+  const __nv_bfloat16* hrow = g.h_in + static_cast<size_t>(valid ? m.tok : 0) * (2 * I);
+  const uint4* hg = reinterpret_cast<const uint4*>(hrow + i0);
+  const uint4* hu = reinterpret_cast<const uint4*>(hrow + I + i0);
+  float amg = 0.0f, amu = 0.0f;
+  if (valid) {
+    uint4* adst = reinterpret_cast<uint4*>(g.a_prime + p * I + i0);
+    uint4* gdst = reinterpret_cast<uint4*>(g.dh_bf16 + p * (2 * I) + i0);
+    uint4* udst = reinterpret_cast<uint4*>(g.dh_bf16 + p * (2 * I) + I + i0);
+    float ds = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 g4 = hg[c], u4 = hu[c];
+      const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, uw[4] = {u4.x, u4.y, u4.z, u4.w};
+      uint32_t ap[4], dgp[4], dup[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float d0 = __uint_as_float(v[8 * c + 2 * k]), d1 = __uint_as_float(v[8 * c + 2 * k + 1]);
+        float a0, dg0, du0, a1, dg1, du1;
+        dact_grad(d0, __uint_as_float(gw[k] << 16), __uint_as_float(uw[k] << 16), sc, a0, dg0, du0);
+        dact_grad(d1, __uint_as_float(gw[k] & 0xFFFF0000u), __uint_as_float(uw[k] & 0xFFFF0000u), sc, a1, dg1, du1);
+        ds = fmaf(d1, a1, fmaf(d0, a0, ds));
+        amg = fmaxf(amg, fmaxf(fabsf(dg0), fabsf(dg1)));
+        amu = fmaxf(amu, fmaxf(fabsf(du0), fabsf(du1)));
+        ap[k] = pack_bf16x2(sc * a0, sc * a1);
+        dgp[k] = pack_bf16x2(dg0, dg1);
+        dup[k] = pack_bf16x2(du0, du1);
+      }
+      adst[c] = make_uint4(ap[0], ap[1], ap[2], ap[3]);
+      gdst[c] = make_uint4(dgp[0], dgp[1], dgp[2], dgp[3]);
+      udst[c] = make_uint4(dup[0], dup[1], dup[2], dup[3]);
+    }
+    atomicAdd(g.ds + g.s_scatter[m.tok], ds);
+  }
+  float* buf = s_amax + (tcount & 1) * (2 * 4 * kBlockM);
+  buf[cc * kBlockM + r] = amg;
+  buf[(4 + cc) * kBlockM + r] = amu;
+  __syncwarp();
+  if (lane == 0) mbar_arrive(amax_bar);
+  if (!mbar_wait(amax_bar, tcount & 1, g.err, kErrTimeoutEpilogue)) return false;
+  if (!valid) return true;
+  amg = fmaxf(amg, buf[(cc ^ 1) * kBlockM + r]);
+  amu = fmaxf(amu, buf[(4 + (cc ^ 1)) * kBlockM + r]);
+  const int eg = scale_exp_of_amax(amg), eu = scale_exp_of_amax(amu);
+  const float ig = exp2_neg(eg), iu = exp2_neg(eu);
+  const int j = i0 / kBlockK, c0 = i0 % kBlockK;
+  uint4* gq = reinterpret_cast<uint4*>(g.out_q + p * (2 * I) + 256 * j + c0);
+  uint4* uq = reinterpret_cast<uint4*>(g.out_q + p * (2 * I) + 256 * j + 128 + c0);
+#pragma unroll
+  for (int c2 = 0; c2 < 4; ++c2) {
+    uint32_t wg[4], wu[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = 2 * c2 + h;
+      const uint4 g4 = hg[c], u4 = hu[c];
+      const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, uw[4] = {u4.x, u4.y, u4.z, u4.w};
+      uint16_t qg[4], qu[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float a0, dg0, du0, a1, dg1, du1;
+        dact_grad(__uint_as_float(v[8 * c + 2 * k]), __uint_as_float(gw[k] << 16), __uint_as_float(uw[k] << 16), sc,
+                  a0, dg0, du0);
+        dact_grad(__uint_as_float(v[8 * c + 2 * k + 1]), __uint_as_float(gw[k] & 0xFFFF0000u),
+                  __uint_as_float(uw[k] & 0xFFFF0000u), sc, a1, dg1, du1);
+        qg[k] = cvt_e4m3x2(__fmul_rn(dg0, ig), __fmul_rn(dg1, ig));
+        qu[k] = cvt_e4m3x2(__fmul_rn(du0, iu), __fmul_rn(du1, iu));
+      }
+      wg[2 * h] = static_cast<uint32_t>(qg[0]) | (static_cast<uint32_t>(qg[1]) << 16);
+      wg[2 * h + 1] = static_cast<uint32_t>(qg[2]) | (static_cast<uint32_t>(qg[3]) << 16);
+      wu[2 * h] = static_cast<uint32_t>(qu[0]) | (static_cast<uint32_t>(qu[1]) << 16);
+      wu[2 * h + 1] = static_cast<uint32_t>(qu[2]) | (static_cast<uint32_t>(qu[3]) << 16);
+    }
+    gq[c2] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
+    uq[c2] = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+  }
+  if (c0 == 0) {
+    // K blocks 2 j (gate) and 2 j + 1 (up) of the dX GEMM; atoms hold 4 consecutive K blocks
+    const int KG2 = (2 * I / kBlockK + 3) / 4;
+    const size_t base = static_cast<size_t>(m.mb) * KG2 * kSfAtomBytes + 16 * (r % 32) + 4 * (r / 32);
+    g.out_sf[base + static_cast<size_t>((2 * j) / 4) * kSfAtomBytes + ((2 * j) % 4)] = static_cast<uint8_t>(eg + 127);
+    g.out_sf[base + static_cast<size_t>((2 * j + 1) / 4) * kSfAtomBytes + ((2 * j + 1) % 4)] =
+        static_cast<uint8_t>(eu + 127);
+  }
+  return true;
+}
+
 // Epilogue of one accumulator tile: this thread holds row r (0..127) of the tile's 128-row block,
 // output columns [64 cc, 64 cc + 64) of its n-tile in v (f32 bits).  Returns false if a bounded
 // wait gave up.
@@ -236,6 +337,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const uint32_t 
   const bool valid = m.valid != 0;
   const int p = m.p, mb = m.mb, nt = m.nt;
   if constexpr (kKind == kKindDact) {
+    if (g.concat) return dact_tile_concat(g, v, m, cc, lane, tcount, s_amax, amax_bar);
     dact_tile(g, v, m, cc);
   } else if constexpr (kUp) {
     if (g.preact != nullptr && valid) {

@@ -99,7 +99,7 @@ SIGNATURES = {
     "sm_weight_prep_t": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "sm_moe_dact": (
         _I,
-        [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+        [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P],
     ),
     "sm_tq_pack": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_moe_wgrad": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),

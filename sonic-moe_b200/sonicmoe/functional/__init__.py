@@ -31,9 +31,9 @@ backward (``ops.moe_backward``: dx, the router logits' gradient, dw1, dw2), as t
 
 Differences from the reference, all explicit errors: biases and activations other than SwiGLU
 raise ``NotImplementedError`` (the FP8 engine implements the bias-free SwiGLU layer); the backward
-covers the interleaved w1 layout of ``moe_TC_softmax_topk_layer`` with I % 256 == 0 --
-``concat_layout=True`` and ``moe_general_routing_inputs`` raise ``NotImplementedError`` when a
-gradient is requested, instead of returning an output whose expert weights would never receive one.
+covers ``moe_TC_softmax_topk_layer`` (both w1 layouts, I % 256 == 0) -- the fused router and
+``moe_general_routing_inputs`` raise ``NotImplementedError`` when a gradient is requested, instead of
+returning an output whose expert weights would never receive one.
 """
 import weakref
 
@@ -141,11 +141,12 @@ class _FP8MoEFunction(torch.autograd.Function):
     """Training forward + FP8 backward of the token-choice layer after the router GEMM (the reference's
     router function, _UpProjection and _DownProjection autograd functions,
     functional/__init__.py:174-202, 227-479).  Inputs: x [T, H] bf16, router_logits [T, E], w1 / w2 in
-    the reference's (2I, H, E) / (H, I, E) views (interleaved gate/up rows); outputs (o, expert_frequency)."""
+    the reference's (2I, H, E) / (H, I, E) views (interleaved or concatenated gate/up rows); outputs
+    (o, expert_frequency)."""
 
     @staticmethod
-    def forward(ctx, x, router_logits, w1, w2, K, softmax_over_topk, norm_topk_probs):
-        w1q = prepare_fp8_weights(w1, concat_glu=False)
+    def forward(ctx, x, router_logits, w1, w2, K, softmax_over_topk, norm_topk_probs, concat_layout):
+        w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
         w2q = prepare_fp8_weights(w2, concat_glu=False)
         T, H = x.shape
         E = router_logits.shape[1]
@@ -163,7 +164,7 @@ class _FP8MoEFunction(torch.autograd.Function):
         ctx.save_for_backward(x, router_logits, w1, w2, scores, idx, h, err, plan.freq, plan.off, plan.x_gather,
                               plan.s_scatter, plan.s_rev, plan.off_pad, plan.blk_expert, plan.n_blocks)
         ctx.max_blocks = plan.max_blocks
-        ctx.modes = (bool(softmax_over_topk), bool(norm_topk_probs))
+        ctx.modes = (bool(softmax_over_topk), bool(norm_topk_probs), bool(concat_layout))
         freq = plan.freq.clone()
         ctx.mark_non_differentiable(freq)
         return out, freq
@@ -173,9 +174,9 @@ class _FP8MoEFunction(torch.autograd.Function):
         (x, router_logits, w1, w2, scores, idx, h, err, freq, off, x_gather, s_scatter, s_rev, off_pad, blk_expert,
          n_blocks) = ctx.saved_tensors
         plan = ops.RoutePlan(freq, off, x_gather, s_scatter, s_rev, off_pad, blk_expert, n_blocks, ctx.max_blocks)
-        sot, norm = ctx.modes
+        sot, norm, concat = ctx.modes
         # the e4m3 weights the forward ran with (cached per weight version), read transposed
-        w1q = prepare_fp8_weights(w1, concat_glu=False)
+        w1q = prepare_fp8_weights(w1, concat_glu=concat)
         w2q = prepare_fp8_weights(w2, concat_glu=False)
         dx, dlogits, dw1, dw2, _ = ops.moe_backward(dout.to(torch.bfloat16).contiguous(), x, router_logits, w1q, w2q,
                                                     scores, idx, plan, h, sot, norm, err)
@@ -183,7 +184,7 @@ class _FP8MoEFunction(torch.autograd.Function):
         if code:
             raise RuntimeError(f"FP8 MoE backward: device error {code}")
         return (dx, dlogits.to(router_logits.dtype), dw1.permute(1, 2, 0).to(w1.dtype), dw2.permute(1, 2, 0).to(w2.dtype),
-                None, None, None)
+                None, None, None, None)
 
 
 @torch.library.custom_op("sonicmoe::fp8_moe_tc_forward", mutates_args=())
@@ -285,17 +286,16 @@ def moe_TC_softmax_topk_layer(
     if norm_topk_probs and is_softmax_over_topk:
         raise ValueError("`norm_topk_prob` only works with softmax-then-topk")
     training = _wants_training(is_inference_mode_enabled, x, router_w, w1, w2)
-    if training and (concat_layout or fused_router or isinstance(w1, Fp8ExpertWeights)
-                     or isinstance(w2, Fp8ExpertWeights)):
-        raise NotImplementedError("the FP8 backward covers bf16 weights in the interleaved layout with the "
-                                  "F.linear router (no concat_layout, fused_router or prepared weights)")
+    if training and (fused_router or isinstance(w1, Fp8ExpertWeights) or isinstance(w2, Fp8ExpertWeights)):
+        raise NotImplementedError("the FP8 backward covers bf16 weights with the F.linear router "
+                                  "(no fused_router or prepared weights)")
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
     x = x.contiguous()
     if training:
         router_logits = F.linear(x, router_w.to(x.dtype))
         o, expert_frequency = _FP8MoEFunction.apply(x, router_logits, w1, w2, K, is_softmax_over_topk,
-                                                    norm_topk_probs)
+                                                    norm_topk_probs, concat_layout)
         return o, router_logits, expert_frequency
     if fused_router:
         rw = router_w.to(x.dtype).contiguous()

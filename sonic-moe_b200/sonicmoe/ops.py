@@ -403,9 +403,8 @@ def moe_general_forward(
 
 def weight_prep_t(w: Fp8ExpertWeights) -> Fp8ExpertWeights:
     """W^T as a backward GEMM's K-major operand, from the forward's prepared weight: e4m3 [E, N, K] ->
-    [E, K, N], the same values and 128x128 block scales read transposed."""
-    if w.concat_glu:
-        raise NotImplementedError("the FP8 backward takes the interleaved w1 layout")
+    [E, K, N], the same values and 128x128 block scales read transposed (for a concatenated w1 the K
+    order is the prepared weight's re-blocked row order)."""
     E, N, K = w.shape
     q = torch.empty(E, K, N, dtype=torch.uint8, device=w.q.device)
     sf = torch.zeros(E, K // _BLOCK_M, -(-(N // 128) // 4), 512, dtype=torch.uint8, device=w.q.device)
@@ -414,7 +413,7 @@ def weight_prep_t(w: Fp8ExpertWeights) -> Fp8ExpertWeights:
 
 
 def moe_dact(doq, dosf, w2t: Fp8ExpertWeights, plan: RoutePlan, scores_flat: torch.Tensor, preact: torch.Tensor, err,
-             dscores: torch.Tensor = None):
+             dscores: torch.Tensor = None, concat_layout: bool = False):
     """dA' = dO W2 per entry fused with the SwiGLU backward: (dh_q, dh_sf, dh_bf16, a_prime, dscores)."""
     E, I, H = w2t.shape
     rows = plan.max_blocks * _BLOCK_M
@@ -429,8 +428,8 @@ def moe_dact(doq, dosf, w2t: Fp8ExpertWeights, plan: RoutePlan, scores_flat: tor
     nat.call(
         "sm_moe_dact", _ptr(doq), _ptr(dosf), _ptr(w2t.q), _ptr(w2t.sf), H, I, E, plan.max_blocks,
         _ptr(plan.blk_expert), _ptr(plan.n_blocks), _ptr(plan.off_pad), _ptr(plan.off), _ptr(plan.freq),
-        _ptr(plan.s_scatter), _ptr(scores_flat), _ptr(preact), _ptr(dh_q), _ptr(dh_sf), _ptr(dh), _ptr(a_prime),
-        _ptr(dscores), _ptr(err), _stream(),
+        _ptr(plan.s_scatter), _ptr(scores_flat), _ptr(preact), int(concat_layout), _ptr(dh_q), _ptr(dh_sf), _ptr(dh),
+        _ptr(a_prime), _ptr(dscores), _ptr(err), _stream(),
     )
     return dh_q, dh_sf, dh, a_prime, dscores
 
@@ -475,14 +474,16 @@ def moe_backward(dout: torch.Tensor, x: torch.Tensor, router_logits: torch.Tenso
                  softmax_over_topk: bool, norm_topk_probs: bool, err):
     """The layer backward from dO [T, H]: (dx [T, H] bf16, dlogits [T, E] fp32, dw1 [E, 2I, H] bf16,
     dw2 [E, H, I] bf16, dscores [T, K] fp32).  w1 / w2: the forward's prepared e4m3 expert weights
-    ([E, 2I, H] interleaved gate/up rows / [E, H, I]); the backward GEMMs use them transposed."""
+    ([E, 2I, H] / [E, H, I]; w1 interleaved or concatenated, as prepared); the backward GEMMs use them
+    transposed, and dw1 comes back in the caller's w1 row order."""
     T, H = dout.shape
     E = w1.shape[0]
     K = idx.shape[1]
     dout = dout.contiguous()
     doq, dosf = quant_pack(dout, idx, plan)
     w2t = weight_prep_t(w2)
-    dh_q, dh_sf, dh, a_prime, ds = moe_dact(doq, dosf, w2t, plan, scores.view(-1), preact, err)
+    dh_q, dh_sf, dh, a_prime, ds = moe_dact(doq, dosf, w2t, plan, scores.view(-1), preact, err,
+                                            concat_layout=w1.concat_glu)
     del doq, dosf, w2t
     w1t = weight_prep_t(w1)
     dx = torch.zeros(T, H, dtype=torch.bfloat16, device=dout.device)

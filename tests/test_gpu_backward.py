@@ -18,10 +18,11 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-2
 
 CASES = [
-    # T, H, I, E, K, softmax_over_topk, norm
-    (256, 512, 256, 8, 2, True, False),
-    (384, 1024, 512, 16, 4, False, True),
-    (64, 512, 256, 64, 8, False, False),  # most experts empty
+    # T, H, I, E, K, softmax_over_topk, norm, concat
+    (256, 512, 256, 8, 2, True, False, False),
+    (384, 1024, 512, 16, 4, False, True, True),  # Qwen3-style routing + concatenated w1
+    (64, 512, 256, 64, 8, False, False, False),  # most experts empty
+    (320, 512, 768, 8, 4, True, False, True),  # concat with I = 768 (three 256-column tiles)
 ]
 
 
@@ -33,7 +34,7 @@ def ops():
     return _ops
 
 
-def _forward_state(ops, x, rw, w1, w2, K, sot, norm):
+def _forward_state(ops, x, rw, w1, w2, K, sot, norm, concat=False):
     """Routing, plan and stored pre-activation of the training forward (as the autograd function runs it)."""
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     logits = torch.nn.functional.linear(x, rw)
@@ -41,19 +42,19 @@ def _forward_state(ops, x, rw, w1, w2, K, sot, norm):
     plan = ops.route_plan(idx, w1.shape[0], err)
     xq, xsf = ops.quant_pack(x, idx, plan)
     h = torch.empty(x.shape[0] * K, w1.shape[1], dtype=torch.bfloat16, device="cuda")
-    ops.moe_up(xq, xsf, ops.weight_prep(w1), plan, err, preact_out=h)
+    ops.moe_up(xq, xsf, ops.weight_prep(w1, concat_glu=concat), plan, err, preact_out=h)
     return logits, scores, idx, plan, h, err
 
 
-@pytest.mark.parametrize("T,H,I,E,K,sot,norm", CASES)
-def test_moe_backward_stages_vs_oracle(ops, T, H, I, E, K, sot, norm):
+@pytest.mark.parametrize("T,H,I,E,K,sot,norm,concat", CASES)
+def test_moe_backward_stages_vs_oracle(ops, T, H, I, E, K, sot, norm, concat):
     x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=11 * T + E)
     xc, rwc, w1c, w2c = x.cuda(), rw.cuda(), w1.cuda(), w2.cuda()
-    logits, scores, idx, plan, h, err = _forward_state(ops, xc, rwc, w1c, w2c, K, sot, norm)
+    logits, scores, idx, plan, h, err = _forward_state(ops, xc, rwc, w1c, w2c, K, sot, norm, concat)
     g = torch.Generator().manual_seed(T + 1)
     dout = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
-    dx, dl, dw1, dw2, ds = ops.moe_backward(dout.cuda(), xc, logits, ops.weight_prep(w1c), ops.weight_prep(w2c),
-                                            scores, idx, plan, h, sot, norm, err)
+    dx, dl, dw1, dw2, ds = ops.moe_backward(dout.cuda(), xc, logits, ops.weight_prep(w1c, concat_glu=concat),
+                                            ops.weight_prep(w2c), scores, idx, plan, h, sot, norm, err)
     torch.cuda.synchronize()
     assert err.item() == 0, f"kernel error word {err.item()}"
     s_np, i_np = scores.cpu().numpy(), idx.cpu().numpy()
@@ -61,7 +62,7 @@ def test_moe_backward_stages_vs_oracle(ops, T, H, I, E, K, sot, norm):
     np.testing.assert_array_equal(i_np, i_ref)
     rdx, rdw1, rdw2, rds, rdl = obwd.fp8_backward(
         x.float().numpy(), dout.float().numpy(), w1.float().numpy(), w2.float().numpy(), s_np, i_np,
-        h.float().cpu().numpy(), sot, norm, logits=logits.float().cpu().numpy())
+        h.float().cpu().numpy(), sot, norm, logits=logits.float().cpu().numpy(), concat_layout=concat)
     for name, got, ref in (("ds", ds, rds), ("dlogits", dl, rdl), ("dx", dx, rdx), ("dw2", dw2, rdw2),
                            ("dw1", dw1, rdw1)):
         err_rel = rel_fro(got.float().cpu().numpy(), ref)
@@ -100,8 +101,8 @@ def test_weight_prep_t_is_the_transpose(ops):
                 assert atoms[e, kb, nb // 4, nb % 4] == sf[e, nb, kb]
 
 
-@pytest.mark.parametrize("T,H,I,E,K,sot,norm", CASES[:2])
-def test_layer_autograd_vs_oracle(T, H, I, E, K, sot, norm):
+@pytest.mark.parametrize("T,H,I,E,K,sot,norm,concat", CASES[:2])
+def test_layer_autograd_vs_oracle(T, H, I, E, K, sot, norm, concat):
     """moe_TC_softmax_topk_layer in training mode: gradients of x (expert path + router F.linear),
     router_w, w1, w2 through the autograd function, against the oracle plus the router GEMM's
     float64 backward."""
@@ -114,18 +115,18 @@ def test_layer_autograd_vs_oracle(T, H, I, E, K, sot, norm):
     w2c = w2.cuda().requires_grad_()
     o, logits, freq = moe_TC_softmax_topk_layer(xc, rwc, w1c.permute(1, 2, 0), None, w2c.permute(1, 2, 0), None, K,
                                                 None, is_inference_mode_enabled=False, is_softmax_over_topk=sot,
-                                                norm_topk_probs=norm)
+                                                norm_topk_probs=norm, concat_layout=concat)
     g = torch.Generator().manual_seed(T + 2)
     dout = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
     (o.float() * dout.cuda().float()).sum().backward()
     torch.cuda.synchronize()
     from sonicmoe import ops
 
-    _, scores, idx, plan, h, _ = _forward_state(ops, x.cuda(), rw.cuda(), w1.cuda(), w2.cuda(), K, sot, norm)
+    _, scores, idx, plan, h, _ = _forward_state(ops, x.cuda(), rw.cuda(), w1.cuda(), w2.cuda(), K, sot, norm, concat)
     lg = logits.detach().float().cpu().numpy()
     rdx, rdw1, rdw2, _, rdl = obwd.fp8_backward(
         x.float().numpy(), dout.float().numpy(), w1.float().numpy(), w2.float().numpy(), scores.cpu().numpy(),
-        idx.cpu().numpy(), h.float().cpu().numpy(), sot, norm, logits=lg)
+        idx.cpu().numpy(), h.float().cpu().numpy(), sot, norm, logits=lg, concat_layout=concat)
     rdx_total = rdx + rdl @ rw.double().numpy()
     rdrw = rdl.T @ x.double().numpy()
     for name, got, ref in (("dx", xc.grad, rdx_total), ("drouter_w", rwc.grad, rdrw), ("dw1", w1c.grad, rdw1),
@@ -140,6 +141,6 @@ def test_training_refusals():
 
     x, rw, w1, w2 = make_layer_inputs(64, 512, 256, 8, seed=1)
     w1c = w1.cuda().requires_grad_()
-    with pytest.raises(NotImplementedError, match="interleaved"):
+    with pytest.raises(NotImplementedError, match="fused_router"):
         moe_TC_softmax_topk_layer(x.cuda(), rw.cuda(), w1c.permute(1, 2, 0), None, w2.cuda().permute(1, 2, 0), None,
-                                  2, None, is_inference_mode_enabled=False, concat_layout=True)
+                                  2, None, is_inference_mode_enabled=False, fused_router=True)

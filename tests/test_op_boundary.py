@@ -31,8 +31,8 @@ def test_moe_forward_exports_as_one_graph():
 
 
 def test_training_without_a_backward_is_refused():
-    """Gradient requests the FP8 backward does not cover raise before any device work: the
-    concatenated w1 layout, the fused router, and the general-routing layer."""
+    """Gradient requests the FP8 backward does not cover raise before any device work: the fused
+    router and the general-routing layer."""
     import sonicmoe
     from sonicmoe.functional import moe_TC_softmax_topk_layer, moe_general_routing_inputs
 
@@ -40,10 +40,7 @@ def test_training_without_a_backward_is_refused():
     m = sonicmoe.MoE(E, K, H, I, sonicmoe.ActivationType.SWIGLU, False, 0.02)
     x = torch.randn(T, H)
     w1, w2 = m.c_fc.weight.permute(1, 2, 0), m.c_proj.weight.permute(1, 2, 0)
-    with pytest.raises(NotImplementedError, match="interleaved layout"):
-        moe_TC_softmax_topk_layer(x, m.router.weight, w1, None, w2, None, K, None, is_inference_mode_enabled=False,
-                                  concat_layout=True)
-    with pytest.raises(NotImplementedError, match="interleaved layout"):
+    with pytest.raises(NotImplementedError, match="fused_router"):
         moe_TC_softmax_topk_layer(x, m.router.weight, w1, None, w2, None, K, None, is_inference_mode_enabled=False,
                                   fused_router=True)
     tok = torch.arange(T, dtype=torch.int32)
