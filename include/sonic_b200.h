@@ -217,6 +217,21 @@ int sm_route_plan(const int32_t* topk_indices, int T, int K, int E, int32_t* exp
                   int32_t* s_reverse_scatter_idx, int32_t* off_pad, int32_t* blk_expert, int32_t* n_blocks,
                   void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
 
+/* sm_route_plan for explicit routing lists (moe_general_routing_inputs): the general metadata of
+ * sm_general_route_metadata plus this build's padded layout (off_pad [E+1], blk_expert, n_blocks).
+ * Workspace: sm_route_metadata_workspace(T, TK, E). */
+int sm_general_route_plan(const int32_t* sorted_token_idx, const int32_t* expert_idx, int T, int TK, int E,
+                          int32_t* expert_frequency, int32_t* expert_frequency_offset, int32_t* x_gather_idx,
+                          int32_t* s_scatter_idx, int32_t* s_reverse_scatter_idx,
+                          int32_t* num_activated_expert_per_token_offset, int32_t* off_pad, int32_t* blk_expert,
+                          int32_t* n_blocks, void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
+/* sm_quant_pack for explicit routing lists: token t's row goes to the padded rows of its entries
+ * [tok_off[t], tok_off[t+1]) (expert_idx per entry). */
+int sm_quant_pack_general(const void* x, int T, int H, const int32_t* expert_idx,
+                          const int32_t* num_activated_expert_per_token_offset, const int32_t* s_reverse_scatter_idx,
+                          const int32_t* expert_frequency_offset, const int32_t* off_pad, uint8_t* xq, uint8_t* xsf,
+                          void* stream);
+
 /* Quantise x [T, H] and write each token's row to its K padded positions:
  * xq [max_blocks*128, H] e4m3, xsf atoms [max_blocks][ceil(H/512)][512]. */
 int sm_quant_pack(const void* x, int T, int H, const int32_t* topk_indices, int K,

@@ -55,44 +55,31 @@ def router_backward(logits, scores, idx, ds, softmax_over_topk=True, norm_topk_p
     return p * (dp - dot)
 
 
-def fp8_backward(x, dout, w1, w2, scores, idx, h, softmax_over_topk=True, norm_topk_probs=False, logits=None,
-                 concat_layout=False):
-    """(dx [T, H], dw1 [E, 2I, H], dw2 [E, H, I], ds [T, K], dlogits [T, E] or None), float64.
-
-    x, dout [T, H]; w1 [E, 2I, H], w2 [E, H, I] (bf16 values as float); scores / idx [T, K] the
-    forward's routing; h [T*K, 2I] the stored pre-activation in expert-sorted entry order.  With
-    concat_layout the gate / up halves of w1, h and dH are [gate | up] instead of interleaved; dH's 1x128
-    groups along 2I are then gate-only and up-only groups, as in the engine."""
-    x = np.asarray(x, dtype=np.float32)
-    dout = np.asarray(dout, dtype=np.float32)
-    idx = np.asarray(idx)
+def _fp8_backward_entries(x, dout, w1, w2, tok, e, s, meta, h, concat_layout):
+    """Expert part of the backward over explicit entries (token tok[f], expert e[f], score s[f])."""
     T, H = x.shape
-    K = idx.shape[1]
     E, N2, _ = np.asarray(w1).shape
     I = N2 // 2
-    freq, off, x_gather, s_scatter, s_rev = metadata.tc_metadata(idx, E)
+    freq, off, s_rev = meta
     off_pad, _, nblk = metadata.padded_layout(freq)
-    prow = metadata.padded_rows(idx, s_rev, off, off_pad)  # padded row of flat entry f
+    prow = (np.asarray(s_rev).astype(np.int64) - off[e] + off_pad[e]).astype(np.int64)  # padded row of entry f
     w1d = quant.dequant_128x128(*quant.quant_128x128(np.asarray(w1, dtype=np.float32))).astype(np.float64)
     w2d = quant.dequant_128x128(*quant.quant_128x128(np.asarray(w2, dtype=np.float32))).astype(np.float64)
-    f = np.arange(T * K)
-    tok = f // K
-    e = idx.reshape(-1)
-    s = np.asarray(scores, dtype=np.float64).reshape(-1)
+    TK = tok.shape[0]
     # h rows are in expert-sorted order: entry f sits at row s_rev[f]
     hf = np.asarray(h, dtype=np.float64)[s_rev]
     g, u = (hf[:, :I], hf[:, I:]) if concat_layout else (hf[:, 0::2], hf[:, 1::2])
     sig = 1.0 / (1.0 + np.exp(-g))
     a = g * sig * u
     dod = _q1x128(dout)
-    dap = np.zeros((T * K, I))
+    dap = np.zeros((TK, I))
     for ex in np.unique(e):
         r = np.nonzero(e == ex)[0]
         dap[r] = dod[tok[r]] @ w2d[ex]
     ds = (dap * a).sum(1)
     da = s[:, None] * dap
     dg, du = da * u * sig * (1.0 + g * (1.0 - sig)), da * g * sig
-    dh = np.empty((T * K, 2 * I))
+    dh = np.empty((TK, 2 * I))
     if concat_layout:
         dh[:, :I], dh[:, I:] = dg, du
     else:
@@ -121,6 +108,41 @@ def fp8_backward(x, dout, w1, w2, scores, idx, h, softmax_over_topk=True, norm_t
         if c1 > c0:
             dw2[ex] = dot_[:, c0:c1] @ apt[:, c0:c1].T
             dw1[ex] = dht[:, c0:c1] @ xt[:, c0:c1].T
+    return dx, dw1, dw2, ds
+
+
+def fp8_backward(x, dout, w1, w2, scores, idx, h, softmax_over_topk=True, norm_topk_probs=False, logits=None,
+                 concat_layout=False):
+    """(dx [T, H], dw1 [E, 2I, H], dw2 [E, H, I], ds [T, K], dlogits [T, E] or None), float64.
+
+    x, dout [T, H]; w1 [E, 2I, H], w2 [E, H, I] (bf16 values as float); scores / idx [T, K] the
+    forward's routing; h [T*K, 2I] the stored pre-activation in expert-sorted entry order.  With
+    concat_layout the gate / up halves of w1, h and dH are [gate | up] instead of interleaved; dH's 1x128
+    groups along 2I are then gate-only and up-only groups, as in the engine."""
+    x = np.asarray(x, dtype=np.float32)
+    dout = np.asarray(dout, dtype=np.float32)
+    idx = np.asarray(idx)
+    T, K = idx.shape
+    E = np.asarray(w1).shape[0]
+    freq, off, _, _, s_rev = metadata.tc_metadata(idx, E)
+    tok = np.arange(T * K) // K
+    e = idx.reshape(-1).astype(np.int64)
+    s = np.asarray(scores, dtype=np.float64).reshape(-1)
+    dx, dw1, dw2, ds = _fp8_backward_entries(x, dout, w1, w2, tok, e, s, (freq, off, s_rev), h, concat_layout)
     ds = ds.reshape(T, K)
     dl = None if logits is None else router_backward(logits, scores, idx, ds, softmax_over_topk, norm_topk_probs)
     return dx, dw1, dw2, ds, dl
+
+
+def fp8_backward_general(x, dout, w1, w2, router_scores, token_idx, expert_idx, h, concat_layout=False):
+    """(dx [T, H], dw1, dw2, d router_scores [TK]), float64, of the layer over explicit entries
+    (``moe_general_routing_inputs``; token_idx sorted ascending); h [TK, 2I] in expert-sorted order."""
+    x = np.asarray(x, dtype=np.float32)
+    dout = np.asarray(dout, dtype=np.float32)
+    T = x.shape[0]
+    E = np.asarray(w1).shape[0]
+    tok = np.asarray(token_idx).astype(np.int64)
+    e = np.asarray(expert_idx).astype(np.int64)
+    freq, off, _, _, s_rev, _ = metadata.general_metadata(tok, e, T, E)
+    s = np.asarray(router_scores, dtype=np.float64)
+    return _fp8_backward_entries(x, dout, w1, w2, tok, e, s, (freq, off, s_rev), h, concat_layout)

@@ -333,6 +333,36 @@ int sm_route_plan(const int32_t* topk_indices, int T, int K, int E, int32_t* exp
                       workspace_bytes, err, static_cast<cudaStream_t>(stream), off_pad, blk_expert, n_blocks);
 }
 
+int sm_general_route_plan(const int32_t* sorted_token_idx, const int32_t* expert_idx, int T, int TK, int E,
+                          int32_t* expert_frequency, int32_t* expert_frequency_offset, int32_t* x_gather_idx,
+                          int32_t* s_scatter_idx, int32_t* s_reverse_scatter_idx,
+                          int32_t* num_activated_expert_per_token_offset, int32_t* off_pad, int32_t* blk_expert,
+                          int32_t* n_blocks, void* workspace, size_t workspace_bytes, int32_t* err, void* stream) {
+  if (T < 0 || TK < 0 || E < 1 || E > 16384) return fail(SM_EINVAL, "bad shape T=%d TK=%d E=%d (E <= 16384)", T, TK, E);
+  if (!expert_frequency || !expert_frequency_offset || !num_activated_expert_per_token_offset || !off_pad ||
+      !blk_expert || !n_blocks || !err)
+    return fail(SM_EINVAL, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = route_common(expert_idx, sorted_token_idx, T, TK, 1, E, 1024, route_tiles_general(TK), expert_frequency,
+                        expert_frequency_offset, x_gather_idx, s_scatter_idx, s_reverse_scatter_idx, workspace,
+                        workspace_bytes, err, st, off_pad, blk_expert, n_blocks);
+  if (rc) return rc;
+  return cuda_status(launch_token_offset(sorted_token_idx, T, TK, num_activated_expert_per_token_offset, st),
+                     "token_offset");
+}
+
+int sm_quant_pack_general(const void* x, int T, int H, const int32_t* expert_idx,
+                          const int32_t* num_activated_expert_per_token_offset, const int32_t* s_reverse_scatter_idx,
+                          const int32_t* expert_frequency_offset, const int32_t* off_pad, uint8_t* xq, uint8_t* xsf,
+                          void* stream) {
+  if (T < 0 || H <= 0 || H % 128) return fail(SM_EINVAL, "bad shape T=%d H=%d", T, H);
+  if (!aligned16(x) || !aligned16(xq) || !aligned16(xsf)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  return cuda_status(launch_quant_pack(x, T, H, expert_idx, 0, num_activated_expert_per_token_offset,
+                                       s_reverse_scatter_idx, expert_frequency_offset, off_pad, xq, xsf,
+                                       static_cast<cudaStream_t>(stream)),
+                     "quant_pack_general");
+}
+
 int sm_quant_pack(const void* x, int T, int H, const int32_t* topk_indices, int K, const int32_t* s_reverse_scatter_idx,
                   const int32_t* expert_frequency_offset, const int32_t* off_pad, uint8_t* xq, uint8_t* xsf,
                   void* stream) {

@@ -94,6 +94,8 @@ SIGNATURES = {
     "sm_copy_d2d_async": (_I, [_P, _P, _SZ, _P]),
     "sm_route_plan": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "sm_quant_pack": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
+    "sm_general_route_plan": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
+    "sm_quant_pack_general": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up_preact": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_weight_prep_t": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),

@@ -24,16 +24,17 @@ after the router GEMM is one more registered op per entry point (``sonicmoe::fp8
 traces a whole ``MoE`` forward without a graph break.
 
 Training: with ``is_inference_mode_enabled=False`` while autograd is recording and an input or
-weight requires grad, ``moe_TC_softmax_topk_layer`` runs the training forward (the up GEMM also
-stores the pre-activation h) inside an autograd function whose backward is the engine's FP8
-backward (``ops.moe_backward``: dx, the router logits' gradient, dw1, dw2), as the reference's
-``_UpProjection`` / ``_DownProjection`` / router functions do.
+weight requires grad, ``moe_TC_softmax_topk_layer`` and ``moe_general_routing_inputs`` run the
+training forward (the up GEMM also stores the pre-activation h) inside an autograd function whose
+backward is the engine's FP8 backward (``ops.moe_backward``: dx, the router logits' or router
+scores' gradient, dw1, dw2), as the reference's ``_UpProjection`` / ``_DownProjection`` / router
+functions do.
 
 Differences from the reference, all explicit errors: biases and activations other than SwiGLU
 raise ``NotImplementedError`` (the FP8 engine implements the bias-free SwiGLU layer); the backward
-covers ``moe_TC_softmax_topk_layer`` (both w1 layouts, I % 256 == 0) -- the fused router and
-``moe_general_routing_inputs`` raise ``NotImplementedError`` when a gradient is requested, instead of
-returning an output whose expert weights would never receive one.
+covers ``moe_TC_softmax_topk_layer`` and ``moe_general_routing_inputs`` (both w1 layouts,
+I % 256 == 0) -- the fused router and prepared e4m3 weights raise ``NotImplementedError`` when a
+gradient is requested, instead of returning an output whose weights would never receive one.
 """
 import weakref
 
@@ -127,14 +128,6 @@ def _wants_training(is_inference_mode_enabled, *tensors) -> bool:
     if is_inference_mode_enabled or not torch.is_grad_enabled():
         return False
     return any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors)
-
-
-def _reject_training(is_inference_mode_enabled, *tensors, what="this layer"):
-    if _wants_training(is_inference_mode_enabled, *tensors):
-        raise NotImplementedError(
-            f"the FP8 B200 engine has no backward for {what}: call it with is_inference_mode_enabled=True "
-            "or under torch.no_grad(); training would leave the expert weights without gradients"
-        )
 
 
 class _FP8MoEFunction(torch.autograd.Function):
@@ -256,6 +249,53 @@ def _(x, router_scores, token_indices, expert_indices, w1, w2, concat_layout):
     return x.new_empty(x.shape, dtype=torch.bfloat16), x.new_empty(w2.shape[-1], dtype=torch.int32)
 
 
+class _FP8MoEGeneralFunction(torch.autograd.Function):
+    """Training forward + FP8 backward of the layer over explicit routing lists
+    (``moe_general_routing_inputs``, reference functional/__init__.py:571-652 with its autograd
+    functions): gradients for x, the router scores and the expert weights."""
+
+    @staticmethod
+    def forward(ctx, x, router_scores, token_indices, expert_indices, w1, w2, concat_layout):
+        w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
+        w2q = prepare_fp8_weights(w2, concat_glu=False)
+        T, H = x.shape
+        E = w2q.shape[0]
+        I = w2q.shape[2]
+        TK = router_scores.numel()
+        dev = x.device
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        plan = ops.general_route_plan(token_indices, expert_indices, T, E, err)
+        xq, xsf = ops.quant_pack_general(x, expert_indices, plan)
+        h = torch.empty(TK, 2 * I, dtype=torch.bfloat16, device=dev)
+        aq, asf = ops.moe_up(xq, xsf, w1q, plan, err, preact_out=h)
+        del xq, xsf
+        out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+        ops.moe_down_combine(aq, asf, w2q, plan, router_scores, T, err, out=out)
+        ctx.save_for_backward(x, router_scores, expert_indices, w1, w2, h, err, plan.freq, plan.off, plan.x_gather,
+                              plan.s_scatter, plan.s_rev, plan.off_pad, plan.blk_expert, plan.n_blocks, plan.tok_off)
+        ctx.max_blocks = plan.max_blocks
+        ctx.concat = bool(concat_layout)
+        freq = plan.freq.clone()
+        ctx.mark_non_differentiable(freq)
+        return out, freq
+
+    @staticmethod
+    def backward(ctx, dout, _dfreq):
+        (x, router_scores, expert_indices, w1, w2, h, err, freq, off, x_gather, s_scatter, s_rev, off_pad,
+         blk_expert, n_blocks, tok_off) = ctx.saved_tensors
+        plan = ops.RoutePlan(freq, off, x_gather, s_scatter, s_rev, off_pad, blk_expert, n_blocks, ctx.max_blocks,
+                             tok_off)
+        w1q = prepare_fp8_weights(w1, concat_glu=ctx.concat)
+        w2q = prepare_fp8_weights(w2, concat_glu=False)
+        dx, _, dw1, dw2, ds = ops.moe_backward(dout.to(torch.bfloat16).contiguous(), x, None, w1q, w2q,
+                                               router_scores, expert_indices, plan, h, True, False, err, general=True)
+        code = int(err.item())
+        if code:
+            raise RuntimeError(f"FP8 MoE backward: device error {code}")
+        return (dx, ds.to(router_scores.dtype), None, None, dw1.permute(1, 2, 0).to(w1.dtype),
+                dw2.permute(1, 2, 0).to(w2.dtype), None)
+
+
 def moe_TC_softmax_topk_layer(
     x: torch.Tensor,
     router_w: torch.Tensor,
@@ -348,7 +388,9 @@ def moe_general_routing_inputs(
     (``functional/__init__.py:592``).
     """
     _check_common(b1, b2, activation_type)
-    _reject_training(is_inference_mode_enabled, x, router_scores, w1, w2, what="moe_general_routing_inputs")
+    training = _wants_training(is_inference_mode_enabled, x, router_scores, w1, w2)
+    if training and (isinstance(w1, Fp8ExpertWeights) or isinstance(w2, Fp8ExpertWeights)):
+        raise NotImplementedError("the FP8 backward covers bf16 weights (no prepared weights)")
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
     x = x.contiguous()
@@ -356,6 +398,8 @@ def moe_general_routing_inputs(
         router_scores = router_scores.float()
     args = (x, router_scores.contiguous(), token_indices.to(torch.int32).contiguous(),
             expert_indices.to(torch.int32).contiguous())
+    if training:
+        return _FP8MoEGeneralFunction.apply(*args, w1, w2, concat_layout)
     if isinstance(w1, Fp8ExpertWeights) or isinstance(w2, Fp8ExpertWeights):
         w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
         w2q = prepare_fp8_weights(w2, concat_glu=False)

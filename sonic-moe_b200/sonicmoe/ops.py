@@ -206,6 +206,7 @@ class RoutePlan:
     blk_expert: torch.Tensor
     n_blocks: torch.Tensor
     max_blocks: int
+    tok_off: torch.Tensor = None  # explicit routing lists: entries [tok_off[t], tok_off[t+1]) of token t
 
 
 def route_plan(topk_indices: torch.Tensor, E: int, err: torch.Tensor) -> RoutePlan:
@@ -232,6 +233,48 @@ def route_plan(topk_indices: torch.Tensor, E: int, err: torch.Tensor) -> RoutePl
         ws.numel(), _ptr(err), _stream(),
     )
     return p
+
+
+def general_route_plan(token_indices: torch.Tensor, expert_indices: torch.Tensor, T: int, E: int,
+                       err: torch.Tensor) -> RoutePlan:
+    """Routing plan of explicit (token, expert) entries, token_indices sorted ascending."""
+    _need(token_indices, "token_indices", torch.int32)
+    _need(expert_indices, "expert_indices", torch.int32)
+    TK = token_indices.numel()
+    dev = token_indices.device
+    mb = max_padded_blocks(TK, E)
+    p = RoutePlan(
+        freq=torch.empty(E, dtype=torch.int32, device=dev),
+        off=torch.empty(E + 1, dtype=torch.int32, device=dev),
+        x_gather=torch.empty(TK, dtype=torch.int32, device=dev),
+        s_scatter=torch.empty(TK, dtype=torch.int32, device=dev),
+        s_rev=torch.empty(TK, dtype=torch.int32, device=dev),
+        off_pad=torch.empty(E + 1, dtype=torch.int32, device=dev),
+        blk_expert=torch.empty(mb + 1, dtype=torch.int32, device=dev),
+        n_blocks=torch.empty(1, dtype=torch.int32, device=dev),
+        max_blocks=mb,
+        tok_off=torch.empty(T + 1, dtype=torch.int32, device=dev),
+    )
+    ws = _workspace(nat.load().sm_route_metadata_workspace(T, TK, E), dev)
+    nat.call(
+        "sm_general_route_plan", _ptr(token_indices), _ptr(expert_indices), T, TK, E, _ptr(p.freq), _ptr(p.off),
+        _ptr(p.x_gather), _ptr(p.s_scatter), _ptr(p.s_rev), _ptr(p.tok_off), _ptr(p.off_pad), _ptr(p.blk_expert),
+        _ptr(p.n_blocks), _ptr(ws), ws.numel(), _ptr(err), _stream(),
+    )
+    return p
+
+
+def quant_pack_general(x: torch.Tensor, expert_indices: torch.Tensor, plan: RoutePlan):
+    """quant_pack for explicit routing lists (plan from general_route_plan)."""
+    _need(x, "x", torch.bfloat16)
+    T, H = x.shape
+    xq = torch.empty(plan.max_blocks * _BLOCK_M, H, dtype=torch.uint8, device=x.device)
+    xsf = torch.zeros(plan.max_blocks, -(-H // 512), 512, dtype=torch.uint8, device=x.device)
+    nat.call(
+        "sm_quant_pack_general", _ptr(x), T, H, _ptr(expert_indices), _ptr(plan.tok_off), _ptr(plan.s_rev),
+        _ptr(plan.off), _ptr(plan.off_pad), _ptr(xq), _ptr(xsf), _stream(),
+    )
+    return xq, xsf
 
 
 def quant_pack(x: torch.Tensor, topk_indices: torch.Tensor, plan: RoutePlan):
@@ -471,16 +514,20 @@ def router_bwd(router_logits: torch.Tensor, scores: torch.Tensor, idx: torch.Ten
 
 def moe_backward(dout: torch.Tensor, x: torch.Tensor, router_logits: torch.Tensor, w1: Fp8ExpertWeights,
                  w2: Fp8ExpertWeights, scores: torch.Tensor, idx: torch.Tensor, plan: RoutePlan, preact: torch.Tensor,
-                 softmax_over_topk: bool, norm_topk_probs: bool, err):
+                 softmax_over_topk: bool, norm_topk_probs: bool, err, general: bool = False):
     """The layer backward from dO [T, H]: (dx [T, H] bf16, dlogits [T, E] fp32, dw1 [E, 2I, H] bf16,
     dw2 [E, H, I] bf16, dscores [T, K] fp32).  w1 / w2: the forward's prepared e4m3 expert weights
     ([E, 2I, H] / [E, H, I]; w1 interleaved or concatenated, as prepared); the backward GEMMs use them
-    transposed, and dw1 comes back in the caller's w1 row order."""
+    transposed, and dw1 comes back in the caller's w1 row order.
+
+    general=True: explicit routing lists (plan from ``general_route_plan``, ``idx`` = the entries'
+    expert ids [TK], ``scores`` = the router scores [TK]); dlogits is None and dscores [TK] is the
+    gradient of the router scores."""
     T, H = dout.shape
     E = w1.shape[0]
-    K = idx.shape[1]
+    K = 1 if general else idx.shape[1]
     dout = dout.contiguous()
-    doq, dosf = quant_pack(dout, idx, plan)
+    doq, dosf = quant_pack_general(dout, idx, plan) if general else quant_pack(dout, idx, plan)
     w2t = weight_prep_t(w2)
     dh_q, dh_sf, dh, a_prime, ds = moe_dact(doq, dosf, w2t, plan, scores.view(-1), preact, err,
                                             concat_layout=w1.concat_glu)
@@ -501,6 +548,8 @@ def moe_backward(dout: torch.Tensor, x: torch.Tensor, router_logits: torch.Tenso
     dht_q, dht_sf = tq_pack(dh, plan, padded=True)
     xt_q, xt_sf = tq_pack(x.contiguous(), plan, padded=False)
     dw1 = moe_wgrad(dht_q, dht_sf, xt_q, xt_sf, E, plan, err)  # [E, 2I, H]
+    if general:
+        return dx, None, dw1, dw2, ds
     ds = ds.view(T, K)
     dlogits = router_bwd(router_logits, scores, idx, ds, softmax_over_topk, norm_topk_probs)
     return dx, dlogits, dw1, dw2, ds

@@ -144,3 +144,55 @@ def test_training_refusals():
     with pytest.raises(NotImplementedError, match="fused_router"):
         moe_TC_softmax_topk_layer(x.cuda(), rw.cuda(), w1c.permute(1, 2, 0), None, w2.cuda().permute(1, 2, 0), None,
                                   2, None, is_inference_mode_enabled=False, fused_router=True)
+
+
+def _general_entries(T, E, avg_k, seed):
+    rs = np.random.RandomState(seed)
+    toks, exps, scs = [], [], []
+    for t in range(T):
+        k = rs.randint(0, min(2 * avg_k, E) + 1)  # tokens without entries get zero gradients
+        e = rs.permutation(E)[:k]
+        w = rs.rand(k).astype(np.float32)
+        toks += [t] * k
+        exps += list(e)
+        scs += list(w / max(w.sum(), 1e-6))
+    return (np.array(toks, dtype=np.int32), np.array(exps, dtype=np.int32), np.array(scs, dtype=np.float32))
+
+
+@pytest.mark.parametrize("T,H,I,E,avg_k,concat", [(256, 512, 256, 8, 2, False), (300, 512, 512, 16, 4, True)])
+def test_general_routing_autograd_vs_oracle(T, H, I, E, avg_k, concat):
+    """moe_general_routing_inputs in training mode: gradients of x, the router scores, w1 and w2
+    through the autograd function, against oracle.backward.fp8_backward_general."""
+    from sonicmoe import ops
+    from sonicmoe.functional import moe_general_routing_inputs
+
+    x, _, w1, w2 = make_layer_inputs(T, H, I, E, seed=T + 5 * E)
+    tok, ex, sc = _general_entries(T, E, avg_k, seed=T + 1)
+    xc = x.cuda().requires_grad_()
+    scc = torch.from_numpy(sc).cuda().requires_grad_()
+    w1c = w1.cuda().requires_grad_()
+    w2c = w2.cuda().requires_grad_()
+    tokc, exc = torch.from_numpy(tok).cuda(), torch.from_numpy(ex).cuda()
+    o, freq = moe_general_routing_inputs(xc, scc, tokc, exc, w1c.permute(1, 2, 0), None, w2c.permute(1, 2, 0), None,
+                                         E, None, is_inference_mode_enabled=False, concat_layout=concat)
+    g = torch.Generator().manual_seed(T + 3)
+    dout = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
+    (o.float() * dout.cuda().float()).sum().backward()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(freq.cpu().numpy(), np.bincount(ex, minlength=E))
+    # the stored pre-activation, recomputed through the same stages
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    plan = ops.general_route_plan(tokc, exc, T, E, err)
+    xq, xsf = ops.quant_pack_general(x.cuda(), exc, plan)
+    h = torch.empty(tok.shape[0], 2 * I, dtype=torch.bfloat16, device="cuda")
+    ops.moe_up(xq, xsf, ops.weight_prep(w1.cuda(), concat_glu=concat), plan, err, preact_out=h)
+    rdx, rdw1, rdw2, rds = obwd.fp8_backward_general(x.float().numpy(), dout.float().numpy(), w1.float().numpy(),
+                                                     w2.float().numpy(), sc, tok, ex, h.float().cpu().numpy(),
+                                                     concat_layout=concat)
+    for name, got, ref in (("dx", xc.grad, rdx), ("dscores", scc.grad, rds), ("dw1", w1c.grad, rdw1),
+                           ("dw2", w2c.grad, rdw2)):
+        assert got is not None, name
+        err_rel = rel_fro(got.float().cpu().numpy(), ref)
+        assert err_rel <= TOL, f"{name}: rel. Frobenius {err_rel:.3g}"
+    counts = np.bincount(tok, minlength=T)
+    assert torch.all(xc.grad[torch.from_numpy(counts == 0).cuda()] == 0)

@@ -32,9 +32,9 @@ def test_moe_forward_exports_as_one_graph():
 
 def test_training_without_a_backward_is_refused():
     """Gradient requests the FP8 backward does not cover raise before any device work: the fused
-    router and the general-routing layer."""
+    router."""
     import sonicmoe
-    from sonicmoe.functional import moe_TC_softmax_topk_layer, moe_general_routing_inputs
+    from sonicmoe.functional import moe_TC_softmax_topk_layer
 
     T, H, I, E, K = 16, 256, 128, 4, 2
     m = sonicmoe.MoE(E, K, H, I, sonicmoe.ActivationType.SWIGLU, False, 0.02)
@@ -43,7 +43,4 @@ def test_training_without_a_backward_is_refused():
     with pytest.raises(NotImplementedError, match="fused_router"):
         moe_TC_softmax_topk_layer(x, m.router.weight, w1, None, w2, None, K, None, is_inference_mode_enabled=False,
                                   fused_router=True)
-    tok = torch.arange(T, dtype=torch.int32)
-    with pytest.raises(NotImplementedError, match="no backward for moe_general_routing_inputs"):
-        moe_general_routing_inputs(x, torch.ones(T), tok, tok % E, w1, None, w2, None, E, None,
-                                   is_inference_mode_enabled=False)
+

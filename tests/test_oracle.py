@@ -273,3 +273,55 @@ def test_home_rows_layout_invariants():
     r = rows[:, None]
     byte = ((r // 128) * KG + g // 4) * 512 + 16 * (r % 32) + 4 * ((r % 128) // 32) + g % 4
     assert len(np.unique(byte)) == byte.size and byte.max() < (max_rows // 128) * KG * 512
+
+
+# ---------------------------------------------------------------- backward restatement
+def test_router_backward_matches_autograd():
+    """oracle.backward.router_backward against torch autograd of the router's forward math
+    (softmax over the top-k; top-k of the softmax, optionally renormalised), float64."""
+    from oracle import backward as obwd
+
+    rs = np.random.RandomState(5)
+    T, E, K = 40, 16, 4
+    lg = rs.randn(T, E)
+    g = rs.randn(T, K)
+    idx = np.argsort(-lg, axis=1)[:, :K]
+    for sot, norm in ((True, False), (False, False), (False, True)):
+        lt = torch.tensor(lg, requires_grad=True)
+        sel = torch.gather(lt, 1, torch.from_numpy(idx))
+        if sot:
+            s = torch.softmax(sel, dim=1)
+        else:
+            p = torch.softmax(lt, dim=1)
+            s = torch.gather(p, 1, torch.from_numpy(idx))
+            if norm:
+                s = s / s.sum(1, keepdim=True)
+        (s * torch.from_numpy(g)).sum().backward()
+        got = obwd.router_backward(lg, s.detach().numpy(), idx, g, sot, norm)
+        np.testing.assert_allclose(got, lt.grad.numpy(), rtol=1e-10, atol=1e-12)
+
+
+def test_backward_general_equals_topk_form():
+    """The explicit-entries backward equals the top-k backward on the same routing."""
+    from oracle import backward as obwd
+    from oracle import quant as oq
+
+    rs = np.random.RandomState(6)
+    T, H, I, E, K = 64, 256, 128, 8, 2
+    x = (rs.randn(T, H)).astype(np.float32)
+    w1 = (rs.randn(E, 2 * I, H) * 0.02).astype(np.float32)
+    w2 = (rs.randn(E, H, I) * 0.02).astype(np.float32)
+    idx = np.stack([np.sort(rs.permutation(E)[:K]) for _ in range(T)]).astype(np.int32)
+    sc = rs.rand(T, K).astype(np.float32)
+    dout = (rs.randn(T, H) * 0.1).astype(np.float32)
+    # pre-activation of the fake-quantised operands, rows in expert-sorted order
+    xd = oq.dequant_1x128(*oq.quant_1x128(x))
+    w1d = oq.dequant_128x128(*oq.quant_128x128(w1))
+    _, _, _, s_scatter, _ = metadata.tc_metadata(idx, E)
+    f = s_scatter.astype(np.int64)
+    h = np.einsum("rh,rnh->rn", xd[f // K], w1d[idx.reshape(-1)[f]]).astype(np.float32)
+    a = obwd.fp8_backward(x, dout, w1, w2, sc, idx, h)
+    b = obwd.fp8_backward_general(x, dout, w1, w2, sc.reshape(-1), np.arange(T * K) // K, idx.reshape(-1), h)
+    for u, v in zip(a[:3], b[:3]):
+        np.testing.assert_allclose(u, v, rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(a[3].reshape(-1), b[3], rtol=1e-12, atol=1e-12)
