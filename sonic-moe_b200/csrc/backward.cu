@@ -90,36 +90,53 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int i = 0; i < 8; ++i) t4[i] = valid ? s4[i] : make_uint4(0, 0, 0, 0);
   __syncthreads();
-  // output row c = source column cb*128 + c; this thread quantises its 64 of the block's 128 rows,
-  // held in registers between the amax and the conversion
-  const int c = tid >> 1;
-  float v[64];
-  float am = 0.0f;
+  // Transpose-quantise: warp w takes the column pairs 32 (w % 2) .. + 31 (lane = pair: one 32-bit word
+  // of each row, 32 lanes on 32 different banks) over the 32 rows of quarter w / 2; the four
+  // quarters' column maxima meet in shared memory.
+  __shared__ float s_am[4][kBlockK];
+  const int warp = tid >> 5, lane = tid & 31;
+  const int cp = (warp & 1) * 32 + lane;  // column pair: columns 2 cp, 2 cp + 1
+  const int quarter = warp >> 1;
+  float v0[32], v1[32];
+  float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-  for (int r = 0; r < 64; ++r) {
-    v[r] = bf16_bits_to_f32(tile[half * 64 + r][c]);
-    am = fmaxf(am, fabsf(v[r]));
+  for (int j = 0; j < 32; ++j) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(&tile[quarter * 32 + j][2 * cp]);
+    v0[j] = __uint_as_float(w << 16);
+    v1[j] = __uint_as_float(w & 0xFFFF0000u);
+    a0 = fmaxf(a0, fabsf(v0[j]));
+    a1 = fmaxf(a1, fabsf(v1[j]));
   }
-  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-  const int e8 = scale_exp_of_amax(am);
-  const float inv = exp2_neg(e8);
-  uint8_t* dst = outq + (static_cast<long long>(cb) * kBlockK + c) * rows_pad + static_cast<long long>(mb) * kBlockM +
-                 half * 64;
+  s_am[quarter][2 * cp] = a0;
+  s_am[quarter][2 * cp + 1] = a1;
+  __syncthreads();
+  a0 = fmaxf(fmaxf(s_am[0][2 * cp], s_am[1][2 * cp]), fmaxf(s_am[2][2 * cp], s_am[3][2 * cp]));
+  a1 = fmaxf(fmaxf(s_am[0][2 * cp + 1], s_am[1][2 * cp + 1]), fmaxf(s_am[2][2 * cp + 1], s_am[3][2 * cp + 1]));
+  const int e0 = scale_exp_of_amax(a0), e1 = scale_exp_of_amax(a1);
+  const float i0 = exp2_neg(e0), i1 = exp2_neg(e1);
+  const long long col = static_cast<long long>(cb) * kBlockK + 2 * cp;
+  uint8_t* d0 = outq + col * rows_pad + static_cast<long long>(mb) * kBlockM + quarter * 32;
+  uint8_t* d1 = d0 + rows_pad;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t wd[4];
+  for (int i = 0; i < 2; ++i) {
+    uint32_t w0[4], w1[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float* q = v + 16 * i + 4 * j;
-      wd[j] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[0], inv), __fmul_rn(q[1], inv))) |
-              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[2], inv), __fmul_rn(q[3], inv))) << 16);
+    for (int k = 0; k < 4; ++k) {
+      const int j = 16 * i + 4 * k;
+      w0[k] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0[j], i0), __fmul_rn(v0[j + 1], i0))) |
+              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0[j + 2], i0), __fmul_rn(v0[j + 3], i0))) << 16);
+      w1[k] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v1[j], i1), __fmul_rn(v1[j + 1], i1))) |
+              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v1[j + 2], i1), __fmul_rn(v1[j + 3], i1))) << 16);
     }
-    reinterpret_cast<uint4*>(dst)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    reinterpret_cast<uint4*>(d0)[i] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+    reinterpret_cast<uint4*>(d1)[i] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
   }
-  if (half == 0) {
+  if (quarter == 0) {
     const long long KG = (rows_pad / kBlockK + 3) / 4;
     const long long atom = (static_cast<long long>(cb) * KG + mb / 4) * kSfAtomBytes;
-    outsf[atom + 16 * (c % 32) + 4 * (c / 32) + (mb % 4)] = static_cast<uint8_t>(e8 + 127);
+    const int c0 = 2 * cp, c1 = 2 * cp + 1;
+    outsf[atom + 16 * (c0 % 32) + 4 * (c0 / 32) + (mb % 4)] = static_cast<uint8_t>(e0 + 127);
+    outsf[atom + 16 * (c1 % 32) + 4 * (c1 / 32) + (mb % 4)] = static_cast<uint8_t>(e1 + 127);
   }
 }
 
