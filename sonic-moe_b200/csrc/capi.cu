@@ -568,9 +568,9 @@ static int moe_forward_impl(const void* x, const void* router_logits, const void
   if (e == cudaSuccess)
     e = launch_route_scatter(idx, nullptr, static_cast<int>(TK), K, kTileTokens * K, E, n_tiles, w.route.tile_counts,
                              w.off, w.s_scatter, w.s_rev, w.x_gather, st);
+  // the pack kernel also zero-fills the output rows the down projection reduces into
   if (e == cudaSuccess)
-    e = launch_quant_pack(x, T, H, idx, K, nullptr, w.s_rev, w.off, w.route.off_pad, w.xq, w.xsf, st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * H * 2, st);
+    e = launch_quant_pack(x, T, H, idx, K, nullptr, w.s_rev, w.off, w.route.off_pad, w.xq, w.xsf, st, out);
   if (e == cudaSuccess) {
     GemmArgs g = up_args(w.xq, w.xsf, w1q, w1_sf, H, I, E, concat_layout, mb, w.route.blk_expert, w.route.n_blocks,
                          w.route.off_pad, expert_frequency, w.aq, w.asf, errw);
@@ -676,8 +676,8 @@ int sm_moe_general_forward(const void* x, int T, int H, int I, int E, int TK, co
                              w.s_scatter, w.s_rev, w.x_gather, st);
   if (e == cudaSuccess) e = launch_token_offset(token_indices, T, TK, w.tok_off, st);
   if (e == cudaSuccess)
-    e = launch_quant_pack(x, T, H, expert_indices, 0, w.tok_off, w.s_rev, w.off, w.route.off_pad, w.xq, w.xsf, st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * H * 2, st);
+    e = launch_quant_pack(x, T, H, expert_indices, 0, w.tok_off, w.s_rev, w.off, w.route.off_pad, w.xq, w.xsf, st,
+                          out);
   if (e == cudaSuccess) {
     GemmArgs g = up_args(w.xq, w.xsf, w1q, w1_sf, H, I, E, concat_layout, mb, w.route.blk_expert, w.route.n_blocks,
                          w.route.off_pad, expert_frequency, w.aq, w.asf, errw);

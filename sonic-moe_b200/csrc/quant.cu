@@ -35,10 +35,15 @@ __global__ void __launch_bounds__(kQuantWarps * 32)
     quant_pack_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, const int32_t* __restrict__ experts, int K,
                       const int32_t* __restrict__ tok_off, const int32_t* __restrict__ s_rev,
                       const int32_t* __restrict__ off, const int32_t* __restrict__ off_pad, uint8_t* __restrict__ xq,
-                      uint8_t* __restrict__ xsf) {
+                      uint8_t* __restrict__ xsf, uint4* __restrict__ zero_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * kQuantWarps + warp;
   if (t >= T) return;
+  if (zero_out) {
+    // the layer's output row t, zeroed for the down projection's reductions (instead of a memset pass)
+    uint4* row = zero_out + static_cast<size_t>(t) * (H / 8);
+    for (int i = lane; i < H / 8; i += 32) row[i] = make_uint4(0, 0, 0, 0);
+  }
   int f0 = t, ncopy = 1;
   if (experts) {
     f0 = tok_off ? tok_off[t] : t * K;
@@ -159,11 +164,12 @@ __global__ void __launch_bounds__(256)
 
 cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* tok_off,
                               const int32_t* s_rev, const int32_t* off, const int32_t* off_pad, uint8_t* xq,
-                              uint8_t* xsf, cudaStream_t st) {
+                              uint8_t* xsf, cudaStream_t st, void* zero_out) {
   if (T == 0) return cudaSuccess;
   const int grid = (T + kQuantWarps - 1) / kQuantWarps;
   quant_pack_kernel<<<grid, kQuantWarps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, experts, K,
-                                                       tok_off, s_rev, off, off_pad, xq, xsf);
+                                                       tok_off, s_rev, off, off_pad, xq, xsf,
+                                                       static_cast<uint4*>(zero_out));
   return cudaGetLastError();
 }
 

@@ -59,9 +59,11 @@ cudaError_t launch_route_scatter(const int32_t* experts, const int32_t* token_of
                                  cudaStream_t st);
 cudaError_t launch_token_offset(const int32_t* sorted_tokens, int T, int TK, int32_t* offset, cudaStream_t st);
 
+// zero_out (optional): a bf16 [T, H] output whose rows the kernel zero-fills, one per token (the
+// layer output the down projection reduces into; 16-byte aligned, H % 8 == 0).
 cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* tok_off,
                               const int32_t* s_rev, const int32_t* off, const int32_t* off_pad, uint8_t* xq,
-                              uint8_t* xsf, cudaStream_t st);
+                              uint8_t* xsf, cudaStream_t st, void* zero_out = nullptr);
 cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_glu, uint8_t* wq, uint8_t* wsf,
                                cudaStream_t st);
 // backward (csrc/backward.cu)

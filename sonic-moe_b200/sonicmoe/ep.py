@@ -284,7 +284,7 @@ class ExpertParallelMoE:
     def __init__(self, router_w, w1_local, w2_local, num_experts: int, top_k: int, group=None,
                  softmax_over_topk: bool = True, norm_topk_probs: bool = False, concat_layout: bool = False,
                  stages=None, reserve_sms: int = None, transport: str = None, max_tokens: int = None,
-                 hidden_size: int = None, chunks: int = None):
+                 hidden_size: int = None, chunks: int = None, record_phases: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -323,6 +323,9 @@ class ExpertParallelMoE:
             nat.call("sm_set_gemm_sm_reserve", reserve_sms)
         self._send_buf = self._out_buf = None
         self.last_exchange = None
+        # home transport: CUDA events at the phase boundaries of every forward (read with phase_times())
+        self.record_phases = bool(record_phases)
+        self._phase_events = None
         self._streams = None
         self._copy_streams = None
         self._home_buf = None
@@ -393,6 +396,18 @@ class ExpertParallelMoE:
         if code:
             raise RuntimeError(f"expert-parallel forward failed: device error {code} "
                                f"({nat.ERR_NAMES.get(code, 'unknown code')}); its output is not valid")
+
+    def phase_times(self):
+        """Device milliseconds of the last home-transport forward's phases (with record_phases=True):
+        route + dispatch records, count exchange (all-gather and the host's read), up stage (record
+        pull + up GEMM storing into the homes), error all-reduce (the cross-rank barrier), down +
+        combine.  Waits for the forward."""
+        ev = self._phase_events
+        if ev is None:
+            return None
+        ev[-1].synchronize()
+        names = ("dispatch", "count_exchange", "up_stage", "allreduce", "down")
+        return {n: ev[i].elapsed_time(ev[i + 1]) for i, n in enumerate(names)}
 
     def check_errors(self):
         """Wait for the last forward and raise if any rank's kernels recorded an error.  Every
@@ -566,28 +581,41 @@ class ExpertParallelMoE:
         s_main = self._streams[0]
         s_main.wait_stream(caller)
         rb = self.stages.record_bytes(H, K)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)] if self.record_phases else None
+
+        def mark(i):
+            if ev is not None:
+                ev[i].record(s_main)
+
         with torch.cuda.stream(s_main):
+            mark(0)
             logits = F.linear(x, self.router_w.to(x.dtype))
             errs = torch.zeros(1, dtype=torch.int32, device=dev)
             scores, idx = ops.router_topk(logits, K, self.sot, self.norm)
             plan = ops.route_plan(idx, self.E, errs)
             records = _RawRows(self._send_buf.ptr, self._send_cap, rb)
             st = self.stages.dispatch_records(x, scores, idx, plan, self.E, W, errs, records=records)
+            mark(1)
         C, _ = self._exchange_counts(st, s_main, dev)
         with torch.cuda.stream(s_main):
+            mark(2)
             recv_counts = [C[q][me] for q in range(W)]
             seg_off = [sum(C[q][:me]) for q in range(W)]
             home_q = list(self._home_buf.peers)
             home_sf = [p + self._home_q_bytes for p in home_q]
             freq = self.stages.expert_up_p2p(self._send_buf.peers, seg_off, recv_counts, H, self.I, self.El, K,
                                              self.w1, home_q, home_sf, self._home_rows, errs, dev)
+            mark(3)
             # every rank's rows have landed in every home; MAX keeps one rank's code intact
             self._reduce_err(errs)
+            mark(4)
             out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
             aq = _RawRows(self._home_buf.ptr, self._home_rows, self.I)
             asf = _RawRows(self._home_buf.ptr + self._home_q_bytes, self._home_sf_shape[0], 1024)
             ops.moe_down_combine(aq, asf, self.w2_full, plan, scores.view(-1), T, errs, out=out)
+            mark(5)
             remote = (idx // self.El != me).sum()
+        self._phase_events = ev
         caller.wait_stream(s_main)
         for t in (logits, out, freq, remote):
             t.record_stream(caller)
