@@ -66,6 +66,14 @@ class DispatchState:
     send_counts: torch.Tensor  # [W] int32 (device)
 
 
+class _HomeRows:
+    """The parts of a routing plan a chunk's record dispatch reads: the chunk's slice of s_rev and the
+    plan's per-expert offsets (the home rows of its entries are rows of the whole plan)."""
+
+    def __init__(self, s_rev, off, off_pad):
+        self.s_rev, self.off, self.off_pad = s_rev, off, off_pad
+
+
 class _RawRows:
     """Stand-in for a [rows, width] uint8 tensor at a raw device address (an IPC buffer)."""
 
@@ -312,8 +320,6 @@ class ExpertParallelMoE:
             chunks = 6 if (transport == "copy" and self.world >= 8 and (max_tokens or 0) >= 4096) else 1
         if chunks < 1:
             raise ValueError("chunks must be >= 1")
-        if transport == "home" and chunks != 1:
-            raise ValueError("the home transport runs one chunk per forward")
         self.chunks = int(chunks)
         if stages is None:
             # SMs the persistent GEMMs leave free for the dispatch / combine kernels and NCCL that run
@@ -347,10 +353,12 @@ class ExpertParallelMoE:
             self._send_buf = IpcBuffer(self.chunks * self._send_chunk_bytes, group)
             if transport != "home":
                 self._out_buf = IpcBuffer(self.chunks * self._out_chunk_bytes, group)
-            if transport == "copy":
-                # local landing buffers: the records of every source, the partial rows of every owner
+            if transport == "copy" or (transport == "home" and self.chunks > 1):
+                # local landing buffers: the records of every source (and, copy transport, the partial
+                # rows of every owner)
                 dev = torch.device("cuda", torch.cuda.current_device())
                 self._recv_local = torch.empty(self.chunks, max(self._out_cap, 1), rb, dtype=torch.uint8, device=dev)
+            if transport == "copy":
                 self._ret_local = torch.empty(self.chunks, max(self._send_cap, 1), hidden_size, dtype=torch.bfloat16,
                                               device=dev)
         self.router_w = router_w
@@ -623,6 +631,115 @@ class ExpertParallelMoE:
         self._note_exchange_home(sum(C[q][me] for q in range(W) if q != me), remote, rb)
         return out, logits, freq
 
+    def _land_records(self, A, W, me, Cn, rb, ev_counts):
+        """Copy-engine transfers of every chunk's record segments from the peers' send regions into
+        this rank's landing buffer (one copy per (chunk, peer), on that peer's copy stream, all issued
+        after the count exchange).  Returns per chunk: the events to wait for, the record source
+        bases (own segment read in place) and their segment offsets."""
+        lib_copy = lambda dst, src, nbytes, stream: nat.call("sm_copy_d2d_async", dst, src, nbytes,  # noqa: E731
+                                                             stream.cuda_stream)
+        in_events, bases, seg_offs = [], [], []
+        for c in range(Cn):
+            evs, base, seg, landed = [], [], [], 0
+            for q in range(W):
+                n = A[q][c][me]
+                if q == me:  # this rank's own segment is read in place
+                    base.append(self._send_buf.ptr + c * self._send_chunk_bytes)
+                    seg.append(sum(A[me][c][:me]))
+                    continue
+                dst = self._recv_local[c].data_ptr() + landed * rb
+                base.append(dst)
+                seg.append(0)
+                if n > 0:
+                    cs = self._copy_streams[q]
+                    cs.wait_event(ev_counts)
+                    src = self._send_buf.peers[q] + c * self._send_chunk_bytes + sum(A[q][c][:me]) * rb
+                    lib_copy(dst, src, n * rb, cs)
+                    ev = torch.cuda.Event()
+                    ev.record(cs)
+                    evs.append(ev)
+                landed += n
+            in_events.append(evs)
+            bases.append(base)
+            seg_offs.append(seg)
+        return in_events, bases, seg_offs
+
+    def _forward_home_chunked(self, x: torch.Tensor):
+        """Home-down forward over token chunks: one routing plan of all this rank's tokens (so every
+        record's home row is global), records dispatched per chunk into the chunk's send region,
+        one count exchange for all chunks, then the records of every chunk land through copy
+        engines while the main stream runs the owner's up projection of the chunks already landed
+        (rows stored into their homes).  After all chunks: the error all-reduce (every rank's rows are
+        home) and one down projection + combine over this rank's plan."""
+        from . import ops
+
+        T, H = x.shape
+        W, K, me, Cn = self.world, self.K, self.rank, self.chunks
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the shared buffers")
+        dev = x.device
+        caller = torch.cuda.current_stream(dev)
+        if self._streams is None:
+            self._streams = (torch.cuda.Stream(dev, priority=-1), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        if self._copy_streams is None:
+            self._copy_streams = [torch.cuda.Stream(dev) for _ in range(W)]
+        s_main = self._streams[0]
+        s_main.wait_stream(caller)
+        rb = self.stages.record_bytes(H, K)
+        Tc = -(-T // Cn) if T else 0
+        spans = [(min(T, c * Tc), min(T, (c + 1) * Tc)) for c in range(Cn)]
+        with torch.cuda.stream(s_main):
+            logits = F.linear(x, self.router_w.to(x.dtype))
+            errs = torch.zeros(1, dtype=torch.int32, device=dev)
+            scores, idx = ops.router_topk(logits, K, self.sot, self.norm)
+            plan = ops.route_plan(idx, self.E, errs)
+            states = []
+            for c, (a, b) in enumerate(spans):
+                records = _RawRows(self._send_buf.ptr + c * self._send_chunk_bytes, self._send_cap, rb)
+                # the chunk's entries are entries [a K, b K) of the plan: its s_rev rows from there
+                plan_c = _HomeRows(plan.s_rev[a * K:b * K], plan.off, plan.off_pad)
+                states.append(self.stages.dispatch_records(x[a:b], scores[a:b], idx[a:b], plan_c, self.E, W, errs,
+                                                           records=records))
+            mine = torch.stack([st.send_counts for st in states]).contiguous()  # [Cn, W]
+            allc = torch.empty(W * Cn * W, dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(allc, mine.view(-1), group=self.group)
+            A = allc.view(W, Cn, W).cpu().tolist()  # A[s][c][d]: records of chunk c from s to d
+            self._raise_pending()  # the previous forward ran on this stream and has finished
+            msg = ""
+            for c in range(Cn):  # the whole matrix on every rank: the same verdict everywhere
+                msg = msg or check_count_matrix([[A[q][c][d] for d in range(W)] for q in range(W)],
+                                                self._send_cap, self._out_cap, me)
+            ev_counts = torch.cuda.Event()
+            ev_counts.record(s_main)
+        if msg:
+            raise RuntimeError(f"expert-parallel exchange aborted on every rank: {msg}")
+        in_events, bases, seg_offs = self._land_records(A, W, me, Cn, rb, ev_counts)
+        home_q = list(self._home_buf.peers)
+        home_sf = [p + self._home_q_bytes for p in home_q]
+        with torch.cuda.stream(s_main):
+            freq = torch.zeros(self.El, dtype=torch.int32, device=dev)
+            for c in range(Cn):
+                for ev in in_events[c]:
+                    s_main.wait_event(ev)
+                recv_counts = [A[q][c][me] for q in range(W)]
+                freq += self.stages.expert_up_p2p(bases[c], seg_offs[c], recv_counts, H, self.I, self.El, K, self.w1,
+                                                  home_q, home_sf, self._home_rows, errs, dev)
+            # every rank's rows have landed in every home; MAX keeps one rank's code intact
+            self._reduce_err(errs)
+            out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+            aq = _RawRows(self._home_buf.ptr, self._home_rows, self.I)
+            asf = _RawRows(self._home_buf.ptr + self._home_q_bytes, self._home_sf_shape[0], 1024)
+            ops.moe_down_combine(aq, asf, self.w2_full, plan, scores.view(-1), T, errs, out=out)
+            remote = (idx // self.El != me).sum()
+        caller.wait_stream(s_main)
+        for t in (logits, out, freq, remote):
+            t.record_stream(caller)
+        for st in states:
+            st.ret_row.record_stream(caller)
+        self._err_pending = errs
+        self._note_exchange_home(sum(A[q][c][me] for c in range(Cn) for q in range(W) if q != me), remote, rb)
+        return out, logits, freq
+
     def _forward_copy(self, x: torch.Tensor):
         """Copy-engine forward: the peer buffers of the p2p transport, but the record segments and
         the returned partial rows cross NVLink as plain device-to-device copies (one per peer
@@ -770,7 +887,7 @@ class ExpertParallelMoE:
         if self.transport == "copy":
             return self._forward_copy(x)
         if self.transport == "home":
-            return self._forward_home(x)
+            return self._forward_home(x) if self.chunks == 1 else self._forward_home_chunked(x)
         T, H = x.shape
         W, K = self.world, self.K
         if chunks is None:

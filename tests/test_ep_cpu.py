@@ -144,15 +144,15 @@ def test_check_counts():
 
 
 def test_home_transport_arguments():
-    """The home transport needs the native stages (its up stage stores into peer memory) and runs
-    one chunk per forward; both are rejected before any buffer is allocated."""
+    """The home transport needs the native stages (its up stage stores into peer memory), and sized
+    shared buffers; both are checked before any buffer is allocated."""
     from _ep_fakes import FakeStages
     from sonicmoe.ep import ExpertParallelMoE
 
     x, rw, w1, w2 = _inputs()
     with pytest.raises(ValueError, match="native stages"):
         ExpertParallelMoE(rw, w1, w2, E, K, stages=FakeStages(), transport="home")
-    with pytest.raises(ValueError, match="one chunk"):
+    with pytest.raises(ValueError, match="max_tokens and hidden_size"):
         ExpertParallelMoE(rw, w1, w2, E, K, transport="home", chunks=2)
     with pytest.raises(ValueError, match="unknown transport"):
         ExpertParallelMoE(rw, w1, w2, E, K, stages=FakeStages(), transport="bogus")

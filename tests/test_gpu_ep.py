@@ -261,7 +261,8 @@ def _nccl_worker(rank, W, port, q, T, H, I, E, K, transport, chunks):
 
 
 @pytest.mark.parametrize("transport,chunks", [("p2p", 1), ("p2p", 2), ("p2p", 3), ("copy", 1), ("copy", 2),
-                                              ("copy", 3), ("copy", 6), ("nccl", 1), ("nccl", 2), ("home", 1)])
+                                              ("copy", 3), ("copy", 6), ("nccl", 1), ("nccl", 2), ("home", 1),
+                                              ("home", 2), ("home", 3)])
 def test_ep_multi_gpu(transport, chunks):
     """W processes, one per GPU.  chunks > 1 runs the pipelined forward (dispatch, expert stage and
     combine of different token chunks on different streams); chunks=3 and 6 leave the last chunk
@@ -343,7 +344,8 @@ def _world1_worker(port, q, T, H, I, E, K, transport, chunks):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport,chunks", [("home", 1), ("p2p", 1), ("p2p", 2), ("copy", 2), ("nccl", 1)])
+@pytest.mark.parametrize("transport,chunks", [("home", 1), ("home", 2), ("home", 3), ("p2p", 1), ("p2p", 2),
+                                              ("copy", 2), ("nccl", 1)])
 def test_ep_world1_transports(transport, chunks):
     """Every transport's host orchestration on a one-rank NCCL group (runs on a one-GPU box):
     output within 1e-2 of the fake-quantised oracle, exact expert counts; for the home transport,
