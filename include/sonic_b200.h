@@ -43,6 +43,7 @@ extern "C" {
 #define SM_ERR_TIMEOUT_EPILOGUE 103
 #define SM_ERR_BAD_EXPERT 201
 #define SM_ERR_BAD_RETURN_ROW 202 /* home-down EP: an up-projection row with no valid home row */
+#define SM_ERR_BAD_COUNT 203      /* EP with device-side counts: a count outside the exchange buffers */
 
 /* Message describing the calling thread's most recent non-zero return. */
 const char* sm_last_error(void);
@@ -291,6 +292,11 @@ int sm_moe_down_combine(const uint8_t* aq, const uint8_t* asf, const uint8_t* w2
  * transposed, atoms_t [E][K/128][ceil(N/512)][512] (sm_weight_sf_bytes(E, K, N) bytes). */
 int sm_weight_prep_t(const uint8_t* wq, const uint8_t* sf_atoms, int E, int N, int K, uint8_t* wq_t,
                      uint8_t* sf_atoms_t, void* stream);
+/* sm_weight_prep and sm_weight_prep_t in one pass over the bf16 weight (a training step's new
+ * weight version): wq / sf_atoms exactly as sm_weight_prep, wq_t / sf_atoms_t exactly as
+ * sm_weight_prep_t of them. */
+int sm_weight_prep_with_t(const void* w, int E, int N, int K, int concat_glu, uint8_t* wq, uint8_t* sf_atoms,
+                          uint8_t* wq_t, uint8_t* sf_atoms_t, void* stream);
 /* Stage 2 above.  doq/dosf: dO packed like sm_quant_pack's xq/xsf; w2t: [E, I, H]; preact [T*K, 2I]
  * bf16 (expert-sorted rows, the caller's w1 column order); dh_q [max_blocks*128, 2I] + dh_sf atoms,
  * dh_bf16 [max_blocks*128, 2I], a_prime [max_blocks*128, I] (padded rows); dscores [T*K] fp32, flat
@@ -406,6 +412,20 @@ int sm_ep_expert_up_p2p(const void* const* peer_send_bases, const int32_t* seg_o
                         int concat_layout, void* const* home_q_bases, void* const* home_sf_bases,
                         long long home_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
                         int32_t* err, void* stream);
+/*
+ *   sm_ep_expert_up_home: sm_ep_expert_up_p2p with the counts left in device memory -- counts is the
+ *     all-gathered matrix counts[s * count_stride + d] (records of source s for destination d, this
+ *     rank d = me), read by the kernels, so the host never waits for the exchange and the call can
+ *     be captured in a CUDA graph.  Every grid is sized for recv_cap records (the most this rank can
+ *     receive; workspace from sm_ep_expert_workspace_bytes(recv_cap, ...)); a source's send region
+ *     holds send_cap records.  A count outside those bounds writes SM_ERR_BAD_COUNT into err and
+ *     nothing is read.
+ */
+int sm_ep_expert_up_home(const void* const* peer_send_bases, const int32_t* counts, int count_stride, int me, int W,
+                         int send_cap, int recv_cap, int H, int I, int El, int K, const uint8_t* w1q,
+                         const uint8_t* w1_sf, int concat_layout, void* const* home_q_bases,
+                         void* const* home_sf_bases, long long home_rows, int32_t* expert_frequency,
+                         void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
 
 /*
  * Device buffers shared between the processes of one node through CUDA IPC (no counterpart in the

@@ -20,7 +20,8 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as
 
 // One CTA of 256 threads per 128x128 block of the prepared weight: blockIdx = (k block, n block,
 // expert).  The e4m3 bytes are transposed through shared memory (rows 144 bytes apart: the 16-byte
-// stores of a warp's rows fall into distinct bank groups), and the block's scale byte moves from
+// stores of a warp's rows fall into distinct bank groups; the transposing reads are whole words),
+// and the block's scale byte moves from
 // atom (n block, k block) of wq to atom (k block, n block) of wq_t -- the same 128x128 block, so the
 // values are those of the forward's weight, read transposed.
 __global__ void __launch_bounds__(256)
@@ -37,20 +38,9 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int i = 0; i < 4; ++i) srow[i] = src[i];
   __syncthreads();
-  // output row k = column k of the block; this thread gathers 64 of its 128 n values, 4 at a time
-  const int k = tid >> 1;
-  uint32_t w[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int n = half * 64 + 4 * j;
-    w[j] = static_cast<uint32_t>(tile[n * kStride + k]) | (static_cast<uint32_t>(tile[(n + 1) * kStride + k]) << 8) |
-           (static_cast<uint32_t>(tile[(n + 2) * kStride + k]) << 16) |
-           (static_cast<uint32_t>(tile[(n + 3) * kStride + k]) << 24);
-  }
-  uint4* dst = reinterpret_cast<uint4*>(wqt + (static_cast<size_t>(e) * Kd + static_cast<size_t>(kb) * kBlockK + k) * N +
-                                        static_cast<size_t>(nb) * kBlockM + half * 64);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  store_tile_transposed_128<kStride>(
+      tile, wqt + (static_cast<size_t>(e) * Kd + static_cast<size_t>(kb) * kBlockK) * N + static_cast<size_t>(nb) * kBlockM,
+      static_cast<size_t>(N), tid);
   if (tid < 128) {
     // the block's scale: byte (kb % 4) of any row slot of atom (e, nb, kb / 4) of wq
     const int KG = (Kd / kBlockK + 3) / 4;
@@ -66,7 +56,7 @@ __global__ void __launch_bounds__(256)
 // rel < freq[e]; its source row is x_gather[off[e] + rel] (token rows, gathered) or p itself
 // (src_padded).  out [C, rows_pad] e4m3: out[c][p] = q(src[row(p)][c]); atoms [C/128][KG][512] with
 // KG = ceil(rows_pad / 512), one scale per (c, 128-row block).
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 5)
     tq_pack_kernel(const __nv_bfloat16* __restrict__ src, int C, int src_padded, const int32_t* __restrict__ blk_expert,
                    const int32_t* __restrict__ off_pad, const int32_t* __restrict__ off,
                    const int32_t* __restrict__ freq, const int32_t* __restrict__ x_gather,
@@ -97,15 +87,13 @@ __global__ void __launch_bounds__(256)
   const int warp = tid >> 5, lane = tid & 31;
   const int cp = (warp & 1) * 32 + lane;  // column pair: columns 2 cp, 2 cp + 1
   const int quarter = warp >> 1;
-  float v0[32], v1[32];
+  // two passes over the tile (maxima, then conversion) keep no row values in registers
   float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const uint32_t w = *reinterpret_cast<const uint32_t*>(&tile[quarter * 32 + j][2 * cp]);
-    v0[j] = __uint_as_float(w << 16);
-    v1[j] = __uint_as_float(w & 0xFFFF0000u);
-    a0 = fmaxf(a0, fabsf(v0[j]));
-    a1 = fmaxf(a1, fabsf(v1[j]));
+    a0 = fmaxf(a0, fabsf(__uint_as_float(w << 16)));
+    a1 = fmaxf(a1, fabsf(__uint_as_float(w & 0xFFFF0000u)));
   }
   s_am[quarter][2 * cp] = a0;
   s_am[quarter][2 * cp + 1] = a1;
@@ -123,10 +111,17 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int j = 16 * i + 4 * k;
-      w0[k] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0[j], i0), __fmul_rn(v0[j + 1], i0))) |
-              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0[j + 2], i0), __fmul_rn(v0[j + 3], i0))) << 16);
-      w1[k] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v1[j], i1), __fmul_rn(v1[j + 1], i1))) |
-              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v1[j + 2], i1), __fmul_rn(v1[j + 3], i1))) << 16);
+      float v0[4], v1[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(&tile[quarter * 32 + j + q][2 * cp]);
+        v0[q] = __uint_as_float(w << 16);
+        v1[q] = __uint_as_float(w & 0xFFFF0000u);
+      }
+      w0[k] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0[0], i0), __fmul_rn(v0[1], i0))) |
+              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0[2], i0), __fmul_rn(v0[3], i0))) << 16);
+      w1[k] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v1[0], i1), __fmul_rn(v1[1], i1))) |
+              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v1[2], i1), __fmul_rn(v1[3], i1))) << 16);
     }
     reinterpret_cast<uint4*>(d0)[i] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
     reinterpret_cast<uint4*>(d1)[i] = make_uint4(w1[0], w1[1], w1[2], w1[3]);

@@ -425,6 +425,18 @@ int sm_weight_prep_t(const uint8_t* wq, const uint8_t* sf_atoms, int E, int N, i
                      "weight_prep_t");
 }
 
+int sm_weight_prep_with_t(const void* w, int E, int N, int K, int concat_glu, uint8_t* wq, uint8_t* sf_atoms,
+                          uint8_t* wq_t, uint8_t* sf_atoms_t, void* stream) {
+  if (E < 1 || N <= 0 || K <= 0 || N % 128 || K % 128)
+    return fail(SM_EINVAL, "need E >= 1 and N, K multiples of 128 (E=%d N=%d K=%d)", E, N, K);
+  if (concat_glu && N % 256) return fail(SM_EINVAL, "concatenated GLU weight needs N = 2I with I %% 128 == 0");
+  if (!w || !wq || !sf_atoms || !wq_t || !sf_atoms_t) return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(w) || !aligned16(wq) || !aligned16(wq_t)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  return cuda_status(launch_weight_prep(w, E, N, K, concat_glu, wq, sf_atoms, static_cast<cudaStream_t>(stream),
+                                        wq_t, sf_atoms_t),
+                     "weight_prep_with_t");
+}
+
 int sm_moe_dact(const uint8_t* doq, const uint8_t* dosf, const uint8_t* w2t_q, const uint8_t* w2t_sf, int H, int I,
                 int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks, const int32_t* off_pad,
                 const int32_t* expert_frequency_offset, const int32_t* expert_frequency, const int32_t* s_scatter_idx,

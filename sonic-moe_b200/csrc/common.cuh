@@ -23,6 +23,7 @@ enum DevError : int {
   kErrSelfTestWait = 105,  // sm_selftest_bounded_wait: the expected give-up
   kErrBadExpert = 201,
   kErrBadReturnRow = 202,  // an up-projection row whose home rank / row lies outside the home buffers
+  kErrBadCount = 203,  // expert parallel: an exchange count read on the device lies outside the buffers
 };
 
 // A single wait never legitimately lasts more than a few milliseconds; 2 s means a bug.
@@ -276,6 +277,35 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float a, float b) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(a), "f"(b));
   return r;
+}
+
+// Transposed store of a 128 x 128 byte tile in shared memory (row r at tile + r * kStride, kStride a
+// multiple of 4): byte (r, c) goes to dst[c * ld + r].  256 threads: warp w, lane l writes output
+// rows 4l .. 4l + 3, bytes 16w .. 16w + 15 -- one 32-bit word per tile row (a warp reads 32
+// consecutive words of one row) and 4 x 4 byte blocks transposed with byte permutes.  dst and ld
+// must keep the 16-byte stores aligned (ld % 16 == 0).
+template <int kStride>
+__device__ __forceinline__ void store_tile_transposed_128(const uint8_t* tile, uint8_t* dst, size_t ld, int tid) {
+  const int lane = tid & 31, grp = tid >> 5;
+  uint32_t r[4][4];  // [output row b][tile-row quad q]
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int n = 16 * grp + 4 * q;
+    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(tile + (n + 0) * kStride + 4 * lane);
+    const uint32_t w1 = *reinterpret_cast<const uint32_t*>(tile + (n + 1) * kStride + 4 * lane);
+    const uint32_t w2 = *reinterpret_cast<const uint32_t*>(tile + (n + 2) * kStride + 4 * lane);
+    const uint32_t w3 = *reinterpret_cast<const uint32_t*>(tile + (n + 3) * kStride + 4 * lane);
+    const uint32_t t0 = __byte_perm(w0, w1, 0x5140), t1 = __byte_perm(w2, w3, 0x5140);
+    const uint32_t t2 = __byte_perm(w0, w1, 0x7362), t3 = __byte_perm(w2, w3, 0x7362);
+    r[0][q] = __byte_perm(t0, t1, 0x5410);
+    r[1][q] = __byte_perm(t0, t1, 0x7632);
+    r[2][q] = __byte_perm(t2, t3, 0x5410);
+    r[3][q] = __byte_perm(t2, t3, 0x7632);
+  }
+  uint8_t* d = dst + static_cast<size_t>(4 * lane) * ld + 16 * grp;
+#pragma unroll
+  for (int b = 0; b < 4; ++b)
+    *reinterpret_cast<uint4*>(d + static_cast<size_t>(b) * ld) = make_uint4(r[b][0], r[b][1], r[b][2], r[b][3]);
 }
 
 }  // namespace smb

@@ -32,26 +32,73 @@ __host__ __device__ constexpr int ep_meta_offset(int H) { return (H + H / kBlock
 
 constexpr int kMaxRanks = kMaxEpRanks;
 
+// The segment table of a RecordSource when it is resolved on the device from the all-gathered
+// count matrix (ep_resolve_counts_kernel): start[W] is the number of records received.
+struct RecordIndex {
+  int start[kMaxRanks + 1];
+  int seg_off[kMaxRanks];
+};
+
 // Where received record j lives: in the send buffer of source rank s (possibly another GPU's memory,
 // reached by peer loads) at record index seg_off[s] + (j - start[s]), for start[s] <= j < start[s+1].
-// A contiguous local buffer is the case W = 1, seg_off = 0.
+// A contiguous local buffer is the case W = 1, seg_off = 0.  With dev != nullptr the table is read
+// from device memory instead of the by-value arrays, and the kernels' record count is an upper bound.
 struct RecordSource {
   const uint8_t* base[kMaxRanks];
   int seg_off[kMaxRanks];
   int start[kMaxRanks + 1];
   int W;
   int rb;
+  const RecordIndex* dev;
 };
+
+__device__ __forceinline__ int rs_start(const RecordSource& rs, int s) { return rs.dev ? rs.dev->start[s] : rs.start[s]; }
+
+// records actually received: R itself for a host-resolved table, else the device table's total (<= R)
+__device__ __forceinline__ int rs_count(const RecordSource& rs, int R) { return rs.dev ? rs.dev->start[rs.W] : R; }
 
 __device__ __forceinline__ int record_src(const RecordSource& rs, int j) {
   int s = 0;
-  while (s + 1 < rs.W && j >= rs.start[s + 1]) ++s;
+  while (s + 1 < rs.W && j >= rs_start(rs, s + 1)) ++s;
   return s;
 }
 
 __device__ __forceinline__ const uint8_t* record_ptr(const RecordSource& rs, int j) {
   const int s = record_src(rs, j);
-  return rs.base[s] + static_cast<size_t>(rs.seg_off[s] + (j - rs.start[s])) * rs.rb;
+  const int seg = rs.dev ? rs.dev->seg_off[s] : rs.seg_off[s];
+  return rs.base[s] + static_cast<size_t>(seg + (j - rs_start(rs, s))) * rs.rb;
+}
+
+// One thread: this rank's segment table from counts[s * stride + d] (records of source s for
+// destination d; device memory, written by the count all-gather).  A count outside the buffers
+// (negative, a segment past send_cap records of its source, more than r_cap records in all) sets
+// SM_ERR_BAD_COUNT and leaves an empty table, so no record is read.
+__global__ void ep_resolve_counts_kernel(const int32_t* __restrict__ counts, int stride, int W, int me, int send_cap,
+                                         int r_cap, RecordIndex* __restrict__ out, int32_t* __restrict__ err) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  long long R = 0;
+  bool bad = false;
+  for (int s = 0; s < W; ++s) {
+    long long seg = 0;
+    for (int d = 0; d < me; ++d) {
+      const int c = counts[static_cast<size_t>(s) * stride + d];
+      bad = bad || c < 0;
+      seg += c;
+    }
+    const int n = counts[static_cast<size_t>(s) * stride + me];
+    bad = bad || n < 0 || seg + n > send_cap;
+    out->start[s] = static_cast<int>(bad ? 0 : R);
+    out->seg_off[s] = static_cast<int>(bad ? 0 : seg);
+    R += n;
+  }
+  bad = bad || R > r_cap;
+  if (bad) {
+    for (int s = 0; s <= W; ++s) out->start[s] = 0;
+    for (int s = 0; s < W; ++s) out->seg_off[s] = 0;
+    atomicCAS(err, 0, kErrBadCount);
+  } else {
+    out->start[W] = static_cast<int>(R);
+  }
 }
 
 // Where the partial row for this rank's send record p lives: p falls in the segment of destination
@@ -161,6 +208,11 @@ __global__ void ep_recv_unpack_kernel(const RecordSource rs, int R, int H, int K
                                       float* __restrict__ scores) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= R * K) return;
+  if (i >= rs_count(rs, R) * K) {  // past the received records: holes for the metadata passes
+    idx_local[i] = -1;
+    scores[i] = 0.0f;
+    return;
+  }
   const int j = i / K, k = i - (i / K) * K;
   const uint8_t* meta = record_ptr(rs, j) + ep_meta_offset(H);
   idx_local[i] = __ldcg(reinterpret_cast<const int32_t*>(meta) + k);
@@ -179,7 +231,7 @@ __global__ void __launch_bounds__(256)
                        int32_t* __restrict__ ret_dst) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = blockIdx.x * 8 + warp;
-  if (j >= R) return;
+  if (j >= rs_count(rs, R)) return;
   int my_dst = -1;
   if (lane < K) {
     const int f = j * K + lane;
@@ -401,14 +453,26 @@ struct HomeReturn {
   int W;
 };
 
+// The count matrix (device memory) an expert stage resolves its segment table from on the device:
+// counts[s * stride + d] records of source s for destination d; this rank is d = me; a source's
+// send region holds send_cap records.
+struct DeviceCounts {
+  const int32_t* counts;
+  int stride;
+  int me;
+  int send_cap;
+};
+
 // The expert stage: local routing metadata over the received records, the pack into the padded
 // layout, the up projection, then either the down projection with the per-record combine into
 // out_rows, or (home != nullptr) nothing more -- the up projection has returned every row to its
-// token's home rank.
+// token's home rank.  With dc, R is the capacity: every grid is sized for R records and the table
+// resolved on the device says how many arrived (no host round trip).
 static int ep_expert_forward(const RecordSource& src, int R, int H, int I, int El, int K, const uint8_t* w1q,
                              const uint8_t* w1_sf, const uint8_t* w2q, const uint8_t* w2_sf, int concat_layout,
                              void* out_rows, int32_t* expert_frequency, void* workspace, size_t workspace_bytes,
-                             int32_t* err, void* stream, const HomeReturn* home = nullptr) {
+                             int32_t* err, void* stream, const HomeReturn* home = nullptr,
+                             const DeviceCounts* dc = nullptr) {
   if (R < 0 || H <= 0 || H % 256 || I <= 0 || I % 128 || El < 1 || K < 1 || K > 32)
     return set_last_error(SM_EINVAL, "ep expert: bad shape R=%d H=%d I=%d El=%d K=%d", R, H, I, El, K);
   if (!expert_frequency || !err) return set_last_error(SM_EINVAL, "ep expert: null pointer");
@@ -439,8 +503,14 @@ static int ep_expert_forward(const RecordSource& src, int R, int H, int I, int E
   uint8_t* aq = take(static_cast<size_t>(mb) * kBlockM * I);
   uint8_t* asf = take(static_cast<size_t>(mb) * ceil_div(I, 512) * kSfAtomBytes);
   int32_t* ret_dst = reinterpret_cast<int32_t*>(take(static_cast<size_t>(mb) * kBlockM * sizeof(int32_t)));
+  RecordIndex* table = dc ? reinterpret_cast<RecordIndex*>(take(sizeof(RecordIndex))) : nullptr;
   if (used > workspace_bytes) return set_last_error(SM_EINVAL, "ep expert: workspace too small");
-  ep_recv_unpack_kernel<<<static_cast<int>((TK + 255) / 256), 256, 0, st>>>(src, R, H, K, idx, scores);
+  RecordSource rs = src;
+  if (dc) {
+    ep_resolve_counts_kernel<<<1, 32, 0, st>>>(dc->counts, dc->stride, src.W, dc->me, dc->send_cap, R, table, err);
+    rs.dev = table;
+  }
+  ep_recv_unpack_kernel<<<static_cast<int>((TK + 255) / 256), 256, 0, st>>>(rs, R, H, K, idx, scores);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && home)
     e = cudaMemsetAsync(ret_dst, 0xFF, static_cast<size_t>(mb) * kBlockM * sizeof(int32_t), st);
@@ -453,7 +523,7 @@ static int ep_expert_forward(const RecordSource& src, int R, int H, int I, int E
     e = launch_route_scatter(idx, nullptr, static_cast<int>(TK), K, kTileTokens * K, El, n_tiles, tile_counts, off,
                              s_scatter, s_rev, x_gather, st);
   if (e == cudaSuccess) {
-    ep_pack_fp8_kernel<<<(R + 7) / 8, 256, 0, st>>>(src, R, H, K, El, idx, s_rev, off, off_pad, xq, xsf,
+    ep_pack_fp8_kernel<<<(R + 7) / 8, 256, 0, st>>>(rs, R, H, K, El, idx, s_rev, off, off_pad, xq, xsf,
                                                     home ? ret_dst : nullptr);
     e = cudaGetLastError();
   }
@@ -579,6 +649,38 @@ int sm_ep_expert_up_p2p(const void* const* peer_send_bases, const int32_t* seg_o
   home.W = W;
   return ep_expert_forward(src, R, H, I, El, K, w1q, w1_sf, nullptr, nullptr, concat_layout, nullptr,
                            expert_frequency, workspace, workspace_bytes, err, stream, &home);
+}
+
+int sm_ep_expert_up_home(const void* const* peer_send_bases, const int32_t* counts, int count_stride, int me, int W,
+                         int send_cap, int recv_cap, int H, int I, int El, int K, const uint8_t* w1q,
+                         const uint8_t* w1_sf, int concat_layout, void* const* home_q_bases,
+                         void* const* home_sf_bases, long long home_rows, int32_t* expert_frequency,
+                         void* workspace, size_t workspace_bytes, int32_t* err, void* stream) {
+  if (W < 1 || W > kMaxRanks || me < 0 || me >= W || !peer_send_bases || !counts || !home_q_bases ||
+      !home_sf_bases || !err)
+    return set_last_error(SM_EINVAL, "ep expert up home: W must be in [1, %d], 0 <= me < W, pointers non-null",
+                          kMaxRanks);
+  if (count_stride < W || send_cap < 0 || recv_cap < 1 || static_cast<long long>(recv_cap) * K > (1ll << 30))
+    return set_last_error(SM_EINVAL, "ep expert up home: bad capacities (stride %d, send %d, recv %d)", count_stride,
+                          send_cap, recv_cap);
+  if (home_rows < 0 || home_rows > (1ll << kHomeShift))
+    return set_last_error(SM_EINVAL, "ep expert up home: home_rows %lld outside [0, 2^%d]", home_rows, kHomeShift);
+  RecordSource src{};
+  HomeReturn home{};
+  for (int s = 0; s < W; ++s) {
+    if (!home_q_bases[s] || !home_sf_bases[s] || reinterpret_cast<uintptr_t>(home_q_bases[s]) % 16)
+      return set_last_error(SM_EINVAL, "ep expert up home: home buffers must be non-null and 16-byte aligned");
+    src.base[s] = static_cast<const uint8_t*>(peer_send_bases[s]);
+    home.q[s] = static_cast<uint8_t*>(home_q_bases[s]);
+    home.sf[s] = static_cast<uint8_t*>(home_sf_bases[s]);
+  }
+  src.W = W;
+  src.rb = sm_ep_record_bytes(H, K);
+  home.rows = home_rows;
+  home.W = W;
+  const DeviceCounts dc{counts, count_stride, me, send_cap};
+  return ep_expert_forward(src, recv_cap, H, I, El, K, w1q, w1_sf, nullptr, nullptr, concat_layout, nullptr,
+                           expert_frequency, workspace, workspace_bytes, err, stream, &home, &dc);
 }
 
 static int ep_combine(const RowSource& rs, const int32_t* ret_row, int T, int K, int H, void* out, void* stream) {

@@ -116,10 +116,16 @@ __global__ void __launch_bounds__(kQuantWarps * 32)
 
 // One CTA per 128x128 block: blockIdx = (k block, destination n block, expert).  With concat_glu
 // the destination row blocks interleave the gate and up halves at 128-row granularity:
-// destination block 2j <- gate block j, 2j+1 <- up block j (rows I + 128j ...).
+// destination block 2j <- gate block j, 2j+1 <- up block j (rows I + 128j ...).  With wqt the same
+// e4m3 block is also written transposed ([E, Kd, N], the backward GEMMs' operand) with its scale in
+// atom (k block, n block) of wsft, through a shared-memory tile, so the transpose costs no second
+// pass over the weight.
 __global__ void __launch_bounds__(256)
     weight_prep_kernel(const __nv_bfloat16* __restrict__ w, int E, int N, int Kd, int concat_glu,
-                       uint8_t* __restrict__ wq, uint8_t* __restrict__ wsf) {
+                       uint8_t* __restrict__ wq, uint8_t* __restrict__ wsf, uint8_t* __restrict__ wqt,
+                       uint8_t* __restrict__ wsft) {
+  constexpr int kStride = 144;  // transposed copy: rows 144 bytes apart
+  __shared__ __align__(16) uint8_t tile[kBlockM * kStride];
   __shared__ float s_red[8];
   const int kb = blockIdx.x, nb = blockIdx.y, e = blockIdx.z;
   const int nbs = concat_glu ? ((nb % 2 == 0) ? nb / 2 : (N / 2) / kBlockM + nb / 2) : nb;
@@ -154,11 +160,25 @@ __global__ void __launch_bounds__(256)
               (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[2], inv), __fmul_rn(q[3], inv))) << 16);
     }
     reinterpret_cast<uint4*>(dst)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    if (wqt != nullptr)
+      *reinterpret_cast<uint4*>(tile + row * kStride + half * 64 + 16 * i) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
   if (tid < 128) {
     const int KG = (Kd / kBlockK + 3) / 4;
     const size_t atom = ((static_cast<size_t>(e) * (N / kBlockM) + nb) * KG + kb / 4) * kSfAtomBytes;
     wsf[atom + 16 * (tid >> 2) + 4 * (tid & 3) + (kb % 4)] = static_cast<uint8_t>(e8 + 127);
+  }
+  if (wqt != nullptr) {  // uniform over the block
+    __syncthreads();
+    store_tile_transposed_128<kStride>(
+        tile,
+        wqt + (static_cast<size_t>(e) * Kd + static_cast<size_t>(kb) * kBlockK) * N + static_cast<size_t>(nb) * kBlockM,
+        static_cast<size_t>(N), tid);
+    if (tid < 128) {
+      const int KGn = (N / kBlockK + 3) / 4;
+      const size_t atom = ((static_cast<size_t>(e) * (Kd / kBlockM) + kb) * KGn + nb / 4) * kSfAtomBytes;
+      wsft[atom + 16 * (tid >> 2) + 4 * (tid & 3) + (nb % 4)] = static_cast<uint8_t>(e8 + 127);
+    }
   }
 }
 
@@ -174,10 +194,11 @@ cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* expert
 }
 
 cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_glu, uint8_t* wq, uint8_t* wsf,
-                               cudaStream_t st) {
+                               cudaStream_t st, uint8_t* wqt, uint8_t* wsft) {
   if (E == 0) return cudaSuccess;
   dim3 grid(Kd / kBlockK, N / kBlockM, E);
-  weight_prep_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), E, N, Kd, concat_glu, wq, wsf);
+  weight_prep_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), E, N, Kd, concat_glu, wq, wsf, wqt,
+                                           wsft);
   return cudaGetLastError();
 }
 

@@ -64,8 +64,9 @@ cudaError_t launch_token_offset(const int32_t* sorted_tokens, int T, int TK, int
 cudaError_t launch_quant_pack(const void* x, int T, int H, const int32_t* experts, int K, const int32_t* tok_off,
                               const int32_t* s_rev, const int32_t* off, const int32_t* off_pad, uint8_t* xq,
                               uint8_t* xsf, cudaStream_t st, void* zero_out = nullptr);
+// wqt / wsft (both or neither): also the transposed e4m3 weight [E, Kd, N] and its scale atoms
 cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_glu, uint8_t* wq, uint8_t* wsf,
-                               cudaStream_t st);
+                               cudaStream_t st, uint8_t* wqt = nullptr, uint8_t* wsft = nullptr);
 // backward (csrc/backward.cu)
 cudaError_t launch_weight_t(const uint8_t* wq, const uint8_t* wsf, int E, int N, int Kd, uint8_t* wqt, uint8_t* wsft,
                             cudaStream_t st);

@@ -23,6 +23,7 @@ ERR_NAMES = {
     104: "drain wait timed out",
     201: "expert index outside [0, E)",
     202: "up-projection row without a valid home row (home-down expert parallel)",
+    203: "exchange count outside the expert-parallel buffers (device-side counts)",
 }
 
 _P = ctypes.c_void_p
@@ -87,6 +88,10 @@ SIGNATURES = {
         _I,
         [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _LL, _P, _P, _SZ, _P, _P],
     ),
+    "sm_ep_expert_up_home": (
+        _I,
+        [_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _LL, _P, _P, _SZ, _P, _P],
+    ),
     "sm_ipc_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),
     "sm_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "sm_ipc_close": (_I, [_P]),
@@ -99,6 +104,7 @@ SIGNATURES = {
     "sm_moe_up": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_moe_up_preact": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "sm_weight_prep_t": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
+    "sm_weight_prep_with_t": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "sm_moe_dact": (
         _I,
         [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P],

@@ -184,6 +184,21 @@ class NativeStages:
         )
         return freq
 
+    def expert_up_home(self, peer_send, counts, stride, me, send_cap, recv_cap, H, I, El, K, w1, home_q, home_sf,
+                       home_rows, err, device):
+        """expert_up_p2p with the all-gathered count matrix left on the device (counts: int32 device
+        tensor, counts[s * stride + d] = records of source s for destination d): every grid is sized for
+        recv_cap records and the kernels read the segment table, so the host never waits."""
+        W = len(peer_send)
+        freq = torch.empty(El, dtype=torch.int32, device=device)
+        ws = _workspace(self.lib.sm_ep_expert_workspace_bytes(recv_cap, H, I, El, K), device)
+        nat.call(
+            "sm_ep_expert_up_home", self._ptrs(peer_send), _ptr(counts), stride, me, W, send_cap, recv_cap, H, I, El,
+            K, _ptr(w1.q), _ptr(w1.sf), int(w1.concat_glu), self._ptrs(home_q), self._ptrs(home_sf), int(home_rows),
+            _ptr(freq), _ptr(ws), ws.numel(), _ptr(err), _stream(),
+        )
+        return freq
+
     def combine_p2p(self, peer_out, send_counts, recv_start, ret_row, T, K, H, device, out=None):
         if out is None:
             out = torch.empty(T, H, dtype=torch.bfloat16, device=device)
@@ -337,8 +352,10 @@ class ExpertParallelMoE:
         self._home_buf = None
         # device error word of the last forward (already reduced over the ranks with MAX), read at
         # the next forward's count exchange -- where the host waits for this stream anyway -- or
-        # by check_errors()
+        # by check_errors(); the one-chunk home transport, which never waits, uses _err_async
         self._err_pending = None
+        # (event, pinned error word) of forwards that never wait on the host, oldest first
+        self._err_async = []
         if transport in ("p2p", "copy", "home"):
             if max_tokens is None or hidden_size is None:
                 raise ValueError("the p2p transport needs max_tokens and hidden_size to size its shared buffers")
@@ -397,6 +414,7 @@ class ExpertParallelMoE:
     def _raise_pending(self):
         """Raise if the previous forward's kernels recorded an error on any rank.  The word was
         all-reduced with MAX, so every rank reads the same value and raises at the same point."""
+        self._poll_async_errors()
         pending, self._err_pending = self._err_pending, None
         if pending is None:
             return
@@ -407,8 +425,8 @@ class ExpertParallelMoE:
 
     def phase_times(self):
         """Device milliseconds of the last home-transport forward's phases (with record_phases=True):
-        route + dispatch records, count exchange (all-gather and the host's read), up stage (record
-        pull + up GEMM storing into the homes), error all-reduce (the cross-rank barrier), down +
+        route + dispatch records, count exchange (the all-gather), up stage (record pull + up GEMM
+        storing into the homes), error all-reduce (the cross-rank barrier), down +
         combine.  Waits for the forward."""
         ev = self._phase_events
         if ev is None:
@@ -417,12 +435,38 @@ class ExpertParallelMoE:
         names = ("dispatch", "count_exchange", "up_stage", "allreduce", "down")
         return {n: ev[i].elapsed_time(ev[i + 1]) for i, n in enumerate(names)}
 
+    def _push_async_error(self, errs, stream):
+        """Forwards without a host wait (home transport, one chunk): the reduced error word is copied
+        into pinned host memory on `stream` and read by a later forward (_poll_async_errors), so the
+        host does not wait for the device within a forward."""
+        host = torch.empty(errs.shape, dtype=errs.dtype, pin_memory=True)
+        host.copy_(errs, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(stream)
+        self._err_async.append((done, host))
+
+    def _poll_async_errors(self, wait: bool = False):
+        """Raise for a queued forward whose error word is non-zero.  A forward is checked when the one
+        after it has been queued too (the device is then still busy with that one, so the host rarely
+        waits), or at once with wait.  The queue has the same length on every rank at the same call, so
+        every rank raises in the same forward and no rank is left alone in a collective."""
+        keep = 0 if wait else 1
+        while len(self._err_async) > keep:
+            done, host = self._err_async.pop(0)
+            done.synchronize()
+            code = int(host.max())
+            if code:
+                self._err_async.clear()
+                raise RuntimeError(f"expert-parallel forward failed: device error {code} "
+                                   f"({nat.ERR_NAMES.get(code, 'unknown code')}); its output is not valid")
+
     def check_errors(self):
         """Wait for the last forward and raise if any rank's kernels recorded an error.  Every
-        forward also checks the one before it, so only the last forward of a run needs this call."""
+        forward also checks earlier ones, so only the last forward of a run needs this call."""
         if self._err_pending is not None and self._err_pending.is_cuda:
             torch.cuda.synchronize(self._err_pending.device)
         self._raise_pending()
+        self._poll_async_errors(wait=True)
 
     def _reduce_err(self, err):
         if self.world > 1:
@@ -570,13 +614,21 @@ class ExpertParallelMoE:
           router, top-k, this rank's routing plan over all E experts, records carrying each
           entry's row in that plan's padded layout
           count exchange (all-gather; also: every rank's records are complete, and every rank has
-                          finished the down projection that read its intermediate last forward)
-          up stage       records pulled from the peers' send buffers, up GEMM whose epilogue
-                          stores each row into its token's home intermediate (peer stores)
+                          finished the down projection that read its intermediate last forward);
+                          the matrix stays in device memory
+          up stage       segment table resolved on the device from that matrix, records pulled from
+                          the peers' send buffers, up GEMM whose epilogue stores each row into its
+                          token's home intermediate (peer stores); grids sized for the most records
+                          a rank can receive
           all-reduce     of the error word: every rank's rows have landed in every home
           down stage     down GEMM + top-k combine over this rank's own plan, replicated w2
+
+        The host never waits for the device: the error word reaches pinned memory asynchronously and
+        a later forward (or check_errors()) raises for it.
         """
         from . import ops
+
+        self._poll_async_errors()
 
         T, H = x.shape
         W, K, me = self.world, self.K, self.rank
@@ -604,15 +656,18 @@ class ExpertParallelMoE:
             records = _RawRows(self._send_buf.ptr, self._send_cap, rb)
             st = self.stages.dispatch_records(x, scores, idx, plan, self.E, W, errs, records=records)
             mark(1)
-        C, _ = self._exchange_counts(st, s_main, dev)
-        with torch.cuda.stream(s_main):
+            # the count matrix stays on the device: the up stage's kernels read it (no host round trip)
+            allc = torch.empty(W * W, dtype=torch.int32, device=dev)
+            if W > 1:
+                dist.all_gather_into_tensor(allc, st.send_counts, group=self.group)
+            else:
+                allc.copy_(st.send_counts)
             mark(2)
-            recv_counts = [C[q][me] for q in range(W)]
-            seg_off = [sum(C[q][:me]) for q in range(W)]
             home_q = list(self._home_buf.peers)
             home_sf = [p + self._home_q_bytes for p in home_q]
-            freq = self.stages.expert_up_p2p(self._send_buf.peers, seg_off, recv_counts, H, self.I, self.El, K,
-                                             self.w1, home_q, home_sf, self._home_rows, errs, dev)
+            freq = self.stages.expert_up_home(self._send_buf.peers, allc, W, me, self._send_cap, self._out_cap, H,
+                                              self.I, self.El, K, self.w1, home_q, home_sf, self._home_rows, errs,
+                                              dev)
             mark(3)
             # every rank's rows have landed in every home; MAX keeps one rank's code intact
             self._reduce_err(errs)
@@ -623,12 +678,14 @@ class ExpertParallelMoE:
             ops.moe_down_combine(aq, asf, self.w2_full, plan, scores.view(-1), T, errs, out=out)
             mark(5)
             remote = (idx // self.El != me).sum()
+            cm = allc.view(W, W)
+            records_in_remote = cm[:, me].sum() - cm[me, me]
+            self._push_async_error(errs, s_main)
         self._phase_events = ev
         caller.wait_stream(s_main)
-        for t in (logits, out, freq, remote):
+        for t in (logits, out, freq, remote, records_in_remote):
             t.record_stream(caller)
-        self._err_pending = errs
-        self._note_exchange_home(sum(C[q][me] for q in range(W) if q != me), remote, rb)
+        self._note_exchange_home(records_in_remote, remote, rb)
         return out, logits, freq
 
     def _land_records(self, A, W, me, Cn, rb, ev_counts):

@@ -80,12 +80,14 @@ def _storage_owner(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
-def prepare_fp8_weights(w, concat_glu: bool = False) -> Fp8ExpertWeights:
+def prepare_fp8_weights(w, concat_glu: bool = False, with_t: bool = False) -> Fp8ExpertWeights:
     """e4m3 + 128x128 UE8M0 version of an expert weight given in the reference's (N, K, E) view.
 
     Cached on the tensor that owns the weight's storage, for its current (data pointer, version
     counter, shape, strides, layout): repeated forwards with unchanged weights quantise once, an
     in-place update or a storage swap re-quantises, and the entry is dropped with the tensor.
+    with_t (training): the result also holds the transposed copy the backward reads (prepared in the
+    same pass over the weight, or added to a cached entry that lacks it).
     """
     if isinstance(w, Fp8ExpertWeights):
         return w
@@ -97,9 +99,11 @@ def prepare_fp8_weights(w, concat_glu: bool = False) -> Fp8ExpertWeights:
     if per_owner is not None:
         hit = per_owner.get(layout)
         if hit is not None and hit[0] == state:
+            if with_t and hit[1].t is None:
+                hit[1].t = ops.weight_prep_t(hit[1])
             return hit[1]
     with torch.no_grad():
-        prepared = ops.weight_prep(_as_expert_major(w.detach()), concat_glu=concat_glu)
+        prepared = ops.weight_prep(_as_expert_major(w.detach()), concat_glu=concat_glu, with_t=with_t)
     if per_owner is None:
         key = id(owner)
         ref = weakref.ref(owner, lambda r, k=key: _forget(k, r))
@@ -139,8 +143,8 @@ class _FP8MoEFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, router_logits, w1, w2, K, softmax_over_topk, norm_topk_probs, concat_layout):
-        w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
-        w2q = prepare_fp8_weights(w2, concat_glu=False)
+        w1q = prepare_fp8_weights(w1, concat_glu=concat_layout, with_t=True)
+        w2q = prepare_fp8_weights(w2, concat_glu=False, with_t=True)
         T, H = x.shape
         E = router_logits.shape[1]
         I = w1q.shape[1] // 2
@@ -256,8 +260,8 @@ class _FP8MoEGeneralFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, router_scores, token_indices, expert_indices, w1, w2, concat_layout):
-        w1q = prepare_fp8_weights(w1, concat_glu=concat_layout)
-        w2q = prepare_fp8_weights(w2, concat_glu=False)
+        w1q = prepare_fp8_weights(w1, concat_glu=concat_layout, with_t=True)
+        w2q = prepare_fp8_weights(w2, concat_glu=False, with_t=True)
         T, H = x.shape
         E = w2q.shape[0]
         I = w2q.shape[2]

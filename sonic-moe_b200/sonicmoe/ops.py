@@ -164,20 +164,24 @@ class Fp8ExpertWeights:
     """e4m3 expert weights + 128x128 UE8M0 scale atoms, as produced by ``weight_prep``.
 
     ``q``: [E, N, K] uint8 (e4m3 bits); ``sf``: [E, N/128, ceil(K/512), 512] uint8;
-    ``concat_glu``: the rows were re-blocked from a concatenated [gate; up] layout.
+    ``concat_glu``: the rows were re-blocked from a concatenated [gate; up] layout;
+    ``t``: the same weight transposed for the backward GEMMs (``weight_prep_t``), when it was
+    prepared alongside.
     """
 
     q: torch.Tensor
     sf: torch.Tensor
     concat_glu: bool
+    t: "Fp8ExpertWeights" = None
 
     @property
     def shape(self):
         return tuple(self.q.shape)
 
 
-def weight_prep(w: torch.Tensor, concat_glu: bool = False) -> Fp8ExpertWeights:
-    """Quantise expert weights [E, N, K] (bf16) to e4m3 with 128x128 UE8M0 scales."""
+def weight_prep(w: torch.Tensor, concat_glu: bool = False, with_t: bool = False) -> Fp8ExpertWeights:
+    """Quantise expert weights [E, N, K] (bf16) to e4m3 with 128x128 UE8M0 scales; with_t also
+    writes the transposed copy the backward uses (``.t``, as ``weight_prep_t`` would), in the same pass."""
     if w.dtype != torch.bfloat16:
         w = w.to(torch.bfloat16)
     w = w.contiguous()
@@ -185,8 +189,14 @@ def weight_prep(w: torch.Tensor, concat_glu: bool = False) -> Fp8ExpertWeights:
     E, N, K = w.shape
     q = torch.empty(E, N, K, dtype=torch.uint8, device=w.device)
     sf = torch.zeros(E, N // _BLOCK_M, -(-(K // 128) // 4), 512, dtype=torch.uint8, device=w.device)
-    nat.call("sm_weight_prep", _ptr(w), E, N, K, int(concat_glu), _ptr(q), _ptr(sf), _stream())
-    return Fp8ExpertWeights(q, sf, bool(concat_glu))
+    if not with_t:
+        nat.call("sm_weight_prep", _ptr(w), E, N, K, int(concat_glu), _ptr(q), _ptr(sf), _stream())
+        return Fp8ExpertWeights(q, sf, bool(concat_glu))
+    qt = torch.empty(E, K, N, dtype=torch.uint8, device=w.device)
+    sft = torch.zeros(E, K // _BLOCK_M, -(-(N // 128) // 4), 512, dtype=torch.uint8, device=w.device)
+    nat.call("sm_weight_prep_with_t", _ptr(w), E, N, K, int(concat_glu), _ptr(q), _ptr(sf), _ptr(qt), _ptr(sft),
+             _stream())
+    return Fp8ExpertWeights(q, sf, bool(concat_glu), Fp8ExpertWeights(qt, sft, False))
 
 
 def max_padded_blocks(TK: int, E: int) -> int:
@@ -447,7 +457,10 @@ def moe_general_forward(
 def weight_prep_t(w: Fp8ExpertWeights) -> Fp8ExpertWeights:
     """W^T as a backward GEMM's K-major operand, from the forward's prepared weight: e4m3 [E, N, K] ->
     [E, K, N], the same values and 128x128 block scales read transposed (for a concatenated w1 the K
-    order is the prepared weight's re-blocked row order)."""
+    order is the prepared weight's re-blocked row order).  A weight prepared with ``with_t`` returns
+    the copy it already holds."""
+    if w.t is not None:
+        return w.t
     E, N, K = w.shape
     q = torch.empty(E, K, N, dtype=torch.uint8, device=w.q.device)
     sf = torch.zeros(E, K // _BLOCK_M, -(-(N // 128) // 4), 512, dtype=torch.uint8, device=w.q.device)

@@ -186,3 +186,35 @@ def test_check_count_matrix_same_verdict_on_every_rank():
     over = [[3, 9], [5, 9]]  # rank 1 receives 18 records, more than its output region of 12
     assert "exceed the output region" in check_count_matrix(over, 20, 12, 1)
     assert "peer rank (1)" in check_count_matrix(over, 20, 12, 0)
+
+
+def test_async_error_words_raise_two_forwards_later_on_every_rank():
+    """Forwards that never wait on the host queue their reduced error word; forward n checks forward
+    n - 2 (a fixed point, identical on every rank, since the words are MAX-reduced), check_errors()
+    checks everything left.  Events are stand-ins here (the host logic only)."""
+    from sonicmoe.ep import ExpertParallelMoE
+
+    class _Done:
+        def synchronize(self):
+            pass
+
+    moe = object.__new__(ExpertParallelMoE)
+    moe._err_async = []
+    words = [0, 0, 202, 0]
+    raised_at = None
+    for n, code in enumerate(words):
+        try:
+            moe._poll_async_errors()  # the start of forward n
+        except RuntimeError as e:
+            raised_at = n
+            assert "device error 202" in str(e)
+        moe._err_async.append((_Done(), torch.tensor([code], dtype=torch.int32)))  # forward n's word
+    assert raised_at is None  # forward 2's word is read at the start of forward 4
+    with pytest.raises(RuntimeError, match="device error 202"):
+        moe._poll_async_errors()
+    assert moe._err_async == []
+    moe._err_async.append((_Done(), torch.tensor([0], dtype=torch.int32)))
+    moe._err_async.append((_Done(), torch.tensor([203], dtype=torch.int32)))
+    moe._poll_async_errors()  # the newest stays queued
+    with pytest.raises(RuntimeError, match="device error 203"):
+        moe._poll_async_errors(wait=True)

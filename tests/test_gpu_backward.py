@@ -101,6 +101,57 @@ def test_weight_prep_t_is_the_transpose(ops):
                 assert atoms[e, kb, nb // 4, nb % 4] == sf[e, nb, kb]
 
 
+@pytest.mark.parametrize("concat", [False, True])
+def test_weight_prep_with_t_matches_the_two_passes(ops, concat):
+    """The one-pass preparation (forward weight + transposed copy) writes exactly what weight_prep
+    followed by weight_prep_t writes, in both w1 layouts."""
+    g = torch.Generator().manual_seed(6)
+    w = (torch.randn(3, 512, 384, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    both = ops.weight_prep(w, concat_glu=concat, with_t=True)
+    one = ops.weight_prep(w, concat_glu=concat)
+    t = ops.weight_prep_t(one)
+    assert ops.weight_prep_t(both) is both.t
+    for a, b in ((both.q, one.q), (both.sf, one.sf), (both.t.q, t.q), (both.t.sf, t.sf)):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("padded", [False, True])
+@pytest.mark.parametrize("T,C,E,K", [(300, 512, 8, 2), (200, 384, 64, 8)])
+def test_tq_pack_bit_exact(ops, T, C, E, K, padded):
+    """The weight-gradient operand: column c of the padded layout's rows (token rows gathered, or the
+    padded rows themselves with pad rows read as zero) quantised in 1x128 groups along the rows, bytes
+    and scale atoms equal to the oracle quantiser's on the transposed matrix."""
+    from oracle import metadata as ometa
+    from oracle import quant as oq
+
+    g = torch.Generator().manual_seed(T + C)
+    lg = torch.randn(T, E, generator=g).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _, idx = ops.router_topk(lg.cuda(), K)
+    plan = ops.route_plan(idx, E, err)
+    i_np = idx.cpu().numpy()
+    freq, off, _, _, s_rev = ometa.tc_metadata(i_np, E)
+    off_pad, _, nblk = ometa.padded_layout(freq)
+    prow = ometa.padded_rows(i_np, s_rev, off, off_pad)
+    rows = plan.max_blocks * 128
+    P = np.zeros((nblk * 128, C), dtype=np.float32)
+    if padded:
+        src = (torch.randn(rows, C, generator=g) * 3).to(torch.bfloat16)
+        P[prow] = src.float().numpy()[prow]
+    else:
+        src = (torch.randn(T, C, generator=g) * 3).to(torch.bfloat16)
+        P[prow] = src.float().numpy()[np.arange(T * K) // K]
+    q, sf = ops.tq_pack(src.cuda(), plan, padded)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    q_ref, e8_ref = oq.quant_1x128(P.T.copy())  # [C, nblk*128], [C, nblk]
+    np.testing.assert_array_equal(q.cpu().numpy()[:, :nblk * 128], q_ref)
+    atoms = sf.cpu().numpy()
+    kg = -(-nblk // 4)
+    np.testing.assert_array_equal(atoms[:, :kg], oq.act_sf_atoms(e8_ref))
+    assert not atoms[:, kg:].any()
+
+
 @pytest.mark.parametrize("T,H,I,E,K,sot,norm,concat", CASES[:2])
 def test_layer_autograd_vs_oracle(T, H, I, E, K, sot, norm, concat):
     """moe_TC_softmax_topk_layer in training mode: gradients of x (expert path + router F.linear),

@@ -125,10 +125,13 @@ def _gpu_layer_inputs(T, H, I, E, seed):
     return x, rw, w1, w2
 
 
-def _home_emulated(W, T, H, I, E, K, seed, corrupt=False, inputs=make_layer_inputs):
+def _home_emulated(W, T, H, I, E, K, seed, corrupt=False, inputs=make_layer_inputs, device_counts=False,
+                   bad_count=False):
     """Home-down stages with W virtual ranks on one GPU: every owner's up GEMM stores its rows into
     the W separate home buffers (the peer-store address arithmetic), then every home runs the down
-    projection over its own plan with all experts' w2."""
+    projection over its own plan with all experts' w2.  With device_counts the owners' up stages
+    read the count matrix from device memory (sm_ep_expert_up_home, grids sized for W * T records);
+    bad_count plants a count past the send region there."""
     import torch.nn.functional as F
 
     from sonicmoe import ops
@@ -162,9 +165,17 @@ def _home_emulated(W, T, H, I, E, K, seed, corrupt=False, inputs=make_layer_inpu
         row = send[0][0, meta:meta + 4 * K].view(torch.int32)
         row[:] = torch.where(row >= 0, torch.full_like(row, home_rows + 5), row)
     w2_full = weight_prep(w2.to(dev))
+    counts = torch.stack([s_.send_counts for s_ in states]).view(-1).contiguous()  # [W * W], row = source
+    if bad_count:
+        counts[W - 1] = T * min(K, W) + 1  # source 0's segment for the last rank runs past its send region
     freqs = []
     for d in range(W):
         w1p = weight_prep(w1[d * El:(d + 1) * El].to(dev))
+        if device_counts:
+            freqs.append(st.expert_up_home([b.data_ptr() for b in send], counts, W, d, T * min(K, W), W * T, H, I,
+                                           El, K, w1p, [q.data_ptr() for q in home_q],
+                                           [f.data_ptr() for f in home_sf], home_rows, err, dev))
+            continue
         recv_counts = [C[s_][d] for s_ in range(W)]
         seg_off = [sum(C[s_][:d]) for s_ in range(W)]
         freqs.append(st.expert_up_p2p([b.data_ptr() for b in send], seg_off, recv_counts, H, I, El, K, w1p,
@@ -181,10 +192,13 @@ def _home_emulated(W, T, H, I, E, K, seed, corrupt=False, inputs=make_layer_inpu
 
 @pytest.mark.parametrize("W,T,H,I,E,K", [(4, 200, 512, 256, 16, 4), (3, 150, 256, 128, 12, 8),
                                          (2, 333, 256, 384, 8, 8)])
-def test_ep_home_kernels_emulated_ranks(W, T, H, I, E, K):
+@pytest.mark.parametrize("device_counts", [False, True])
+def test_ep_home_kernels_emulated_ranks(W, T, H, I, E, K, device_counts):
     """Up projection at the experts' owners with its rows stored into the tokens' home buffers,
-    down projection + combine at home: same output as the single-GPU layer's oracle."""
-    x, w1, w2, o_all, logits, freq, e = _home_emulated(W, T, H, I, E, K, seed=5 * W + T)
+    down projection + combine at home: same output as the single-GPU layer's oracle, with the
+    segment table passed from the host or resolved on the device from the count matrix."""
+    x, w1, w2, o_all, logits, freq, e = _home_emulated(W, T, H, I, E, K, seed=5 * W + T,
+                                                       device_counts=device_counts)
     assert e == 0
     o_ref, _, idx = fp8_oracle(x.float().numpy(), logits.float().cpu().numpy(), w1.float().numpy(),
                                w2.float().numpy(), K)
@@ -217,6 +231,13 @@ def test_ep_home_bad_return_row_is_reported():
     writes error 202 instead of storing outside the buffer."""
     *_, e = _home_emulated(2, 64, 256, 128, 8, 4, seed=9, corrupt=True)
     assert e == 202
+
+
+def test_ep_home_device_count_out_of_range_is_reported():
+    """A count in the device-side matrix whose segment runs past the source's send region: the
+    owner's table is left empty (no record is read) and error 203 is written."""
+    *_, e = _home_emulated(3, 64, 256, 128, 12, 4, seed=10, device_counts=True, bad_count=True)
+    assert e == 203
 
 
 def _free_port():

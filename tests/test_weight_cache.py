@@ -14,7 +14,7 @@ def _with_counting_prep(monkeypatch):
 
     calls = []
 
-    def fake_prep(w, concat_glu=False):
+    def fake_prep(w, concat_glu=False, with_t=False):
         calls.append((w.data_ptr(), concat_glu))
         return ("prepared", len(calls))
 
