@@ -56,56 +56,68 @@ __global__ void __launch_bounds__(256)
 // rel < freq[e]; its source row is x_gather[off[e] + rel] (token rows, gathered) or p itself
 // (src_padded).  out [C, rows_pad] e4m3: out[c][p] = q(src[row(p)][c]); atoms [C/128][KG][512] with
 // KG = ceil(rows_pad / 512), one scale per (c, 128-row block).
-__global__ void __launch_bounds__(256, 5)
+//
+// Access pattern (the kernel is bound by L1 / shared-memory wavefronts, not DRAM, unless every warp
+// instruction touches few cache lines): the tile is loaded 16 lanes per source row (two 256-byte row
+// slices per warp instruction); warp w then owns the 16 columns of column pairs 8w .. 8w + 7 over
+// all 128 rows -- lane l reads pair 8w + l / 4 in the 32 rows of quarter l % 4 -- so a column's
+// maximum is a 4-lane shuffle and each output store instruction fills 8 cache lines with 4 lanes
+// each.  The tile's 32-bit words are XOR-swizzled by quarter (word ^ 8 q) so that the four quarters
+// of one column pair fall into different banks.
+constexpr int kTqStride = kBlockK / 2 + 4;  // tile row: 64 words of bf16 pairs + 4 words of padding
+
+__device__ __forceinline__ int tq_word(int row, int w) { return row * kTqStride + (w ^ ((row >> 5) << 3)); }
+
+__global__ void __launch_bounds__(256)
     tq_pack_kernel(const __nv_bfloat16* __restrict__ src, int C, int src_padded, const int32_t* __restrict__ blk_expert,
                    const int32_t* __restrict__ off_pad, const int32_t* __restrict__ off,
                    const int32_t* __restrict__ freq, const int32_t* __restrict__ x_gather,
                    const int32_t* __restrict__ n_blocks, long long rows_pad, uint8_t* __restrict__ outq,
                    uint8_t* __restrict__ outsf) {
-  // rows 272 bytes apart: 16-byte aligned for the vector stores, four banks apart from row to row
-  constexpr int kStride = kBlockK + 8;
-  __shared__ __align__(16) uint16_t tile[kBlockM][kStride];
+  __shared__ __align__(16) uint32_t tile[kBlockM * kTqStride];
+  __shared__ int s_row[kBlockM];  // source row of each padded row, -1 = padding
   const int mb = blockIdx.x, cb = blockIdx.y;
   if (mb >= *n_blocks) return;  // blocks past the layout are never read
   const int tid = threadIdx.x;
-  const int row = tid >> 1, half = tid & 1;
-  const int e = blk_expert[mb];
-  const int p = mb * kBlockM + row;
-  const int rel = p - off_pad[e];
-  const bool valid = rel < freq[e];
-  const long long srow = src_padded ? static_cast<long long>(p) : (valid ? x_gather[off[e] + rel] : 0);
-  const uint4* s4 =
-      reinterpret_cast<const uint4*>(src + srow * static_cast<long long>(C) + static_cast<long long>(cb) * kBlockK + half * 64);
-  uint4* t4 = reinterpret_cast<uint4*>(&tile[row][half * 64]);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) t4[i] = valid ? s4[i] : make_uint4(0, 0, 0, 0);
+  if (tid < kBlockM) {
+    const int e = blk_expert[mb];
+    const int p = mb * kBlockM + tid;
+    const int rel = p - off_pad[e];
+    s_row[tid] = rel < freq[e] ? (src_padded ? p : x_gather[off[e] + rel]) : -1;
+  }
   __syncthreads();
-  // Transpose-quantise: warp w takes the column pairs 32 (w % 2) .. + 31 (lane = pair: one 32-bit word
-  // of each row, 32 lanes on 32 different banks) over the 32 rows of quarter w / 2; the four
-  // quarters' column maxima meet in shared memory.
-  __shared__ float s_am[4][kBlockK];
+  // load: chunk k = 16-byte piece k % 16 of row k / 16 (8 chunks per thread)
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int k = i * 256 + tid;
+    const int r = k >> 4, c16 = k & 15;
+    const int sr = s_row[r];
+    const uint4 v = sr >= 0 ? *reinterpret_cast<const uint4*>(src + static_cast<size_t>(sr) * C + cb * kBlockK + 8 * c16)
+                            : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(&tile[tq_word(r, 4 * c16)]) = v;
+  }
+  __syncthreads();
   const int warp = tid >> 5, lane = tid & 31;
-  const int cp = (warp & 1) * 32 + lane;  // column pair: columns 2 cp, 2 cp + 1
-  const int quarter = warp >> 1;
-  // two passes over the tile (maxima, then conversion) keep no row values in registers
+  const int q = lane & 3;                   // row quarter: rows 32 q .. 32 q + 31
+  const int cp = 8 * warp + (lane >> 2);    // column pair: columns 2 cp, 2 cp + 1
   float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(&tile[quarter * 32 + j][2 * cp]);
+    const uint32_t w = tile[tq_word(32 * q + j, cp)];
     a0 = fmaxf(a0, fabsf(__uint_as_float(w << 16)));
     a1 = fmaxf(a1, fabsf(__uint_as_float(w & 0xFFFF0000u)));
   }
-  s_am[quarter][2 * cp] = a0;
-  s_am[quarter][2 * cp + 1] = a1;
-  __syncthreads();
-  a0 = fmaxf(fmaxf(s_am[0][2 * cp], s_am[1][2 * cp]), fmaxf(s_am[2][2 * cp], s_am[3][2 * cp]));
-  a1 = fmaxf(fmaxf(s_am[0][2 * cp + 1], s_am[1][2 * cp + 1]), fmaxf(s_am[2][2 * cp + 1], s_am[3][2 * cp + 1]));
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    a0 = fmaxf(a0, __shfl_xor_sync(0xffffffffu, a0, o));
+    a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, o));
+  }
   const int e0 = scale_exp_of_amax(a0), e1 = scale_exp_of_amax(a1);
   const float i0 = exp2_neg(e0), i1 = exp2_neg(e1);
   const long long col = static_cast<long long>(cb) * kBlockK + 2 * cp;
-  uint8_t* d0 = outq + col * rows_pad + static_cast<long long>(mb) * kBlockM + quarter * 32;
+  uint8_t* d0 = outq + col * rows_pad + static_cast<long long>(mb) * kBlockM + 32 * q;
   uint8_t* d1 = d0 + rows_pad;
-#pragma unroll
+#pragma unroll 1
   for (int i = 0; i < 2; ++i) {
     uint32_t w0[4], w1[4];
 #pragma unroll
@@ -113,10 +125,10 @@ __global__ void __launch_bounds__(256, 5)
       const int j = 16 * i + 4 * k;
       float v0[4], v1[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(&tile[quarter * 32 + j + q][2 * cp]);
-        v0[q] = __uint_as_float(w << 16);
-        v1[q] = __uint_as_float(w & 0xFFFF0000u);
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t w = tile[tq_word(32 * q + j + t, cp)];
+        v0[t] = __uint_as_float(w << 16);
+        v1[t] = __uint_as_float(w & 0xFFFF0000u);
       }
       w0[k] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0[0], i0), __fmul_rn(v0[1], i0))) |
               (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0[2], i0), __fmul_rn(v0[3], i0))) << 16);
@@ -126,7 +138,7 @@ __global__ void __launch_bounds__(256, 5)
     reinterpret_cast<uint4*>(d0)[i] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
     reinterpret_cast<uint4*>(d1)[i] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
   }
-  if (quarter == 0) {
+  if (q == 0) {
     const long long KG = (rows_pad / kBlockK + 3) / 4;
     const long long atom = (static_cast<long long>(cb) * KG + mb / 4) * kSfAtomBytes;
     const int c0 = 2 * cp, c1 = 2 * cp + 1;
