@@ -319,7 +319,7 @@ def run_train(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    T, H, I, E, K = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["K"]
+    T, H, I, E, K = args.tokens, CFG["H"], CFG["I"], CFG["E"], CFG["K"]  # --tokens: smaller profiling cases
     g = torch.Generator(device=dev).manual_seed(1111)
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16).requires_grad_()
     rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16).requires_grad_()
@@ -352,7 +352,8 @@ def run_train(args):
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    print(json.dumps({"workload": "config 2 training step (forward + FP8 backward), one GPU", "T": T, "H": H, "I": I,
+    name = "config 2" if T == CFG["T"] else f"config 2 shapes at T={T}"
+    print(json.dumps({"workload": f"{name} training step (forward + FP8 backward), one GPU", "T": T, "H": H, "I": I,
                       "E": E, "K": K, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
                       "tflops": 18.0 * T * K * H * I / (ms / 1e3) / 1e12, "steps": args.steps,
                       "clocks": clk.summary()}))
@@ -695,11 +696,16 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
             "config": dict(config, parallelism=f"ep{world}", experts_per_rank=E // world,
-                           timing="eager steps (host reads record counts), CUDA events, max over ranks"),
+                           timing=("eager steps (no host wait: device-side record counts)"
+                                   if res["transport"] == "home" and res["chunks"] == 1 else
+                                   "eager steps (host reads record counts)") + ", CUDA events, max over ranks"),
             # per chunk: dispatch 6 kernels, expert stage 7, combine 1 (router logits are cuBLAS); home
-            # transport per forward: top-k 1, routing plan 3, records 5, up stage 6, down 1
+            # transport per forward: top-k 1, routing plan 3, then per chunk records 5 and up stage 6
+            # (one chunk: 7, with the device-side count resolve), down 1
             "tflops_per_gpu": res["tflops_per_gpu"],
-            "gpu_launches": (16 if res["transport"] == "home" else 14 * res["chunks"]) * args.steps,
+            "gpu_launches": (17 if res["transport"] == "home" and res["chunks"] == 1 else
+                             5 + 11 * res["chunks"] if res["transport"] == "home" else
+                             14 * res["chunks"]) * args.steps,
             "e2e": {"value": world * T / (e2e["ms_step"] / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]},
             "clocks": res["clocks"],

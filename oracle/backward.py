@@ -9,7 +9,7 @@ quantises them:
   ``backward.py:211-278``; ``W2q`` the forward's 128x128-block e4m3 weight)
 * ``a = silu(g) u`` from the bf16 pre-activation ``h``, ``dS[r] = <dA'[r], a>``,
   ``a'[r] = s_r a``, ``dg = s_r dA' u silu'(g)``, ``du = s_r dA' silu(g)``
-* ``dx[t] = sum_k q1x128(dH)[r] W1q[e_r]``    (``gemm`` + ``token_broadcast_backward``,
+* ``dx[t] = sum_k q1x128(bf16(dH))[r] W1q[e_r]``    (``gemm`` + ``token_broadcast_backward``,
   ``backward.py:173-206, 281-305``)
 * ``dW2[e] = qcol(dO rows)^T qcol(a')``, ``dW1[e] = qcol(dH)^T qcol(x rows)`` over the expert's rows
   of the padded layout, ``qcol`` = one UE8M0 scale per 128 consecutive padded rows of a column, the
@@ -85,7 +85,7 @@ def _fp8_backward_entries(x, dout, w1, w2, tok, e, s, meta, h, concat_layout):
     else:
         dh[:, 0::2], dh[:, 1::2] = dg, du
     a_prime = s[:, None] * a
-    dhq = _q1x128(dh)
+    dhq = _q1x128(_bf16(dh))  # the dX GEMM's e4m3 dH is quantised from the bf16 dH
     dx = np.zeros((T, H))
     for ex in np.unique(e):
         r = np.nonzero(e == ex)[0]

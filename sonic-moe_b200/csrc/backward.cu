@@ -19,26 +19,26 @@ namespace smb {
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
 
 // One CTA of 256 threads per 128x128 block of the prepared weight: blockIdx = (k block, n block,
-// expert).  The e4m3 bytes are transposed through shared memory (rows 144 bytes apart: the 16-byte
-// stores of a warp's rows fall into distinct bank groups; the transposing reads are whole words),
-// and the block's scale byte moves from
+// expert).  The e4m3 bytes are transposed through a shared-memory tile (tt_chunk layout; loaded 8
+// lanes per 128-byte row, stored 8 lanes per output row), and the block's scale byte moves from
 // atom (n block, k block) of wq to atom (k block, n block) of wq_t -- the same 128x128 block, so the
 // values are those of the forward's weight, read transposed.
 __global__ void __launch_bounds__(256)
     weight_t_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wsf, int N, int Kd,
                     uint8_t* __restrict__ wqt, uint8_t* __restrict__ wsft) {
-  constexpr int kStride = 144;
-  __shared__ __align__(16) uint8_t tile[kBlockM * kStride];
+  __shared__ __align__(16) uint8_t tile[kBlockM * kTtStride];
   const int kb = blockIdx.x, nb = blockIdx.y, e = blockIdx.z;
   const int tid = threadIdx.x;
-  const int row = tid >> 1, half = tid & 1;
-  const uint4* src = reinterpret_cast<const uint4*>(
-      wq + (static_cast<size_t>(e) * N + static_cast<size_t>(nb) * kBlockM + row) * Kd + kb * kBlockK + half * 64);
-  uint4* srow = reinterpret_cast<uint4*>(tile + row * kStride + half * 64);
+  const uint8_t* src = wq + (static_cast<size_t>(e) * N + static_cast<size_t>(nb) * kBlockM) * Kd + kb * kBlockK;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) srow[i] = src[i];
+  for (int i = 0; i < 4; ++i) {
+    const int k = i * 256 + tid;
+    const int r = k >> 3, ch = k & 7;
+    *reinterpret_cast<uint4*>(tile + tt_chunk(r, ch)) =
+        *reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * Kd + 16 * ch);
+  }
   __syncthreads();
-  store_tile_transposed_128<kStride>(
+  store_tile_transposed_128(
       tile, wqt + (static_cast<size_t>(e) * Kd + static_cast<size_t>(kb) * kBlockK) * N + static_cast<size_t>(nb) * kBlockM,
       static_cast<size_t>(N), tid);
   if (tid < 128) {

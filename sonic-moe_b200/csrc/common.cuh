@@ -279,30 +279,39 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float a, float b) {
   return r;
 }
 
-// Transposed store of a 128 x 128 byte tile in shared memory (row r at tile + r * kStride, kStride a
-// multiple of 4): byte (r, c) goes to dst[c * ld + r].  256 threads: warp w, lane l writes output
-// rows 4l .. 4l + 3, bytes 16w .. 16w + 15 -- one 32-bit word per tile row (a warp reads 32
-// consecutive words of one row) and 4 x 4 byte blocks transposed with byte permutes.  dst and ld
-// must keep the 16-byte stores aligned (ld % 16 == 0).
-template <int kStride>
+// A 128 x 128 byte tile in shared memory for a transposed store: row n at n * kTtStride bytes, its
+// eight 16-byte chunks permuted (chunk k stored at k ^ ((n >> 4) & 7)), so that both the row-wise
+// 16-byte writes that fill it and the column-wise word reads of store_tile_transposed_128 are free
+// of bank conflicts.  tt_chunk: byte offset of chunk k of row n.
+constexpr int kTtStride = 144;
+__device__ __forceinline__ int tt_chunk(int n, int k) { return n * kTtStride + ((k ^ ((n >> 4) & 7)) << 4); }
+
+// Transposed store of such a tile: byte (n, c) goes to dst[c * ld + n].  256 threads: warp w, lane l
+// writes output rows 4 (4w + l / 8) .. + 3, bytes 16 (l % 8) .. + 15 -- it reads one 32-bit word of
+// each of its 16 tile rows and transposes 4 x 4 byte blocks with byte permutes -- so each store
+// instruction of a warp fills 4 whole 128-byte output lines.  dst and ld must keep the 16-byte
+// stores aligned (ld % 16 == 0).
 __device__ __forceinline__ void store_tile_transposed_128(const uint8_t* tile, uint8_t* dst, size_t ld, int tid) {
-  const int lane = tid & 31, grp = tid >> 5;
-  uint32_t r[4][4];  // [output row b][tile-row quad q]
+  const int lane = tid & 31, w = tid >> 5;
+  const int c = lane & 7;                 // output bytes 16c .. 16c + 15 = tile rows 16c ..
+  const int rq = 4 * w + (lane >> 3);     // output rows 4 rq .. 4 rq + 3 = tile bytes 4 rq ..
+  uint32_t r[4][4];                       // [output row b][tile-row quad q]
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const int n = 16 * grp + 4 * q;
-    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(tile + (n + 0) * kStride + 4 * lane);
-    const uint32_t w1 = *reinterpret_cast<const uint32_t*>(tile + (n + 1) * kStride + 4 * lane);
-    const uint32_t w2 = *reinterpret_cast<const uint32_t*>(tile + (n + 2) * kStride + 4 * lane);
-    const uint32_t w3 = *reinterpret_cast<const uint32_t*>(tile + (n + 3) * kStride + 4 * lane);
-    const uint32_t t0 = __byte_perm(w0, w1, 0x5140), t1 = __byte_perm(w2, w3, 0x5140);
-    const uint32_t t2 = __byte_perm(w0, w1, 0x7362), t3 = __byte_perm(w2, w3, 0x7362);
+    uint32_t x[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int n = 16 * c + 4 * q + t;
+      x[t] = *reinterpret_cast<const uint32_t*>(tile + tt_chunk(n, rq >> 2) + 4 * (rq & 3));
+    }
+    const uint32_t t0 = __byte_perm(x[0], x[1], 0x5140), t1 = __byte_perm(x[2], x[3], 0x5140);
+    const uint32_t t2 = __byte_perm(x[0], x[1], 0x7362), t3 = __byte_perm(x[2], x[3], 0x7362);
     r[0][q] = __byte_perm(t0, t1, 0x5410);
     r[1][q] = __byte_perm(t0, t1, 0x7632);
     r[2][q] = __byte_perm(t2, t3, 0x5410);
     r[3][q] = __byte_perm(t2, t3, 0x7632);
   }
-  uint8_t* d = dst + static_cast<size_t>(4 * lane) * ld + 16 * grp;
+  uint8_t* d = dst + static_cast<size_t>(4 * rq) * ld + 16 * c;
 #pragma unroll
   for (int b = 0; b < 4; ++b)
     *reinterpret_cast<uint4*>(d + static_cast<size_t>(b) * ld) = make_uint4(r[b][0], r[b][1], r[b][2], r[b][3]);

@@ -86,6 +86,8 @@ struct GemmSmem {
 
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&p);
@@ -149,8 +151,9 @@ __device__ __forceinline__ RowMeta load_row_meta(const GemmArgs& g, int tile, in
 //   dS[entry] += sum_j dA'_j a_j            (fp32 atomics: four column warps x I/256 tiles)
 //   a'_j = s a_j                            (bf16, padded row; the dW2 operand)
 //   dg_j = s dA'_j u sig (1 + g (1 - sig)),  du_j = s dA'_j g sig
-// dH is written as bf16 (padded row; the dW1 operand) and as e4m3 with one UE8M0 scale for its
-// 128 values -- exactly one 1x128 group of the dX GEMM's K -- plus the scale byte in the atom.
+// dH is written as bf16 (padded row; the dW1 operand) and, quantised from those bf16 values, as
+// e4m3 with one UE8M0 scale for its 128 values -- exactly one 1x128 group of the dX GEMM's K --
+// plus the scale byte in the atom.
 __device__ __forceinline__ void dact_grad(float dap, float gt, float up, float sc, float& a, float& dg, float& du) {
   const float sig = __fdividef(1.0f, 1.0f + __expf(-gt));
   const float silu = gt * sig;
@@ -169,8 +172,11 @@ __device__ __forceinline__ void dact_tile(const GemmArgs& g, const uint32_t (&v)
   const size_t p = static_cast<size_t>(m.p);
   uint4* adst = reinterpret_cast<uint4*>(g.a_prime + p * I + i0);
   uint4* hdst = reinterpret_cast<uint4*>(g.dh_bf16 + p * (2 * I) + 2 * i0);
+  // Pass 1, eight columns at a time: dS, a', and dH as bf16 pairs (dg, du) with the amax of those
+  // bf16 values -- the row's 128 dH values are one 1x128 group.  Pass 2 recomputes dH from h (an L2
+  // hit; the registers hold one pass at a time, the accumulator is already released) and
+  // quantises its bf16 rounding, so the e4m3 copy is the bf16 dH quantised.
   float ds = 0.0f, am = 0.0f;
-  // pass 1, eight columns at a time: dS, a', bf16 dH and the amax of the row's 128 dH values
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const uint4 h0 = hrow[2 * c], h1 = hrow[2 * c + 1];
@@ -182,8 +188,8 @@ __device__ __forceinline__ void dact_tile(const GemmArgs& g, const uint32_t (&v)
       float a, dg, du;
       dact_grad(dap, __uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xFFFF0000u), sc, a, dg, du);
       ds = fmaf(dap, a, ds);
-      am = fmaxf(am, fmaxf(fabsf(dg), fabsf(du)));
       dh[k] = pack_bf16x2(dg, du);
+      am = fmaxf(am, fmaxf(fabsf(__uint_as_float(dh[k] << 16)), fabsf(__uint_as_float(dh[k] & 0xFFFF0000u))));
       if (k & 1) ap[k >> 1] = pack_bf16x2(__uint_as_float(ap[k >> 1]), sc * a);
       else ap[k >> 1] = __float_as_uint(sc * a);
     }
@@ -192,7 +198,6 @@ __device__ __forceinline__ void dact_tile(const GemmArgs& g, const uint32_t (&v)
     hdst[2 * c + 1] = make_uint4(dh[4], dh[5], dh[6], dh[7]);
   }
   atomicAdd(g.ds + g.s_scatter[m.tok], ds);
-  // pass 2: the same dH values (recomputed) as e4m3 under the row's UE8M0 scale
   const int e8 = scale_exp_of_amax(am);
   const float inv = exp2_neg(e8);
   uint4* qdst = reinterpret_cast<uint4*>(g.out_q + p * (2 * I) + 2 * i0);
@@ -208,8 +213,12 @@ __device__ __forceinline__ void dact_tile(const GemmArgs& g, const uint32_t (&v)
                 a0, dg0, du0);
       dact_grad(__uint_as_float(v[8 * c + k + 1]), __uint_as_float(w[k + 1] << 16),
                 __uint_as_float(w[k + 1] & 0xFFFF0000u), sc, a1, dg1, du1);
-      q[k >> 1] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(dg0, inv), __fmul_rn(du0, inv))) |
-                  (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(dg1, inv), __fmul_rn(du1, inv))) << 16);
+      const uint32_t d0 = pack_bf16x2(dg0, du0), d1 = pack_bf16x2(dg1, du1);
+      q[k >> 1] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(__uint_as_float(d0 << 16), inv),
+                                                   __fmul_rn(__uint_as_float(d0 & 0xFFFF0000u), inv))) |
+                  (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(__uint_as_float(d1 << 16), inv),
+                                                    __fmul_rn(__uint_as_float(d1 & 0xFFFF0000u), inv)))
+                   << 16);
     }
     qdst[c] = make_uint4(q[0], q[1], q[2], q[3]);
   }
@@ -240,6 +249,8 @@ __device__ __forceinline__ bool dact_tile_concat(const GemmArgs& g, const uint32
   const uint4* hg = reinterpret_cast<const uint4*>(hrow + i0);
   const uint4* hu = reinterpret_cast<const uint4*>(hrow + I + i0);
   float amg = 0.0f, amu = 0.0f;
+  // dH as bf16 pairs; the e4m3 copy quantises these bf16 values, recomputed after the maxima
+  // exchange (as in dact_tile)
   if (valid) {
     uint4* adst = reinterpret_cast<uint4*>(g.a_prime + p * I + i0);
     uint4* gdst = reinterpret_cast<uint4*>(g.dh_bf16 + p * (2 * I) + i0);
@@ -257,11 +268,12 @@ __device__ __forceinline__ bool dact_tile_concat(const GemmArgs& g, const uint32
         dact_grad(d0, __uint_as_float(gw[k] << 16), __uint_as_float(uw[k] << 16), sc, a0, dg0, du0);
         dact_grad(d1, __uint_as_float(gw[k] & 0xFFFF0000u), __uint_as_float(uw[k] & 0xFFFF0000u), sc, a1, dg1, du1);
         ds = fmaf(d1, a1, fmaf(d0, a0, ds));
-        amg = fmaxf(amg, fmaxf(fabsf(dg0), fabsf(dg1)));
-        amu = fmaxf(amu, fmaxf(fabsf(du0), fabsf(du1)));
+        const uint32_t pg = pack_bf16x2(dg0, dg1), pu = pack_bf16x2(du0, du1);
+        dgp[k] = pg;
+        dup[k] = pu;
+        amg = fmaxf(amg, fmaxf(fabsf(__uint_as_float(pg << 16)), fabsf(__uint_as_float(pg & 0xFFFF0000u))));
+        amu = fmaxf(amu, fmaxf(fabsf(__uint_as_float(pu << 16)), fabsf(__uint_as_float(pu & 0xFFFF0000u))));
         ap[k] = pack_bf16x2(sc * a0, sc * a1);
-        dgp[k] = pack_bf16x2(dg0, dg1);
-        dup[k] = pack_bf16x2(du0, du1);
       }
       adst[c] = make_uint4(ap[0], ap[1], ap[2], ap[3]);
       gdst[c] = make_uint4(dgp[0], dgp[1], dgp[2], dgp[3]);
@@ -283,6 +295,9 @@ __device__ __forceinline__ bool dact_tile_concat(const GemmArgs& g, const uint32
   const int j = i0 / kBlockK, c0 = i0 % kBlockK;
   uint4* gq = reinterpret_cast<uint4*>(g.out_q + p * (2 * I) + 256 * j + c0);
   uint4* uq = reinterpret_cast<uint4*>(g.out_q + p * (2 * I) + 256 * j + 128 + c0);
+  auto q2 = [](uint32_t wd, float inv) {
+    return cvt_e4m3x2(__fmul_rn(__uint_as_float(wd << 16), inv), __fmul_rn(__uint_as_float(wd & 0xFFFF0000u), inv));
+  };
 #pragma unroll
   for (int c2 = 0; c2 < 4; ++c2) {
     uint32_t wg[4], wu[4];
@@ -291,7 +306,7 @@ __device__ __forceinline__ bool dact_tile_concat(const GemmArgs& g, const uint32
       const int c = 2 * c2 + h;
       const uint4 g4 = hg[c], u4 = hu[c];
       const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, uw[4] = {u4.x, u4.y, u4.z, u4.w};
-      uint16_t qg[4], qu[4];
+      uint32_t dgw[4], duw[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         float a0, dg0, du0, a1, dg1, du1;
@@ -299,13 +314,13 @@ __device__ __forceinline__ bool dact_tile_concat(const GemmArgs& g, const uint32
                   a0, dg0, du0);
         dact_grad(__uint_as_float(v[8 * c + 2 * k + 1]), __uint_as_float(gw[k] & 0xFFFF0000u),
                   __uint_as_float(uw[k] & 0xFFFF0000u), sc, a1, dg1, du1);
-        qg[k] = cvt_e4m3x2(__fmul_rn(dg0, ig), __fmul_rn(dg1, ig));
-        qu[k] = cvt_e4m3x2(__fmul_rn(du0, iu), __fmul_rn(du1, iu));
+        dgw[k] = pack_bf16x2(dg0, dg1);
+        duw[k] = pack_bf16x2(du0, du1);
       }
-      wg[2 * h] = static_cast<uint32_t>(qg[0]) | (static_cast<uint32_t>(qg[1]) << 16);
-      wg[2 * h + 1] = static_cast<uint32_t>(qg[2]) | (static_cast<uint32_t>(qg[3]) << 16);
-      wu[2 * h] = static_cast<uint32_t>(qu[0]) | (static_cast<uint32_t>(qu[1]) << 16);
-      wu[2 * h + 1] = static_cast<uint32_t>(qu[2]) | (static_cast<uint32_t>(qu[3]) << 16);
+      wg[2 * h] = static_cast<uint32_t>(q2(dgw[0], ig)) | (static_cast<uint32_t>(q2(dgw[1], ig)) << 16);
+      wg[2 * h + 1] = static_cast<uint32_t>(q2(dgw[2], ig)) | (static_cast<uint32_t>(q2(dgw[3], ig)) << 16);
+      wu[2 * h] = static_cast<uint32_t>(q2(duw[0], iu)) | (static_cast<uint32_t>(q2(duw[1], iu)) << 16);
+      wu[2 * h + 1] = static_cast<uint32_t>(q2(duw[2], iu)) | (static_cast<uint32_t>(q2(duw[3], iu)) << 16);
     }
     gq[c2] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
     uq[c2] = make_uint4(wu[0], wu[1], wu[2], wu[3]);
@@ -649,6 +664,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         ti = tile_info<kKind>(g, tile, n_blocks, ntn, KB);
         if (ti.nkb == 0) continue;
       }
+      RowMeta pre{};
+      if constexpr (kKind == kKindDact) {
+        // the row's metadata, and its stored pre-activation prefetched into L2, while the tile's
+        // main loop runs (the epilogue is bound by the latency of these loads)
+        pre = load_row_meta<kKind>(g, tile, n_blocks, ntn, r);
+        if (pre.valid) {
+          const int i0 = pre.nt * kBN + 64 * cc;
+          const __nv_bfloat16* hrow = g.h_in + static_cast<size_t>(pre.tok) * (2 * g.N);
+          prefetch_l2(g.concat ? hrow + i0 : hrow + 2 * i0);
+          prefetch_l2(g.concat ? hrow + g.N + i0 : hrow + 2 * i0 + 64);
+        }
+      }
       if (!mbar_wait(tmem_full, tcount & 1, g.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       uint32_t v[64];
@@ -679,7 +706,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         continue;
       } else {
         // the accumulator is released: the row's metadata loads overlap the next tile's main loop
-        const RowMeta meta = load_row_meta<kKind>(g, tile, n_blocks, ntn, r);
+        const RowMeta meta = kKind == kKindDact ? pre : load_row_meta<kKind>(g, tile, n_blocks, ntn, r);
         const bool ok_tile = epilogue_tile<kKind>(g, v, meta, r, cc, ew, lane, tcount, s_amax, amax_bar, store_bar,
                                                   sStage, &tmap_out, pol_out);
         ++tcount;

@@ -124,21 +124,28 @@ __global__ void __launch_bounds__(256)
     weight_prep_kernel(const __nv_bfloat16* __restrict__ w, int E, int N, int Kd, int concat_glu,
                        uint8_t* __restrict__ wq, uint8_t* __restrict__ wsf, uint8_t* __restrict__ wqt,
                        uint8_t* __restrict__ wsft) {
-  constexpr int kStride = 144;  // transposed copy: rows 144 bytes apart
-  __shared__ __align__(16) uint8_t tile[kBlockM * kStride];
+  __shared__ __align__(16) uint8_t tile[kBlockM * kTtStride];  // the transposed copy's staging tile
   __shared__ float s_red[8];
   const int kb = blockIdx.x, nb = blockIdx.y, e = blockIdx.z;
   const int nbs = concat_glu ? ((nb % 2 == 0) ? nb / 2 : (N / 2) / kBlockM + nb / 2) : nb;
   const int tid = threadIdx.x;
-  const int row = tid >> 1, half = tid & 1;
-  const __nv_bfloat16* src =
-      w + (static_cast<size_t>(e) * N + static_cast<size_t>(nbs) * kBlockM + row) * Kd + kb * kBlockK + half * 64;
-  float v[64];
+  // piece i of this thread: 8 values (16 bytes of bf16) at row (256 i + tid) / 16, columns
+  // 8 ((256 i + tid) % 16) -- 16 lanes per 256-byte row slice, so a warp's load touches 4 lines
+  const __nv_bfloat16* src = w + (static_cast<size_t>(e) * N + static_cast<size_t>(nbs) * kBlockM) * Kd + kb * kBlockK;
+  uint4 raw[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) bf16x8_to_f32(reinterpret_cast<const uint4*>(src)[i], v + 8 * i);
+  for (int i = 0; i < 8; ++i) {
+    const int k = i * 256 + tid;
+    raw[i] = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(k >> 4) * Kd + 8 * (k & 15));
+  }
   float am = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) am = fmaxf(am, fabsf(v[i]));
+  for (int i = 0; i < 8; ++i) {
+    float v[8];
+    bf16x8_to_f32(raw[i], v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[j]));
+  }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
   if ((tid & 31) == 0) s_red[tid >> 5] = am;
@@ -148,20 +155,20 @@ __global__ void __launch_bounds__(256)
   for (int i = 1; i < 8; ++i) am = fmaxf(am, s_red[i]);
   const int e8 = scale_exp_of_amax(am);
   const float inv = exp2_neg(e8);
-  uint8_t* dst =
-      wq + (static_cast<size_t>(e) * N + static_cast<size_t>(nb) * kBlockM + row) * Kd + kb * kBlockK + half * 64;
+  uint8_t* dst = wq + (static_cast<size_t>(e) * N + static_cast<size_t>(nb) * kBlockM) * Kd + kb * kBlockK;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t wd[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float* q = v + 16 * i + 4 * j;
-      wd[j] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[0], inv), __fmul_rn(q[1], inv))) |
-              (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(q[2], inv), __fmul_rn(q[3], inv))) << 16);
-    }
-    reinterpret_cast<uint4*>(dst)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-    if (wqt != nullptr)
-      *reinterpret_cast<uint4*>(tile + row * kStride + half * 64 + 16 * i) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  for (int i = 0; i < 8; ++i) {
+    const int k = i * 256 + tid;
+    const int row = k >> 4, c8 = k & 15;
+    float v[8];
+    bf16x8_to_f32(raw[i], v);
+    const uint2 b = make_uint2(
+        static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[0], inv), __fmul_rn(v[1], inv))) |
+            (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[2], inv), __fmul_rn(v[3], inv))) << 16),
+        static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[4], inv), __fmul_rn(v[5], inv))) |
+            (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v[6], inv), __fmul_rn(v[7], inv))) << 16));
+    *reinterpret_cast<uint2*>(dst + static_cast<size_t>(row) * Kd + 8 * c8) = b;
+    if (wqt != nullptr) *reinterpret_cast<uint2*>(tile + tt_chunk(row, c8 >> 1) + 8 * (c8 & 1)) = b;
   }
   if (tid < 128) {
     const int KG = (Kd / kBlockK + 3) / 4;
@@ -170,7 +177,7 @@ __global__ void __launch_bounds__(256)
   }
   if (wqt != nullptr) {  // uniform over the block
     __syncthreads();
-    store_tile_transposed_128<kStride>(
+    store_tile_transposed_128(
         tile,
         wqt + (static_cast<size_t>(e) * Kd + static_cast<size_t>(kb) * kBlockK) * N + static_cast<size_t>(nb) * kBlockM,
         static_cast<size_t>(N), tid);

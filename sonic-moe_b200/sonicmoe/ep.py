@@ -9,8 +9,9 @@ Four transports move the records and returned rows between the ranks of one node
 * ``"copy"``: the same shared buffers, but record segments and partial rows cross NVLink as plain
   device-to-device copies (copy engines, no SMs) into local buffers, pipelined over token chunks.
 * ``"nccl"``: ``all_to_all_single`` of the records and of the partial rows.
-* ``"home"`` (default on GPUs, see ``default_transport``): the records move as in ``"p2p"``, but an expert's owner runs only the up projection,
-  whose epilogue stores each entry's e4m3 intermediate row (I + I/128 bytes) straight into the
+* ``"home"`` (default on GPUs, see ``default_transport`` and ``default_chunks``): the records move
+  as in ``"p2p"`` (with chunks, through copy engines), but an expert's owner runs only the up
+  projection, whose epilogue stores each entry's e4m3 intermediate row (I + I/128 bytes) straight into the
   padded layout of the token's own rank over NVLink; that rank then runs the down projection with
   the fused top-k combine over its own routing plan, with every expert's w2 replicated on every
   rank (gathered once at construction).  No partial rows and no combine pass: at config 2 with 8
@@ -35,11 +36,13 @@ its blog).  One process per GPU; rank d of W owns the contiguous global experts
 The home transport instead runs: router top-k and this rank's routing plan over all E experts,
 records carrying each entry's row in that plan, the count all-gather, the up stage (records pulled
 from the peers' send buffers, rows stored into the tokens' home intermediates), one all-reduce,
-and the down projection with the top-k combine over the rank's own plan.
+and the down projection with the top-k combine over the rank's own plan.  In one chunk it never
+waits on the host: the up stage reads the count matrix in device memory (a bad count becomes
+device error 203, raised by a later forward on every rank).
 
-The record counts are read on the host between the two exchanges (one small device-to-host copy
-per forward), and every rank checks them before any data moves; a bad count on any rank makes all
-ranks raise together (the NCCL transport agrees on the verdict with a collective; the peer-memory
+The other transports read the record counts on the host between the two exchanges (one small
+device-to-host copy per forward), and every rank checks them before any data moves; a bad count on
+any rank makes all ranks raise together (the NCCL transport agrees on the verdict with a collective; the peer-memory
 transports all-gather the whole count matrix, so every rank checks every rank's counts and
 reaches the same verdict), so no rank is left waiting in a collective the others skipped.
 """
@@ -277,23 +280,31 @@ def check_count_matrix(C, send_cap: int, out_cap: int, me: int) -> str:
 def default_transport(world: int, native: bool = True, chunks: int = None) -> str:
     """Transport chosen when the caller names none, from the measurements at config 2 per rank.
 
-    * 2-4 ranks: the home-down transport (2 ranks: 4.08-4.13 ms per forward against 4.33 for peer
-      loads with the down projection at the owners; 4 ranks: 5.11 against 6.24 ms, in the same
-      call: the bytes back per rank are 6x smaller for e4m3 intermediate rows than for bf16
-      partial rows).  At config 4 (E=256, H=7168) the two are within 2% at 2 and 4 ranks.
-    * 5-7 ranks: peer loads in one chunk (not measured at these sizes).
-    * 8 and more: copy-engine transfers pipelined over 6 chunks (7.01 ms at 8 ranks, against 9.54
-      for one-chunk peer loads); the home-down transport is not measured at 8.
-    A caller that asks for chunks > 1 gets the chunked transports; device-stage stand-ins (tests)
-    take NCCL.
+    The home-down transport at every measured size: 2 ranks 4.08-4.13 ms per forward against 4.33
+    for peer loads with the down projection at the owners; 4 ranks 5.11 against 6.24 ms; 8 ranks,
+    pipelined over 4 token chunks, 6.28 ms against 6.87 for copy-engine transfers over 6 chunks (the
+    bytes back per rank are 6x smaller for e4m3 intermediate rows than for bf16 partial rows).  5-7
+    ranks are not measured; home wins at both neighbours.  Device-stage stand-ins (tests) take NCCL.
     """
+    del chunks  # every chunk count is served by the home transport
     if not native or world <= 1:
         return "nccl"
-    if world >= 8:
-        return "copy"
-    if world <= 4 and (chunks is None or chunks == 1):
-        return "home"
-    return "p2p"
+    return "home"
+
+
+def default_chunks(transport: str, world: int, max_tokens: int) -> int:
+    """Token chunks the forward is pipelined over when the caller names none: the home transport
+    at 8 and more ranks, 4 chunks (6.28 ms at config 2 against 6.92 with 2 and 8.34 with 1: the
+    records of later chunks land through copy engines under the up projection of earlier ones);
+    at 5-7 ranks 2; up to 4 ranks one (a chunk's fixed expert-stage cost exceeds the transfer time
+    it hides); the copy transport 6 from 8 ranks.  Batches under 4096 tokens per rank: one."""
+    if max_tokens < 4096:
+        return 1
+    if transport == "home":
+        return 4 if world >= 8 else (2 if world > 4 else 1)
+    if transport == "copy" and world >= 8:
+        return 6
+    return 1
 
 
 class ExpertParallelMoE:
@@ -329,10 +340,7 @@ class ExpertParallelMoE:
             raise ValueError("the home transport runs the native stages only")
         self.transport = transport
         if chunks is None:
-            # 2 and 4 ranks: one chunk (a chunk's fixed expert-stage cost exceeds the transfer time
-            # it hides); 8 ranks with copy-engine transfers: 6 chunks (7.01 ms at config 2, vs 7.37
-            # with 4 or 8 chunks and 9.54 for one-chunk peer loads)
-            chunks = 6 if (transport == "copy" and self.world >= 8 and (max_tokens or 0) >= 4096) else 1
+            chunks = default_chunks(transport, self.world, max_tokens or 0)
         if chunks < 1:
             raise ValueError("chunks must be >= 1")
         self.chunks = int(chunks)
