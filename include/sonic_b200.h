@@ -302,7 +302,9 @@ int sm_weight_prep_with_t(const void* w, int E, int N, int K, int concat_glu, ui
  * dh_bf16 [max_blocks*128, 2I], a_prime [max_blocks*128, I] (padded rows); dscores [T*K] fp32, flat
  * entries, accumulated.  concat_layout = 1: h and dh_bf16 in [gate | up] order and dh_q in the
  * re-blocked order of the prepared concatenated w1 (gate block j, up block j, ...), matching
- * sm_weight_prep_t of that weight.  I % 256 == 0. */
+ * sm_weight_prep_t of that weight.  dH's e4m3 copy quantises the bf16 dH.  dh_q = dh_sf = NULL:
+ * no e4m3 copy (sm_tq_pack_dual makes it from dh_bf16 together with the dW1 operand).
+ * I % 256 == 0. */
 int sm_moe_dact(const uint8_t* doq, const uint8_t* dosf, const uint8_t* w2t_q, const uint8_t* w2t_sf, int H, int I,
                 int E, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks, const int32_t* off_pad,
                 const int32_t* expert_frequency_offset, const int32_t* expert_frequency, const int32_t* s_scatter_idx,
@@ -317,6 +319,15 @@ int sm_tq_pack(const void* src, int C, int src_padded, int max_blocks, const int
                const int32_t* n_blocks, const int32_t* off_pad, const int32_t* expert_frequency_offset,
                const int32_t* expert_frequency, const int32_t* x_gather_idx, uint8_t* out_q, uint8_t* out_sf,
                void* stream);
+/* sm_tq_pack of a padded source (dH [max_blocks*128, C] bf16) that also writes the row-quantised
+ * copy from the same read: row_q [max_blocks*128, C] e4m3 with one UE8M0 scale per 128 columns of a
+ * row, atoms row_sf [max_blocks][ceil(C/512)][512] -- the dX GEMM's A operand, exactly what
+ * sm_moe_dact writes as dh_q / dh_sf.  concat_I = I (C = 2I, src in [gate | up] order): row_q
+ * column blocks in the prepared concatenated w1's re-blocked order (gate block j -> 2j, up block
+ * j -> 2j + 1); 0: the source order. */
+int sm_tq_pack_dual(const void* src, int C, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+                    const int32_t* off_pad, const int32_t* expert_frequency, uint8_t* out_q, uint8_t* out_sf,
+                    uint8_t* row_q, uint8_t* row_sf, int concat_I, void* stream);
 /* Weight gradient: out_w[e] [M, N] bf16 = A[:, rows_e] B[:, rows_e]^T over expert e's padded rows
  * (off_pad), A [M, max_blocks*128] and B [N, max_blocks*128] from sm_tq_pack.  Experts without rows
  * get zeros.  M % 128 == 0, N % 256 == 0. */

@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(256)
                    const int32_t* __restrict__ off_pad, const int32_t* __restrict__ off,
                    const int32_t* __restrict__ freq, const int32_t* __restrict__ x_gather,
                    const int32_t* __restrict__ n_blocks, long long rows_pad, uint8_t* __restrict__ outq,
-                   uint8_t* __restrict__ outsf) {
+                   uint8_t* __restrict__ outsf, uint8_t* __restrict__ rowq, uint8_t* __restrict__ rowsf,
+                   int row_concat_i) {
   __shared__ __align__(16) uint32_t tile[kBlockM * kTqStride];
   __shared__ int s_row[kBlockM];  // source row of each padded row, -1 = padding
   const int mb = blockIdx.x, cb = blockIdx.y;
@@ -98,6 +99,44 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
   const int warp = tid >> 5, lane = tid & 31;
+  if (rowq != nullptr) {
+    // The same tile quantised along its rows (padded sources: the dX GEMM's dH operand): each row's
+    // 128 values of this column block are one 1x128 group.  16 lanes per row, 8 values each (a warp
+    // reads two rows per pass and stores two 128-byte lines); column block cb lands at column block
+    // cbd of the row-quantised operand -- itself, or for a concatenated [gate | up] source the
+    // re-blocked order of the prepared w1 (gate block j -> 2 j, up block j -> 2 j + 1).
+    const int hl = lane & 15;
+    const int nI = row_concat_i / kBlockK;
+    const int cbd = row_concat_i > 0 ? (cb < nI ? 2 * cb : 2 * (cb - nI) + 1) : cb;
+    const int KG2 = (C / kBlockK + 3) / 4;
+#pragma unroll 1
+    for (int pass = 0; pass < 8; ++pass) {
+      const int row = 16 * pass + 2 * warp + (lane >> 4);
+      const uint4 w4 = *reinterpret_cast<const uint4*>(&tile[tq_word(row, 4 * hl)]);
+      const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
+      float am = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        am = fmaxf(am, fmaxf(fabsf(__uint_as_float(wd[k] << 16)), fabsf(__uint_as_float(wd[k] & 0xFFFF0000u))));
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      const int er = scale_exp_of_amax(am);
+      const float ir = exp2_neg(er);
+      uint32_t b[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        b[k] = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(__uint_as_float(wd[2 * k] << 16), ir),
+                                                __fmul_rn(__uint_as_float(wd[2 * k] & 0xFFFF0000u), ir))) |
+               (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(__uint_as_float(wd[2 * k + 1] << 16), ir),
+                                                 __fmul_rn(__uint_as_float(wd[2 * k + 1] & 0xFFFF0000u), ir)))
+                << 16);
+      const long long p = static_cast<long long>(mb) * kBlockM + row;
+      *reinterpret_cast<uint2*>(rowq + p * C + static_cast<long long>(cbd) * kBlockK + 8 * hl) = make_uint2(b[0], b[1]);
+      if (hl == 0)
+        rowsf[(static_cast<long long>(mb) * KG2 + cbd / 4) * kSfAtomBytes + 16 * (row % 32) + 4 * (row / 32) +
+              (cbd % 4)] = static_cast<uint8_t>(er + 127);
+    }
+  }
   const int q = lane & 3;                   // row quarter: rows 32 q .. 32 q + 31
   const int cp = 8 * warp + (lane >> 2);    // column pair: columns 2 cp, 2 cp + 1
   float a0 = 0.0f, a1 = 0.0f;
@@ -208,12 +247,13 @@ cudaError_t launch_weight_t(const uint8_t* wq, const uint8_t* wsf, int E, int N,
 
 cudaError_t launch_tq_pack(const void* src, int C, int src_padded, const int32_t* blk_expert, const int32_t* off_pad,
                            const int32_t* off, const int32_t* freq, const int32_t* x_gather, const int32_t* n_blocks,
-                           int max_blocks, uint8_t* outq, uint8_t* outsf, cudaStream_t st) {
+                           int max_blocks, uint8_t* outq, uint8_t* outsf, cudaStream_t st, uint8_t* rowq,
+                           uint8_t* rowsf, int row_concat_i) {
   if (max_blocks == 0) return cudaSuccess;
   dim3 grid(max_blocks, C / kBlockK);
   tq_pack_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), C, src_padded, blk_expert, off_pad, off,
                                        freq, x_gather, n_blocks, static_cast<long long>(max_blocks) * kBlockM, outq,
-                                       outsf);
+                                       outsf, rowq, rowsf, row_concat_i);
   return cudaGetLastError();
 }
 

@@ -444,9 +444,9 @@ int sm_moe_dact(const uint8_t* doq, const uint8_t* dosf, const uint8_t* w2t_q, c
                 void* dh_bf16, void* a_prime, float* dscores, int32_t* err, void* stream) {
   if (H <= 0 || H % 128 || I <= 0 || I % 256 || E < 1 || max_blocks < 0)
     return fail(SM_ENOTSUP, "bad shape H=%d I=%d E=%d (H %% 128 == 0, I %% 256 == 0)", H, I, E);
-  if (!err || !preact || !dh_q || !dh_sf || !dh_bf16 || !a_prime || !dscores || !topk_scores || !s_scatter_idx ||
-      !expert_frequency_offset)
-    return fail(SM_EINVAL, "null pointer");
+  if (!err || !preact || !dh_bf16 || !a_prime || !dscores || !topk_scores || !s_scatter_idx ||
+      !expert_frequency_offset || (dh_q == nullptr) != (dh_sf == nullptr))
+    return fail(SM_EINVAL, "null pointer (dh_q and dh_sf are both set or both NULL)");
   if (!aligned16(preact) || !aligned16(dh_q) || !aligned16(dh_bf16) || !aligned16(a_prime))
     return fail(SM_EINVAL, "pointers must be 16-byte aligned");
   GemmArgs g = up_args(doq, dosf, w2t_q, w2t_sf, H, I / 2, E, concat_layout ? 1 : 0, max_blocks, blk_expert,
@@ -475,6 +475,21 @@ int sm_tq_pack(const void* src, int C, int src_padded, int max_blocks, const int
                                     x_gather_idx, n_blocks, max_blocks, out_q, out_sf,
                                     static_cast<cudaStream_t>(stream)),
                      "tq_pack");
+}
+
+int sm_tq_pack_dual(const void* src, int C, int max_blocks, const int32_t* blk_expert, const int32_t* n_blocks,
+                    const int32_t* off_pad, const int32_t* expert_frequency, uint8_t* out_q, uint8_t* out_sf,
+                    uint8_t* row_q, uint8_t* row_sf, int concat_I, void* stream) {
+  if (C <= 0 || C % 128 || max_blocks < 0) return fail(SM_EINVAL, "need C %% 128 == 0 (C=%d)", C);
+  if (concat_I < 0 || (concat_I > 0 && (2 * concat_I != C || concat_I % 128)))
+    return fail(SM_EINVAL, "concat_I must be 0 or C / 2 with I %% 128 == 0 (C=%d, I=%d)", C, concat_I);
+  if (!src || !blk_expert || !n_blocks || !off_pad || !expert_frequency || !out_q || !out_sf || !row_q || !row_sf)
+    return fail(SM_EINVAL, "null pointer");
+  if (!aligned16(src) || !aligned16(out_q) || !aligned16(row_q)) return fail(SM_EINVAL, "pointers must be 16-byte aligned");
+  return cuda_status(launch_tq_pack(src, C, 1, blk_expert, off_pad, nullptr, expert_frequency, nullptr, n_blocks,
+                                    max_blocks, out_q, out_sf, static_cast<cudaStream_t>(stream), row_q, row_sf,
+                                    concat_I),
+                     "tq_pack_dual");
 }
 
 int sm_moe_wgrad(const uint8_t* a_q, const uint8_t* a_sf, const uint8_t* b_q, const uint8_t* b_sf, int M, int N,

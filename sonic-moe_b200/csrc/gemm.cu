@@ -198,6 +198,7 @@ __device__ __forceinline__ void dact_tile(const GemmArgs& g, const uint32_t (&v)
     hdst[2 * c + 1] = make_uint4(dh[4], dh[5], dh[6], dh[7]);
   }
   atomicAdd(g.ds + g.s_scatter[m.tok], ds);
+  if (g.out_q == nullptr) return;  // the e4m3 copy is made from dh_bf16 by the dual operand pack
   const int e8 = scale_exp_of_amax(am);
   const float inv = exp2_neg(e8);
   uint4* qdst = reinterpret_cast<uint4*>(g.out_q + p * (2 * I) + 2 * i0);
@@ -281,6 +282,7 @@ __device__ __forceinline__ bool dact_tile_concat(const GemmArgs& g, const uint32
     }
     atomicAdd(g.ds + g.s_scatter[m.tok], ds);
   }
+  if (g.out_q == nullptr) return true;  // no e4m3 copy here: no maxima to exchange (uniform over the CTA)
   float* buf = s_amax + (tcount & 1) * (2 * 4 * kBlockM);
   buf[cc * kBlockM + r] = amg;
   buf[(4 + cc) * kBlockM + r] = amu;

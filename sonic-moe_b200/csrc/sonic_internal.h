@@ -70,9 +70,12 @@ cudaError_t launch_weight_prep(const void* w, int E, int N, int Kd, int concat_g
 // backward (csrc/backward.cu)
 cudaError_t launch_weight_t(const uint8_t* wq, const uint8_t* wsf, int E, int N, int Kd, uint8_t* wqt, uint8_t* wsft,
                             cudaStream_t st);
+// rowq / rowsf (padded sources only): also the row-quantised copy, column blocks re-blocked when
+// row_concat_i = I > 0 (a concatenated [gate | up] source)
 cudaError_t launch_tq_pack(const void* src, int C, int src_padded, const int32_t* blk_expert, const int32_t* off_pad,
                            const int32_t* off, const int32_t* freq, const int32_t* x_gather, const int32_t* n_blocks,
-                           int max_blocks, uint8_t* outq, uint8_t* outsf, cudaStream_t st);
+                           int max_blocks, uint8_t* outq, uint8_t* outsf, cudaStream_t st, uint8_t* rowq = nullptr,
+                           uint8_t* rowsf = nullptr, int row_concat_i = 0);
 cudaError_t launch_router_bwd(const void* logits, const float* scores, const int32_t* idx, const float* ds, int T,
                               int E, int K, int sot, int renorm, float* dlogits, cudaStream_t st);
 

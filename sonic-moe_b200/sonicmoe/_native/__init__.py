@@ -110,6 +110,7 @@ SIGNATURES = {
         [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P],
     ),
     "sm_tq_pack": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "sm_tq_pack_dual": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P]),
     "sm_moe_wgrad": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "sm_router_bwd": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "sm_moe_down_combine": (

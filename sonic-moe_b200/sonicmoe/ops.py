@@ -469,13 +469,14 @@ def weight_prep_t(w: Fp8ExpertWeights) -> Fp8ExpertWeights:
 
 
 def moe_dact(doq, dosf, w2t: Fp8ExpertWeights, plan: RoutePlan, scores_flat: torch.Tensor, preact: torch.Tensor, err,
-             dscores: torch.Tensor = None, concat_layout: bool = False):
-    """dA' = dO W2 per entry fused with the SwiGLU backward: (dh_q, dh_sf, dh_bf16, a_prime, dscores)."""
+             dscores: torch.Tensor = None, concat_layout: bool = False, with_q: bool = True):
+    """dA' = dO W2 per entry fused with the SwiGLU backward: (dh_q, dh_sf, dh_bf16, a_prime, dscores).
+    with_q=False: no e4m3 copy of dH (dh_q = dh_sf = None; ``tq_pack_dual`` makes it)."""
     E, I, H = w2t.shape
     rows = plan.max_blocks * _BLOCK_M
     dev = doq.device
-    dh_q = torch.empty(rows, 2 * I, dtype=torch.uint8, device=dev)
-    dh_sf = torch.zeros(plan.max_blocks, -(-(2 * I) // 512), 512, dtype=torch.uint8, device=dev)
+    dh_q = torch.empty(rows, 2 * I, dtype=torch.uint8, device=dev) if with_q else None
+    dh_sf = torch.zeros(plan.max_blocks, -(-(2 * I) // 512), 512, dtype=torch.uint8, device=dev) if with_q else None
     dh = torch.empty(rows, 2 * I, dtype=torch.bfloat16, device=dev)
     a_prime = torch.empty(rows, I, dtype=torch.bfloat16, device=dev)
     if dscores is None:
@@ -503,6 +504,25 @@ def tq_pack(src: torch.Tensor, plan: RoutePlan, padded: bool):
         _ptr(plan.off_pad), _ptr(plan.off), _ptr(plan.freq), _ptr(plan.x_gather), _ptr(q), _ptr(sf), _stream(),
     )
     return q, sf
+
+
+def tq_pack_dual(src: torch.Tensor, plan: RoutePlan, concat_i: int = 0):
+    """``tq_pack`` of a padded source plus its row-quantised copy from the same read: (out_q, out_sf,
+    row_q [rows, C], row_sf) -- the dW1 operand and the dX GEMM's dH operand (column blocks re-blocked
+    for a concatenated [gate | up] source when concat_i = I)."""
+    _need(src, "src", torch.bfloat16)
+    C = src.shape[1]
+    rows = plan.max_blocks * _BLOCK_M
+    dev = src.device
+    q = torch.empty(C, rows, dtype=torch.uint8, device=dev)
+    sf = torch.zeros(C // _BLOCK_M, -(-plan.max_blocks // 4), 512, dtype=torch.uint8, device=dev)
+    rq = torch.empty(rows, C, dtype=torch.uint8, device=dev)
+    rsf = torch.zeros(plan.max_blocks, -(-C // 512), 512, dtype=torch.uint8, device=dev)
+    nat.call(
+        "sm_tq_pack_dual", _ptr(src), C, plan.max_blocks, _ptr(plan.blk_expert), _ptr(plan.n_blocks),
+        _ptr(plan.off_pad), _ptr(plan.freq), _ptr(q), _ptr(sf), _ptr(rq), _ptr(rsf), int(concat_i), _stream(),
+    )
+    return q, sf, rq, rsf
 
 
 def moe_wgrad(aq, asf, bq, bsf, E: int, plan: RoutePlan, err):
@@ -542,9 +562,12 @@ def moe_backward(dout: torch.Tensor, x: torch.Tensor, router_logits: torch.Tenso
     dout = dout.contiguous()
     doq, dosf = quant_pack_general(dout, idx, plan) if general else quant_pack(dout, idx, plan)
     w2t = weight_prep_t(w2)
-    dh_q, dh_sf, dh, a_prime, ds = moe_dact(doq, dosf, w2t, plan, scores.view(-1), preact, err,
-                                            concat_layout=w1.concat_glu)
+    _, _, dh, a_prime, ds = moe_dact(doq, dosf, w2t, plan, scores.view(-1), preact, err,
+                                     concat_layout=w1.concat_glu, with_q=False)
     del doq, dosf, w2t
+    # one read of dH: the dW1 operand (transposed, column-quantised) and the dX operand (row-quantised)
+    dht_q, dht_sf, dh_q, dh_sf = tq_pack_dual(dh, plan, concat_i=dh.shape[1] // 2 if w1.concat_glu else 0)
+    del dh
     w1t = weight_prep_t(w1)
     dx = torch.zeros(T, H, dtype=torch.bfloat16, device=dout.device)
     E1, H1, N2 = w1t.shape
@@ -558,7 +581,6 @@ def moe_backward(dout: torch.Tensor, x: torch.Tensor, router_logits: torch.Tenso
     apt_q, apt_sf = tq_pack(a_prime, plan, padded=True)
     dw2 = moe_wgrad(dot_q, dot_sf, apt_q, apt_sf, E, plan, err)  # [E, H, I]
     del dot_q, dot_sf, apt_q, apt_sf, a_prime
-    dht_q, dht_sf = tq_pack(dh, plan, padded=True)
     xt_q, xt_sf = tq_pack(x.contiguous(), plan, padded=False)
     dw1 = moe_wgrad(dht_q, dht_sf, xt_q, xt_sf, E, plan, err)  # [E, 2I, H]
     if general:

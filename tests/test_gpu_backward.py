@@ -115,6 +115,45 @@ def test_weight_prep_with_t_matches_the_two_passes(ops, concat):
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("concat", [False, True])
+def test_tq_pack_dual_matches_dact_q_and_tq_pack(ops, concat):
+    """The dual operand pack of dH writes, from one read, the dX operand bit for bit as the dA'
+    epilogue's own e4m3 copy (row groups, re-blocked for a concatenated w1) and the dW1 operand bit
+    for bit as tq_pack; the epilogue without its e4m3 copy writes the same bf16 dH, a' and dS."""
+    T, H, I, E, K = 300, 512, 256, 8, 4
+    x, rw, w1, w2 = make_layer_inputs(T, H, I, E, seed=21)
+    xc, rwc, w1c, w2c = x.cuda(), rw.cuda(), w1.cuda(), w2.cuda()
+    logits, scores, idx, plan, h, err = _forward_state(ops, xc, rwc, w1c, w2c, K, True, False, concat)
+    g = torch.Generator().manual_seed(22)
+    dout = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16).cuda()
+    doq, dosf = ops.quant_pack(dout, idx, plan)
+    w2t = ops.weight_prep_t(ops.weight_prep(w2c))
+    dh_q, dh_sf, dh, ap, ds = ops.moe_dact(doq, dosf, w2t, plan, scores.view(-1), h, err, concat_layout=concat)
+    n_q, n_sf, dh2, ap2, ds2 = ops.moe_dact(doq, dosf, w2t, plan, scores.view(-1), h, err, concat_layout=concat,
+                                            with_q=False)
+    assert n_q is None and n_sf is None
+    cq, csf, rq, rsf = ops.tq_pack_dual(dh, plan, concat_i=I if concat else 0)
+    tq, tsf = ops.tq_pack(dh, plan, True)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    nb = int(plan.n_blocks.item())
+    valid = torch.zeros(plan.max_blocks * 128, dtype=torch.bool)
+    fr, op = plan.freq.cpu(), plan.off_pad.cpu()
+    for e in range(E):
+        valid[int(op[e]):int(op[e]) + int(fr[e])] = True
+    valid = valid.cuda()
+    assert torch.equal(rq[valid], dh_q[valid])
+    # scale bytes of the valid rows: rows r of block b at byte 16 (r % 32) + 4 (r / 32) + (kb % 4)
+    rows = torch.nonzero(valid).view(-1).cpu()
+    kbs = torch.arange(2 * I // 128)
+    byte = (16 * (rows % 32) + 4 * ((rows % 128) // 32))[:, None] + (kbs % 4)[None, :]
+    blk, kg = (rows // 128)[:, None].expand(-1, kbs.numel()), (kbs // 4)[None, :].expand(rows.numel(), -1)
+    assert torch.equal(rsf.cpu()[blk, kg, byte], dh_sf.cpu()[blk, kg, byte])
+    assert torch.equal(cq[:, :nb * 128], tq[:, :nb * 128]) and torch.equal(csf, tsf)
+    assert torch.equal(dh2[valid], dh[valid]) and torch.equal(ap2[valid], ap[valid])
+    torch.testing.assert_close(ds2, ds, rtol=1e-5, atol=1e-6)  # fp32 atomics: order may differ
+
+
 @pytest.mark.parametrize("padded", [False, True])
 @pytest.mark.parametrize("T,C,E,K", [(300, 512, 8, 2), (200, 384, 64, 8)])
 def test_tq_pack_bit_exact(ops, T, C, E, K, padded):
