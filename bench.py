@@ -91,6 +91,15 @@ class ClockSampler:
             idx = int(vis.split(",")[self.gpu]) if vis else self.gpu
             h = pynvml.nvmlDeviceGetHandleByIndex(idx)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def sample():
+                return (pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                        pynvml.nvmlDeviceGetCurrentClocksEventReasons(h),
+                        pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0)
+
+            # the first queries after nvmlInit can take a few hundred ms and hold up the CUDA
+            # launches of the timed loop if they run during it: take them here, untimed
+            sample()
         except Exception:
             return self
         self._stop = threading.Event()
@@ -98,10 +107,7 @@ class ClockSampler:
         def run():
             while not self._stop.is_set():
                 try:
-                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
-                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
-                    self.samples.append((sm, rs, pw))
+                    self.samples.append(sample())
                 except Exception:
                     pass
                 time.sleep(self.interval)

@@ -296,13 +296,14 @@ def default_chunks(transport: str, world: int, max_tokens: int) -> int:
     """Token chunks the forward is pipelined over when the caller names none: the home transport
     at 8 and more ranks, 4 chunks (6.28 ms at config 2 against 6.92 with 2 and 8.34 with 1: the
     records of later chunks land through copy engines under the up projection of earlier ones);
-    at 3-7 ranks 2 (4 ranks: 5.23 ms against 5.35 with one chunk and 5.43 with 4, in one call); at 2
-    ranks one (a chunk's fixed expert-stage cost exceeds the transfer time it hides); the copy
-    transport 6 from 8 ranks.  Batches under 4096 tokens per rank: one."""
+    up to 4 ranks one, which also reads the exchange counts on the device and never waits on the
+    host (4 ranks, per-step device times in one call: 4.93 ms against 5.23 with 2 chunks at config
+    2, 4.05 against 4.62 at config 4); 5-7 ranks, not measured, 2; the copy transport 6 from 8
+    ranks.  Batches under 4096 tokens per rank: one."""
     if max_tokens < 4096:
         return 1
     if transport == "home":
-        return 4 if world >= 8 else (2 if world > 2 else 1)
+        return 4 if world >= 8 else (2 if world > 4 else 1)
     if transport == "copy" and world >= 8:
         return 6
     return 1

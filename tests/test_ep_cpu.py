@@ -160,7 +160,7 @@ def test_home_transport_arguments():
 
 def test_default_transport():
     """One process or device-stage stand-ins: NCCL; otherwise the home-down transport (measured best
-    at 2, 4 and 8 ranks), pipelined over 4 token chunks from 8 ranks, 2 at 3-7, one at 2; the copy
+    at 2, 4 and 8 ranks), pipelined over 4 token chunks from 8 ranks, 2 at 5-7, one up to 4; the copy
     transport keeps 6 chunks from 8 ranks; small batches run in one chunk."""
     from sonicmoe.ep import default_chunks, default_transport
 
@@ -168,7 +168,7 @@ def test_default_transport():
     assert default_transport(8, native=False) == "nccl"
     for w in (2, 3, 4, 6, 8, 16):
         assert default_transport(w) == "home" and default_transport(w, chunks=3) == "home"
-    assert [default_chunks("home", w, 32768) for w in (2, 3, 4, 6, 8)] == [1, 2, 2, 2, 4]
+    assert [default_chunks("home", w, 32768) for w in (2, 3, 4, 6, 8)] == [1, 1, 1, 2, 4]
     assert default_chunks("home", 8, 2048) == 1
     assert default_chunks("copy", 8, 32768) == 6 and default_chunks("copy", 4, 32768) == 1
     assert default_chunks("p2p", 8, 32768) == 1
