@@ -38,6 +38,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "FP8 MoE fwd TFLOPS/GPU & tokens/s (T32k,H4096,I1024,E128,K8) at 1/2/4/8 B200"
 CFG = dict(T=32768, H=4096, I=1024, E=128, K=8)
+HEADLINE_T = CFG["T"]  # --tokens overrides CFG["T"] for smaller profiling cases
 CPU_SAMPLE_TOKENS = 2048
 
 
@@ -358,7 +359,7 @@ def run_train(args):
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    name = "config 2" if T == CFG["T"] else f"config 2 shapes at T={T}"
+    name = "config 2" if T == HEADLINE_T else f"config 2 shapes at T={T}"
     print(json.dumps({"workload": f"{name} training step (forward + FP8 backward), one GPU", "T": T, "H": H, "I": I,
                       "E": E, "K": K, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
                       "tflops": 18.0 * T * K * H * I / (ms / 1e3) / 1e12, "steps": args.steps,

@@ -144,6 +144,13 @@ __device__ __forceinline__ void bulk_reduce_add_bf16(void* gdst, const void* ssr
       "r"(smem_u32(ssrc)), "r"(bytes), "l"(policy)
       : "memory");
 }
+// Bulk (TMA) copy of `bytes` contiguous bytes from shared to global memory (16-byte aligned, size a
+// multiple of 16), tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+               "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // every bulk operation committed by this thread has finished reading its shared-memory source
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }

@@ -64,15 +64,17 @@ constexpr int kKindDown = 0, kKindUp = 1, kKindDact = 2, kKindWgrad = 3;
 template <int kKind>
 struct GemmSmem {
   static constexpr bool kUp = kKind == kKindUp;
-  static constexpr int kStages = kKind == kKindDown ? 3 : 4;
+  // down and weight-gradient epilogues stage rows in per-thread slots: one stage fewer makes room
+  static constexpr bool kSlots = kKind == kKindDown || kKind == kKindWgrad;
+  static constexpr int kStages = kSlots ? 3 : 4;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kABytes;
   static constexpr int kOffSfa = kOffB + kStages * kBBytes;
   static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
   static constexpr int kOffStage = kOffSfb + kStages * kSfbBytes;
-  // up: one 128 x 128-byte e4m3 output tile (128B-swizzled, TMA-stored); down: per-thread slots
-  static constexpr int kStageBytes =
-      kUp ? kBlockM * 128 : (kKind == kKindDown ? kEpiWarps * 32 * kSlotStride : 0);
+  // up: one 128 x 128-byte e4m3 output tile (128B-swizzled, TMA-stored); down, weight gradient:
+  // per-thread slots of one 128-byte row chunk
+  static constexpr int kStageBytes = kUp ? kBlockM * 128 : (kSlots ? kEpiWarps * 32 * kSlotStride : 0);
   static constexpr int kOffBar = kOffStage + kStageBytes;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAmax = (kOffTmemHolder + 4 + 15) / 16 * 16;
@@ -694,16 +696,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) mbar_arrive(tmem_empty);
 
       if constexpr (kWgrad) {
-        // D[e] rows 128 mt + r, columns 256 nt + 64 cc .. + 63, as bf16
+        // D[e] rows 128 mt + r, columns 256 nt + 64 cc .. + 63, as bf16: staged in this thread's slot
+        // and written by one bulk copy (a warp's direct row stores would touch 32 lines each); the
+        // slot is rewritten once the previous tile's copy has read it
         __nv_bfloat16* dst = g.out_w + (static_cast<size_t>(ti.e) * g.a_rows + ti.mb * kBlockM + r) * g.N +
                              ti.nt * kBN + 64 * cc;
+        uint8_t* slot = sStage + (ew * 32 + lane) * kSlotStride;
+        bulk_wait_read0();
 #pragma unroll
         for (int j = 0; j < 64; j += 8)
-          *reinterpret_cast<uint4*>(dst + j) =
+          *reinterpret_cast<uint4*>(slot + 2 * j) =
               make_uint4(pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
                          pack_bf16x2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])),
                          pack_bf16x2(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5])),
                          pack_bf16x2(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7])));
+        fence_proxy_async_smem();
+        bulk_store(dst, slot, kRowChunkBytes);
+        bulk_commit();
         ++tcount;
         continue;
       } else {
